@@ -1,0 +1,105 @@
+// Python bindings of the sm_100a kernels (torch extension `_C`). Every entry point launches on the current
+// torch CUDA stream so it can be captured in CUDA graphs, and validates shapes, dtypes and alignment before
+// any launch (a bad launch parameter is a host-side exception, never a device fault).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include "wgemm.h"
+#include "kernels.h"
+
+namespace {
+
+#define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
+#define CHECK_CONTIG(t) TORCH_CHECK((t).is_contiguous(), #t " must be contiguous")
+#define CHECK_ALIGN16(t) TORCH_CHECK(((uintptr_t)(t).data_ptr()) % 16 == 0, #t " must be 16-byte aligned")
+
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+// y = x @ W^T with W in runtime tile blocks. x: fp16 [rows, K] (token matrix, K-contiguous).
+void wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, int64_t row_tiles, int64_t kg,
+           c10::optional<torch::Tensor> items, c10::optional<torch::Tensor> n_items, int64_t max_items,
+           int64_t dense_T, torch::Tensor x, int64_t b_row0, torch::Tensor out, int64_t out_row0,
+           int64_t out_cols, int64_t epi, bool accumulate, double alpha, int64_t n_tile, int64_t max_block_bytes,
+           torch::Tensor err, int64_t timeout_ns) {
+  CHECK_CUDA(wbase); CHECK_CUDA(x); CHECK_CUDA(out); CHECK_CUDA(err);
+  CHECK_CONTIG(x); CHECK_CONTIG(out);
+  CHECK_ALIGN16(wbase); CHECK_ALIGN16(x);
+  TORCH_CHECK(wbase.scalar_type() == torch::kUInt8, "wbase must be uint8");
+  TORCH_CHECK(exp_off.scalar_type() == torch::kInt64 && exp_fmt.scalar_type() == torch::kInt8, "exp_off/fmt dtypes");
+  TORCH_CHECK(x.scalar_type() == torch::kHalf && x.dim() == 2, "x must be fp16 [rows, K]");
+  TORCH_CHECK(x.size(1) == kg * 128, "x has ", x.size(1), " columns, weights have K=", kg * 128);
+  TORCH_CHECK(n_tile == 16 || n_tile == 32 || n_tile == 64 || n_tile == 128, "n_tile must be 16/32/64/128");
+  TORCH_CHECK(err.scalar_type() == torch::kInt32, "err must be int32");
+  int out_dtype;
+  if (out.scalar_type() == torch::kFloat) out_dtype = fw::WGEMM_OUT_F32;
+  else if (out.scalar_type() == torch::kBFloat16) out_dtype = fw::WGEMM_OUT_BF16;
+  else if (out.scalar_type() == torch::kHalf) out_dtype = fw::WGEMM_OUT_F16;
+  else TORCH_CHECK(false, "out must be fp32/bf16/fp16");
+  TORCH_CHECK(!accumulate || out_dtype == fw::WGEMM_OUT_F32, "accumulate needs an fp32 output");
+  const c10::cuda::CUDAGuard guard(x.device());
+
+  fw::WGemmArgs a{};
+  a.wbase = wbase.data_ptr<uint8_t>();
+  a.exp_off = exp_off.data_ptr<int64_t>();
+  a.exp_fmt = exp_fmt.data_ptr<int8_t>();
+  a.row_tiles = (int)row_tiles;
+  a.kg = (int)kg;
+  a.dense_T = (int)dense_T;
+  if (dense_T < 0) {
+    TORCH_CHECK(items.has_value() && n_items.has_value(), "grouped mode needs items and n_items");
+    TORCH_CHECK(items->scalar_type() == torch::kInt32 && items->is_contiguous(), "items must be int32 [n,4]");
+    a.items = reinterpret_cast<const int4*>(items->data_ptr<int32_t>());
+    a.n_items = n_items->data_ptr<int32_t>();
+    a.max_items = (int)max_items;
+  }
+  a.n_tile = (int)n_tile;
+  a.b_row0 = (int)b_row0;
+  a.out = out.data_ptr();
+  a.out_ld = (int)out.size(-1);
+  a.out_cols = (int)out_cols;
+  a.out_row0 = (int)out_row0;
+  a.out_dtype = out_dtype;
+  a.epi = (int)epi;
+  a.accumulate = accumulate ? 1 : 0;
+  a.alpha = (float)alpha;
+  a.err = err.data_ptr<int32_t>();
+  a.timeout_ns = (unsigned long long)timeout_ns;
+
+  const int ab_stages = n_tile >= 128 ? 2 : 3;
+  const size_t fixed = fw::wgemm_smem_bytes((int)n_tile, 0, 0, ab_stages) + 8 * 24;
+  const size_t budget = 232448;
+  int w_stages = (int)((budget - fixed) / (size_t)max_block_bytes);
+  w_stages = std::min(w_stages, 12);
+  TORCH_CHECK(w_stages >= 2, "not enough shared memory for two weight stages");
+  a.w_stage_bytes = (int)max_block_bytes;
+  a.w_stages = w_stages;
+  a.ab_stages = ab_stages;
+
+  CUtensorMap bmap;
+  int rc = fw::make_tmap_2d_f16(&bmap, x.data_ptr(), x.size(0), x.size(1), x.size(1), 64, (uint32_t)n_tile, true);
+  TORCH_CHECK(rc == 0, "cuTensorMapEncodeTiled failed: ", rc);
+  const int64_t work = (dense_T >= 0 ? (dense_T + n_tile - 1) / n_tile : max_items) * row_tiles;
+  if (work <= 0) return;
+  const int grid = (int)std::min<int64_t>(sm_count(), work);
+  rc = fw::wgemm_launch(a, bmap, grid, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "wgemm launch failed: ", cudaGetErrorString((cudaError_t)rc));
+}
+
+}  // namespace
+
+void register_kernels(pybind11::module& m);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of arcagi2_flashnext_dots3_b200";
+  m.def("wgemm", &wgemm, "weight-dequant tcgen05 GEMM");
+  m.def("sm_count", &sm_count);
+  register_kernels(m);
+}

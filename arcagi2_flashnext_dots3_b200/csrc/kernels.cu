@@ -1,0 +1,7 @@
+// CUDA-core kernels of the engine (norms, routing, recurrent state updates, attention, sampling) and their
+// torch bindings. Registered into the `_C` module by register_kernels().
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include "kernels.h"
+
+void register_kernels(pybind11::module& m) {}

@@ -1,0 +1,154 @@
+"""Weight sets for the tcgen05 weight-dequant GEMM and its torch reference.
+
+A :class:`WeightSet` holds one projection for E experts (E = 1 for a dense layer) in the runtime tile-block
+layout (:mod:`..formats.runtime`): one uint8 buffer with every expert's blocks, per-expert byte offsets and
+formats (2/3/4 = GPTQ codes, 8 = FP8 128x128 block-scaled, 16 = fp16). Experts of different bit widths share a
+buffer, so a mixed 4/3-bit MoE layer is one launch (the reference needs one Marlin launch plus one Triton launch
+on a side stream for that, flashnext/kaggle/code_dataset/fnext/moe/hyb_fuse.py:122-165).
+
+``matmul`` / ``grouped`` dispatch on the device of the activations: CUDA tensors go to the kernel (the extension
+is mandatory there), CPU tensors to a plain fp32 torch reference that dequantizes the same blocks.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from ..formats import runtime as rt
+from . import native
+
+EPI_STORE, EPI_SILU_MUL = 0, 1
+
+
+@dataclass
+class WeightSet:
+    blob: torch.Tensor          # uint8 [total bytes]
+    exp_off: torch.Tensor       # int64 [E]
+    exp_fmt: torch.Tensor       # int8 [E]
+    rows: int                   # valid rows per expert (before padding to 128)
+    K: int
+    fmts: tuple                 # python copy of exp_fmt
+    silu_pairs: bool = False    # rows are [gate; up] permuted for the silu*up epilogue
+    _dense_cache: dict = None
+
+    @property
+    def row_tiles(self) -> int:
+        return (self.rows + 127) // 128
+
+    @property
+    def kg(self) -> int:
+        return self.K // 128
+
+    @property
+    def n_experts(self) -> int:
+        return len(self.fmts)
+
+    @property
+    def max_block_bytes(self) -> int:
+        return max(rt.block_bytes(f) for f in set(self.fmts))
+
+    def nbytes(self) -> int:
+        return self.blob.numel()
+
+    def to(self, device):
+        return WeightSet(self.blob.to(device), self.exp_off.to(device), self.exp_fmt.to(device), self.rows,
+                         self.K, self.fmts, self.silu_pairs)
+
+    # ------------------------------------------------------------------ reference dequant
+    def dense(self, e: int = 0) -> torch.Tensor:
+        """fp32 [rows, K] weight of expert e in runtime row order (cached)."""
+        if self._dense_cache is None:
+            self._dense_cache = {}
+        if e not in self._dense_cache:
+            f = self.fmts[e]
+            n = self.row_tiles * self.kg * rt.block_bytes(f)
+            off = int(self.exp_off[e])
+            blob = self.blob[off: off + n].view(self.row_tiles, self.kg, rt.block_bytes(f))
+            self._dense_cache[e] = rt.unpack_blocks(blob, f, self.rows, self.K)
+        return self._dense_cache[e]
+
+
+def build_weight_set(blobs: list, fmts: list, rows: int, K: int, silu_pairs=False, device=None) -> WeightSet:
+    """Concatenate per-expert runtime blocks ([tiles, KG, block_bytes] uint8) into one WeightSet."""
+    offs, total = [], 0
+    for b in blobs:
+        offs.append(total)
+        total += b.numel()
+    dev = device or blobs[0].device
+    blob = torch.empty(total, dtype=torch.uint8, device=dev)
+    for o, b in zip(offs, blobs):
+        blob[o: o + b.numel()] = b.reshape(-1).to(dev)
+    return WeightSet(blob, torch.tensor(offs, dtype=torch.int64, device=dev),
+                     torch.tensor(fmts, dtype=torch.int8, device=dev), rows, K, tuple(int(f) for f in fmts),
+                     silu_pairs)
+
+
+def dense_fp8(w: torch.Tensor, device=None) -> WeightSet:
+    """FP8 block-scaled WeightSet from a dense weight [R, K] (quantized here)."""
+    w8, sc = rt.quantize_fp8_blocks(w)
+    return build_weight_set([rt.pack_fp8(w8, sc)], [8], w.shape[0], w.shape[1], device=device)
+
+
+def dense_fp8_from_ckpt(w8: torch.Tensor, scale: torch.Tensor, device=None) -> WeightSet:
+    return build_weight_set([rt.pack_fp8(w8, scale)], [8], w8.shape[0], w8.shape[1], device=device)
+
+
+def dense_f16(w: torch.Tensor, device=None, silu_pairs=False) -> WeightSet:
+    return build_weight_set([rt.pack_f16(w)], [16], w.shape[0], w.shape[1], silu_pairs=silu_pairs, device=device)
+
+
+def pick_n_tile(max_tokens: int) -> int:
+    for n in (16, 32, 64):
+        if max_tokens <= n:
+            return n
+    return 128
+
+
+def matmul(x16: torch.Tensor, ws: WeightSet, out: torch.Tensor = None, epi: int = EPI_STORE,
+           out_dtype=torch.float32, accumulate=False, alpha=1.0, n_tile=None) -> torch.Tensor:
+    """Dense y = x @ W^T (or silu(gate)*up for a silu_pairs weight). x16: fp16 [T, K]."""
+    T = x16.shape[0]
+    cols = ws.rows // 2 if epi == EPI_SILU_MUL else ws.rows
+    if out is None:
+        out = torch.zeros(T, cols, dtype=out_dtype, device=x16.device) if accumulate else \
+            torch.empty(T, cols, dtype=out_dtype, device=x16.device)
+    if not x16.is_cuda:
+        y = _ref_apply(x16.float() @ ws.dense(0).t(), epi) * alpha
+        if accumulate:
+            out += y.to(out.dtype)
+        else:
+            out.copy_(y.to(out.dtype))
+        return out
+    n = n_tile or pick_n_tile(T)
+    native.C().wgemm(ws.blob, ws.exp_off, ws.exp_fmt, ws.row_tiles, ws.kg, None, None, 0, T, x16, 0, out, 0,
+                     cols, epi, accumulate, alpha, n, ws.max_block_bytes, native.err_word(x16.device),
+                     native.DEFAULT_TIMEOUT_NS)
+    return out
+
+
+def grouped(xs16: torch.Tensor, ws: WeightSet, items: torch.Tensor, n_items: torch.Tensor, max_items: int,
+            out: torch.Tensor, epi: int = EPI_STORE, n_tile: int = 16) -> torch.Tensor:
+    """Grouped (MoE) GEMM: for each item (expert e, token start t0, count n) computes rows t0..t0+n of out
+    from rows t0..t0+n of xs16 with expert e's weights."""
+    cols = ws.rows // 2 if epi == EPI_SILU_MUL else ws.rows
+    if not xs16.is_cuda:
+        it = items[: int(n_items.reshape(-1)[0])].tolist()
+        for e, t0, n, _ in it:
+            y = _ref_apply(xs16[t0: t0 + n].float() @ ws.dense(e).t(), epi)
+            out[t0: t0 + n] = y.to(out.dtype)
+        return out
+    native.C().wgemm(ws.blob, ws.exp_off, ws.exp_fmt, ws.row_tiles, ws.kg, items, n_items, max_items, -1, xs16, 0,
+                     out, 0, cols, epi, False, 1.0, n_tile, ws.max_block_bytes, native.err_word(xs16.device),
+                     native.DEFAULT_TIMEOUT_NS)
+    return out
+
+
+def _ref_apply(y: torch.Tensor, epi: int) -> torch.Tensor:
+    if epi == EPI_STORE:
+        return y
+    # runtime row order: tile t = [gate 64t..64t+63 | up 64t..64t+63]
+    T, R = y.shape
+    v = y.view(T, R // 128, 2, 64)
+    g, u = v[:, :, 0], v[:, :, 1]
+    return (torch.nn.functional.silu(g) * u).reshape(T, R // 2)

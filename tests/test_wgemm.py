@@ -1,0 +1,99 @@
+"""Weight-dequant tcgen05 GEMM vs a plain fp32 torch reference (GPU), and the CPU reference path."""
+import pytest
+import torch
+
+from arcagi2_flashnext_dots3_b200.formats import runtime as rt
+from arcagi2_flashnext_dots3_b200.ops import native, wgemm
+
+
+def _expert_blob(R, K, bits, g):
+    q = torch.randint(0, 1 << bits, (R, K), generator=g, dtype=torch.int32)
+    s = (torch.rand(R, K // 128, generator=g) * 0.02 + 2e-3).half()
+    z = torch.randint(0, 1 << bits, (R, K // 128), generator=g).to(torch.uint8)
+    return rt.pack_q(q, s, z, bits)
+
+
+def test_cpu_reference_dense():
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(192, 256, generator=g) * 0.05
+    ws = wgemm.dense_f16(w)
+    x = torch.randn(5, 256, generator=g).half()
+    y = wgemm.matmul(x, ws)
+    assert torch.allclose(y, x.float() @ w.half().float().t(), atol=1e-4)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", [16, 8])
+@pytest.mark.parametrize("T", [1, 7, 16, 40, 100, 300])
+def test_dense_gemm(fmt, T):
+    g = torch.Generator().manual_seed(T + fmt)
+    R, K = 384, 512
+    w = torch.randn(R, K, generator=g) * 0.05
+    ws = (wgemm.dense_f16(w) if fmt == 16 else wgemm.dense_fp8(w)).to("cuda")
+    x = torch.randn(T, K, generator=g).half()
+    ref = x.float() @ ws.dense(0).cpu().t()
+    y = wgemm.matmul(x.cuda(), ws)
+    torch.cuda.synchronize()
+    native.check_error()
+    assert torch.allclose(y.cpu(), ref, atol=2e-3, rtol=2e-3), (y.cpu() - ref).abs().max()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits", [4, 3, 2])
+def test_grouped_lowbit(bits):
+    g = torch.Generator().manual_seed(bits)
+    E, R, K = 6, 256, 384
+    blobs = [_expert_blob(R, K, bits, g) for _ in range(E)]
+    ws = wgemm.build_weight_set(blobs, [bits] * E, R, K).to("cuda")
+    counts = [3, 0, 17, 1, 40, 5]
+    items, t0 = [], 0
+    for e, c in enumerate(counts):
+        for s in range(0, c, 16):
+            items.append([e, t0 + s, min(16, c - s), 0])
+        t0 += c
+    P = t0
+    x = torch.randn(P, K, generator=g).half()
+    out = torch.zeros(P, R, device="cuda")
+    it = torch.tensor(items, dtype=torch.int32, device="cuda")
+    n = torch.tensor([len(items)], dtype=torch.int32, device="cuda")
+    wgemm.grouped(x.cuda(), ws, it, n, len(items), out, n_tile=16)
+    torch.cuda.synchronize()
+    native.check_error()
+    t0 = 0
+    for e, c in enumerate(counts):
+        ref = x[t0:t0 + c].float() @ ws.dense(e).cpu().t()
+        assert torch.allclose(out[t0:t0 + c].cpu(), ref, atol=2e-2, rtol=1e-2), (e, (out[t0:t0 + c].cpu() - ref).abs().max())
+        t0 += c
+
+
+@pytest.mark.gpu
+def test_grouped_mixed_bits_silu():
+    g = torch.Generator().manual_seed(7)
+    E, I, K = 4, 128, 256
+    perm = rt.gate_up_perm(I)
+    bits = [4, 3, 4, 3]
+    blobs = []
+    for b in bits:
+        q = torch.randint(0, 1 << b, (2 * I, K), generator=g, dtype=torch.int32)[perm]
+        s = (torch.rand(2 * I, K // 128, generator=g) * 0.02 + 2e-3).half()
+        z = torch.randint(0, 1 << b, (2 * I, K // 128), generator=g).to(torch.uint8)
+        blobs.append(rt.pack_q(q, s, z, b))
+    ws = wgemm.build_weight_set(blobs, bits, 2 * I, K, silu_pairs=True).to("cuda")
+    counts = [2, 5, 0, 9]
+    items, t0 = [], 0
+    for e, c in enumerate(counts):
+        if c:
+            items.append([e, t0, c, 0])
+        t0 += c
+    x = torch.randn(t0, K, generator=g).half()
+    out = torch.zeros(t0, I, dtype=torch.float16, device="cuda")
+    it = torch.tensor(items, dtype=torch.int32, device="cuda")
+    n = torch.tensor([len(items)], dtype=torch.int32, device="cuda")
+    wgemm.grouped(x.cuda(), ws, it, n, len(items), out, epi=wgemm.EPI_SILU_MUL, n_tile=16)
+    torch.cuda.synchronize()
+    native.check_error()
+    t0 = 0
+    for e, c in enumerate(counts):
+        ref = wgemm._ref_apply(x[t0:t0 + c].float() @ ws.dense(e).cpu().t(), wgemm.EPI_SILU_MUL)
+        assert torch.allclose(out[t0:t0 + c].float().cpu(), ref, atol=2e-2, rtol=2e-2)
+        t0 += c
