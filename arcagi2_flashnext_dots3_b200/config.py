@@ -72,6 +72,7 @@ class FNConfig:
     lin_k_dim: int = 128
     lin_v_dim: int = 128
     conv_kernel: int = 4
+    gdn_gate: str = "silu"               # output gate of the gated RMSNorm (silu, or sigmoid)
     # attention
     n_heads: int = 16
     n_kv_heads: int = 2
@@ -90,7 +91,8 @@ class FNConfig:
     shared_inter: int = 640
     expert_bits: tuple = (4, 3)          # bit widths, split evenly over the kept experts
     # PLE n-gram embedding
-    ple_layers: tuple = (0, 12, 24, 36)
+    ple_layers: tuple = (0,)             # layers with a PLE block (all share one n-gram table)
+    ple_conv: int = 4
     ngram_size: int = 3
     heads_per_ngram: int = 8
     ple_dim: int = 160

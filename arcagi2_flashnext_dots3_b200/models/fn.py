@@ -1,0 +1,187 @@
+"""Flash-Next-shaped model on the engine path: incremental prefill + decode over per-sequence caches.
+
+The layer wiring is the reference's (flashnext/training/student/student_fn.py:578 `Layer.forward`): PLE add,
+attention hyper-connection, mixer (Gated DeltaNet or block-sparse attention), residual injection into every
+stream, MLP hyper-connection, MoE, residual injection; final hyper-connection mixer and LM head.
+
+Differences from the reference's serving stack (vLLM + the `fnext` overlay) are in HOW each step runs:
+every GEMM is the tcgen05 weight-dequant kernel (fused projections: GDN qkv|z|b|a in one launch, attention
+q|gate|k|v|indexer in one launch, router + shared-expert gate in one launch), the MoE is one grouped launch per
+projection for all experts and bit widths with silu*up fused into the gate_up epilogue, and combine + shared
+expert + hyper-connection injection is one kernel.
+
+Caches (per slot = sequence): paged attention KV (fp8 on GPU), per-slot compressed indexer keys and a ring of
+the last `ratio` raw indexer keys, GDN conv and recurrent states, PLE conv history and n-gram token history.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from ..ops import fn_ops as ops
+from ..ops import wgemm
+from .fn_weights import rank_pad
+
+
+@dataclass
+class FNCaches:
+    k: list            # per attention layer [n_blocks, block_size, KV, D]
+    v: list
+    kr_ring: list      # per attention layer [S, ratio, iD]
+    comp: list         # per attention layer [S, max_comp_blocks, iD]
+    conv: list         # per linear layer [S, C, kc-1]
+    ssm: list          # per linear layer [S, nv, dk, dv]
+    block_table: torch.Tensor  # [S, max_blocks] int32
+    block_size: int
+    n_blocks: int
+    ple_hist: torch.Tensor = None   # [S, (ple_conv-1)*ngram, hc*H] gvn history (PLE layers share one slot)
+    tok_hist: torch.Tensor = None   # [S, ngram-1] previous tokens (-1 = none) + [S] tokens since eos
+
+
+def kv_dtype_for(device, kv_dtype: str):
+    if torch.device(device).type == "cpu":
+        return torch.float32
+    return torch.float8_e4m3fn if kv_dtype == "fp8" else torch.bfloat16
+
+
+def allocate_caches(cfg, device, n_slots: int, max_len: int, block_size: int = 64, n_blocks: int = None,
+                    kv_dtype: str = "fp8", state_dtype: str = "bf16") -> FNCaches:
+    dev = torch.device(device)
+    kvd = kv_dtype_for(dev, kv_dtype)
+    sd = torch.float32 if dev.type == "cpu" or state_dtype == "fp32" else torch.bfloat16
+    max_blocks = (max_len + block_size - 1) // block_size
+    n_blocks = n_blocks or n_slots * max_blocks
+    nk, nv, dk, dv = cfg.lin_k_heads, cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim
+    C = 2 * nk * dk + nv * dv
+    n_attn = sum(cfg.layer_kind(l) == "attention" for l in range(cfg.num_layers))
+    n_lin = cfg.num_layers - n_attn
+    idx_dt = torch.float32 if dev.type == "cpu" else torch.bfloat16
+    c = FNCaches(
+        k=[torch.zeros(n_blocks, block_size, cfg.n_kv_heads, cfg.head_dim, dtype=kvd, device=dev) for _ in range(n_attn)],
+        v=[torch.zeros(n_blocks, block_size, cfg.n_kv_heads, cfg.head_dim, dtype=kvd, device=dev) for _ in range(n_attn)],
+        kr_ring=[torch.zeros(n_slots, cfg.indexer_ratio, cfg.indexer_dim, dtype=torch.float32, device=dev)
+                 for _ in range(n_attn)],
+        comp=[torch.zeros(n_slots, max_len // cfg.indexer_ratio + 1, cfg.indexer_dim, dtype=idx_dt, device=dev)
+              for _ in range(n_attn)],
+        conv=[torch.zeros(n_slots, C, cfg.conv_kernel - 1, dtype=torch.float32, device=dev) for _ in range(n_lin)],
+        ssm=[torch.zeros(n_slots, nv, dk, dv, dtype=sd, device=dev) for _ in range(n_lin)],
+        block_table=torch.zeros(n_slots, max_blocks, dtype=torch.int32, device=dev),
+        block_size=block_size, n_blocks=n_blocks)
+    if cfg.ple_layers:
+        c.ple_hist = torch.zeros(n_slots, (cfg.ple_conv - 1) * cfg.ngram_size, cfg.hc_count * cfg.hidden_size,
+                                 dtype=torch.float32, device=dev)
+        c.tok_hist = torch.full((n_slots, cfg.ngram_size), -1, dtype=torch.int64, device=dev)
+    return c
+
+
+class FNModel:
+    """Engine model. ``step(ids, slots, positions, n_tok)`` runs rows = len(slots) * n_tok tokens (token j of
+    sequence b at positions[b] + j) through all layers, updating the caches of `slots`, and returns the final
+    hidden state [rows, H] (act dtype); ``logits`` applies the LM head."""
+
+    def __init__(self, cfg, weights: dict, caches: FNCaches, device):
+        self.cfg = cfg
+        self.W = weights
+        self.c = caches
+        self.device = torch.device(device)
+        self.act = ops.act_dtype(self.device)
+        self.rope = ops.rope_tables(caches.block_table.shape[1] * caches.block_size + 8, cfg.rope_dim,
+                                    cfg.rope_theta, self.device)
+        self.rank_pad = rank_pad(cfg)
+        self.attn_idx = {}
+        self.lin_idx = {}
+        for l in range(cfg.num_layers):
+            d = self.attn_idx if cfg.layer_kind(l) == "attention" else self.lin_idx
+            d[l] = len(d)
+
+    # ------------------------------------------------------------------------------------------ pieces
+    def _mm(self, x, ws, epi=wgemm.EPI_STORE, out_dtype=torch.float32):
+        if not x.is_cuda:
+            return wgemm.matmul(x.float(), ws, epi=epi, out_dtype=torch.float32)
+        return wgemm.matmul(x, ws, epi=epi, out_dtype=out_dtype)
+
+    def _hc(self, h, p, with_inj=True):
+        cfg = self.cfg
+        hn = ops.hc_prenorm(h, p["norm"], cfg.hc_count, cfg.hidden_size, cfg.rms_eps)
+        z = self._mm(hn, p["w1"])
+        a, inj = ops.hc_act(z, self.rank_pad, cfg.hc_count, with_inj)
+        u = self._mm(a, p["w2"])
+        x = ops.hc_mix(u, hn, cfg.hc_count, cfg.hidden_size)
+        return x, inj
+
+    def _gdn(self, x, p, li, slots, n_tok):
+        proj = self._mm(x, p["proj"])
+        o = ops.gdn_step(proj, p["conv"], self.c.conv[li], self.c.ssm[li], p["A_log"], p["dt_bias"], p["norm"],
+                         slots, self.cfg, n_tok)
+        return self._mm(o, p["out"])
+
+    def _attn(self, x, p, ai, slots, positions, n_tok):
+        cfg, c = self.cfg, self.c
+        proj = self._mm(x, p["proj"])
+        q, gate, iq = ops.qsa_prep(proj, p["qn"], p["kn"], p["iqn"], p["ikn"], self.rope, c.k[ai], c.v[ai],
+                                   c.block_table, slots, positions, c.kr_ring[ai], c.comp[ai], cfg, n_tok)
+        sel, sparse = ops.qsa_select(iq, c.comp[ai], slots, positions, cfg, n_tok)
+        o = ops.attn_decode(q, gate, c.k[ai], c.v[ai], c.block_table, slots, positions, sel, sparse, cfg, n_tok)
+        return self._mm(o, p["o"])
+
+    def _moe(self, x, p, h, inj):
+        cfg = self.cfg
+        T = x.shape[0]
+        E = cfg.n_experts
+        logits = self._mm(x, p["router"])
+        ids, w = ops.moe_route(logits, E, cfg.top_k)
+        P = T * cfg.top_k
+        n_tile = wgemm.pick_n_tile(max(1, (2 * P) // E)) if x.is_cuda else 16
+        max_items = (P + n_tile - 1) // n_tile + E
+        pair_pos, items, n_items = ops.moe_plan(ids, E, n_tile, max_items)
+        xs = ops.moe_scatter(x, pair_pos)
+        act = torch.empty(P, cfg.moe_inter, dtype=self.act, device=x.device)
+        wgemm.grouped(xs, p["gu"], items, n_items, max_items, act, epi=wgemm.EPI_SILU_MUL, n_tile=n_tile)
+        ypair = torch.empty(P, cfg.hidden_size, dtype=torch.float32, device=x.device)
+        wgemm.grouped(act, p["d"], items, n_items, max_items, ypair, n_tile=n_tile)
+        sact = self._mm(x, p["sgu"], epi=wgemm.EPI_SILU_MUL, out_dtype=self.act)
+        ysh = self._mm(sact, p["sd"])
+        ops.moe_combine(h, ypair, pair_pos, w, ysh, logits[:, E], inj)
+
+    # ------------------------------------------------------------------------------------------- step
+    def step(self, ids: torch.Tensor, slots: torch.Tensor, positions: torch.Tensor, n_tok: int = 1):
+        cfg, W = self.cfg, self.W
+        h = ops.embed_hc(ids, W["embed"], cfg.hc_count)
+        if cfg.ple_layers:
+            from . import fn_ple
+            emb = fn_ple.embed_rows(self, ids, slots, positions, n_tok)
+        for l, L in enumerate(W["layers"]):
+            if "ple" in L:
+                fn_ple.apply(self, h, emb, L["ple"], slots, n_tok)
+            x, inj = self._hc(h, L["ahc"])
+            if cfg.layer_kind(l) == "linear":
+                y = self._gdn(x, L["mix"], self.lin_idx[l], slots, n_tok)
+            else:
+                y = self._attn(x, L["mix"], self.attn_idx[l], slots, positions, n_tok)
+            ops.hc_residual(h, y, inj)
+            x, inj = self._hc(h, L["mhc"])
+            self._moe(x, L["moe"], h, inj)
+        x, _ = self._hc(h, W["mixer"], with_inj=False)
+        return x
+
+    def logits(self, x: torch.Tensor) -> torch.Tensor:
+        return self._mm(x, self.W["lm_head"])
+
+    # --------------------------------------------------------------------------------------- helpers
+    def assign_blocks(self, slot: int, n_tokens: int, allocator):
+        """Make sure slot's block table covers n_tokens positions, taking blocks from `allocator`."""
+        bs = self.c.block_size
+        need = (n_tokens + bs - 1) // bs
+        have = allocator.n_blocks_of(slot)
+        if need > have:
+            new = allocator.allocate(slot, need - have)
+            self.c.block_table[slot, have:need] = torch.tensor(new, dtype=torch.int32, device=self.device)
+
+    def reset_slot(self, slot: int):
+        c = self.c
+        for t in c.conv + c.ssm + c.kr_ring:
+            t[slot].zero_()
+        if c.ple_hist is not None:
+            c.ple_hist[slot].zero_()
+            c.tok_hist[slot].fill_(-1)
