@@ -1,0 +1,1029 @@
+// CUDA-core kernels of the Flash-Next-shaped engine step (everything that is not a weight-streaming GEMM):
+// hyper-connection norms/activations/mixing, Gated DeltaNet conv + recurrent update, attention prep with paged
+// KV writes, the block indexer (scores + radix top-k), split-K sparse GQA decode attention, MoE routing
+// (softmax top-k), expert plan (stable expert sort + tile items), token scatter, weighted combine fused with the
+// shared expert and the hyper-connection injection, and greedy argmax.
+//
+// Math references (student_fn.py = flashnext/training/student/student_fn.py): rms1p :58, GatedResidual :232,
+// GDN :251, QSA :295-378, MoE :461-563. Each kernel has a torch twin in ops/fn_ops.py used as its test oracle.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cfloat>
+#include "kernels.h"
+
+namespace {
+
+#define CK(x) TORCH_CHECK(x)
+#define STREAM at::cuda::getCurrentCUDAStream()
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum (blockDim.x multiple of 32, <= 1024). `sh` needs 32 floats.
+__device__ float block_sum(float v, float* sh) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) sh[w] = v;
+  __syncthreads();
+  float t = lane < nw ? sh[lane] : 0.f;
+  t = warp_sum(t);
+  return t;
+}
+
+__device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
+__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
+__device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
+
+template <typename T>
+__device__ __forceinline__ float ldf(const T* p) { return (float)*p; }
+template <>
+__device__ __forceinline__ float ldf<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+template <>
+__device__ __forceinline__ float ldf<__half>(const __half* p) { return __half2float(*p); }
+template <>
+__device__ __forceinline__ float ldf<__nv_fp8_e4m3>(const __nv_fp8_e4m3* p) { return (float)(*p); }
+
+template <typename T>
+__device__ __forceinline__ void stf(T* p, float v) { *p = (T)v; }
+template <>
+__device__ __forceinline__ void stf<__nv_bfloat16>(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ void stf<__half>(__half* p, float v) { *p = __float2half_rn(v); }
+template <>
+__device__ __forceinline__ void stf<__nv_fp8_e4m3>(__nv_fp8_e4m3* p, float v) { *p = __nv_fp8_e4m3(v); }
+
+// ============================================================================================ embedding
+template <typename IT>
+__global__ void embed_hc_kernel(const IT* ids, const __nv_bfloat16* table, float* out, int H, int hc) {
+  const int t = blockIdx.x;
+  const int64_t id = (int64_t)ids[t];
+  const __nv_bfloat16* row = table + id * H;
+  float* o = out + (int64_t)t * hc * H;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float v = __bfloat162float(row[i]);
+    for (int s = 0; s < hc; ++s) o[s * H + i] = v;
+  }
+}
+
+void embed_hc(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t hc) {
+  CK(table.scalar_type() == torch::kBFloat16 && table.is_contiguous());
+  CK(out.scalar_type() == torch::kFloat && out.is_contiguous());
+  const int T = ids.size(0), H = table.size(1);
+  if (!T) return;
+  if (ids.scalar_type() == torch::kInt64)
+    embed_hc_kernel<<<T, 256, 0, STREAM>>>(ids.data_ptr<int64_t>(), (const __nv_bfloat16*)table.data_ptr(),
+                                           out.data_ptr<float>(), H, hc);
+  else
+    embed_hc_kernel<<<T, 256, 0, STREAM>>>(ids.data_ptr<int32_t>(), (const __nv_bfloat16*)table.data_ptr(),
+                                           out.data_ptr<float>(), H, hc);
+}
+
+// ===================================================================================== hyper-connections
+// hn[t, s*H+i] = h * rsqrt(mean_s(h^2) + eps) * (1 + w[s*H+i]), one block per (token, stream).
+__global__ void hc_prenorm_kernel(const float* h, const float* w, __half* out, int H, float eps) {
+  __shared__ float sh[32];
+  const int t = blockIdx.x, s = blockIdx.y, S = gridDim.y;
+  const float* x = h + ((int64_t)t * S + s) * H;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) ss += x[i] * x[i];
+  ss = block_sum(ss, sh);
+  const float r = rsqrtf(ss / H + eps);
+  __half* o = out + ((int64_t)t * S + s) * H;
+  const float* ww = w + (int64_t)s * H;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) o[i] = __float2half_rn(x[i] * r * (1.f + ww[i]));
+}
+
+void hc_prenorm(torch::Tensor h, torch::Tensor w, torch::Tensor out, int64_t H, double eps) {
+  const int T = h.size(0);
+  const int hc = h.size(1) / H;
+  if (!T) return;
+  hc_prenorm_kernel<<<dim3(T, hc), 256, 0, STREAM>>>(h.data_ptr<float>(), w.data_ptr<float>(),
+                                                     (__half*)out.data_ptr(), H, (float)eps);
+}
+
+__global__ void hc_act_kernel(const float* z, int ldz, __half* a, float* inj, int rank_pad, int hc, int with_inj) {
+  const int t = blockIdx.x;
+  const float inv = 1.f / hc;
+  for (int i = threadIdx.x; i < rank_pad; i += blockDim.x)
+    a[(int64_t)t * rank_pad + i] = __float2half_rn(silu(z[(int64_t)t * ldz + i] * inv));
+  if (with_inj && threadIdx.x < hc)
+    inj[t * hc + threadIdx.x] = 2.f * sigm(z[(int64_t)t * ldz + rank_pad + threadIdx.x] * inv);
+}
+
+void hc_act(torch::Tensor z, torch::Tensor a, torch::Tensor inj, int64_t rank_pad, int64_t hc, bool with_inj) {
+  const int T = z.size(0);
+  if (!T) return;
+  hc_act_kernel<<<T, 128, 0, STREAM>>>(z.data_ptr<float>(), z.size(1), (__half*)a.data_ptr(), inj.data_ptr<float>(),
+                                       rank_pad, hc, with_inj);
+}
+
+__global__ void hc_mix_kernel(const float* u, const __half* hn, __half* out, int hc, int H) {
+  const int t = blockIdx.x;
+  const float inv = 1.f / hc;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < hc; ++s) {
+      const int64_t o = ((int64_t)t * hc + s) * H + i;
+      acc += sigm(u[o]) * __half2float(hn[o]);
+    }
+    out[(int64_t)t * H + i] = __float2half_rn(acc * inv);
+  }
+}
+
+void hc_mix(torch::Tensor u, torch::Tensor hn, torch::Tensor out, int64_t hc, int64_t H) {
+  const int T = u.size(0);
+  if (!T) return;
+  hc_mix_kernel<<<T, 256, 0, STREAM>>>(u.data_ptr<float>(), (const __half*)hn.data_ptr(), (__half*)out.data_ptr(),
+                                       hc, H);
+}
+
+__global__ void hc_residual_kernel(float* h, const float* y, const float* inj, int hc, int H) {
+  const int t = blockIdx.x;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float v = y[(int64_t)t * H + i];
+    for (int s = 0; s < hc; ++s) h[((int64_t)t * hc + s) * H + i] += v * inj[t * hc + s];
+  }
+}
+
+void hc_residual(torch::Tensor h, torch::Tensor y, torch::Tensor inj) {
+  const int T = h.size(0), hc = inj.size(1), H = y.size(1);
+  if (!T) return;
+  hc_residual_kernel<<<T, 256, 0, STREAM>>>(h.data_ptr<float>(), y.data_ptr<float>(), inj.data_ptr<float>(), hc, H);
+}
+
+// ======================================================================================= Gated DeltaNet
+// Causal depthwise conv over [conv_state | new tokens] + SiLU for every channel; updates conv_state in place.
+// Rows of proj: seq b token j at b*n_tok + j. One thread per (seq, channel).
+__global__ void gdn_conv_kernel(const float* proj, int ldp, const float* conv_w, float* conv_state, const int* slots,
+                                float* out, int C, int kc, int n_tok, int B) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)B * C) return;
+  const int b = idx / C, c = idx % C;
+  const int s = slots[b];
+  float* st = conv_state + ((int64_t)s * C + c) * (kc - 1);
+  float hist[8];  // kc - 1 <= 7
+  for (int j = 0; j < kc - 1; ++j) hist[j] = st[j];
+  float w[8];
+  for (int j = 0; j < kc; ++j) w[j] = conv_w[c * kc + j];
+  for (int t = 0; t < n_tok; ++t) {
+    const float x = proj[((int64_t)b * n_tok + t) * ldp + c];
+    float acc = w[kc - 1] * x;
+    for (int j = 0; j < kc - 1; ++j) acc += w[j] * hist[j];
+    for (int j = 0; j < kc - 2; ++j) hist[j] = hist[j + 1];
+    hist[kc - 2] = x;
+    out[((int64_t)b * n_tok + t) * C + c] = silu(acc);
+  }
+  for (int j = 0; j < kc - 1; ++j) st[j] = hist[j];
+}
+
+// Gated delta rule for one (sequence, value head) over n_tok tokens; DK = DV = 128, 256 threads:
+// thread (j = tid & 127, half = tid >> 7) keeps S[64*half .. 64*half+63][j] in registers.
+template <typename ST>
+__global__ void __launch_bounds__(256) gdn_recur_kernel(const float* qkv, const float* proj, int ldp, ST* ssm,
+                                                        const int* slots, const float* A_log, const float* dt_bias,
+                                                        const float* norm_w, __half* out, int nk, int nv, int n_tok,
+                                                        float eps, int gate_sigmoid) {
+  constexpr int DK = 128, DV = 128;
+  __shared__ float q_s[DK], k_s[DK], part[2][DV], red[32];
+  const int b = blockIdx.x, hv = blockIdx.y;
+  const int tid = threadIdx.x, j = tid & 127, half = tid >> 7;
+  const int r = nv / nk, hk = hv / r;
+  const int s = slots[b];
+  const int C = 2 * nk * DK + nv * DV;
+  ST* S = ssm + ((int64_t)s * nv + hv) * DK * DV;
+  float Sr[64];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) Sr[i] = ldf(&S[(int64_t)(64 * half + i) * DV + j]);
+  const float A = -__expf(A_log[hv]);
+  const float dtb = dt_bias[hv];
+  const float scale = rsqrtf((float)DK);
+  for (int t = 0; t < n_tok; ++t) {
+    const int64_t row = (int64_t)b * n_tok + t;
+    const float* x = qkv + row * C;
+    const float* pr = proj + row * ldp;
+    // q, k of head hk: l2 normalize (eps 1e-6 inside the sqrt)
+    float qv = 0.f, kv = 0.f;
+    if (tid < DK) {
+      qv = x[hk * DK + tid];
+      kv = x[nk * DK + hk * DK + tid];
+    }
+    const float qn = block_sum(tid < DK ? qv * qv : 0.f, red);
+    const float kn = block_sum(tid < DK ? kv * kv : 0.f, red);
+    if (tid < DK) {
+      q_s[tid] = qv * rsqrtf(qn + 1e-6f) * scale;
+      k_s[tid] = kv * rsqrtf(kn + 1e-6f);
+    }
+    const float beta = sigm(pr[C + nv * DV + hv]);
+    const float g = A * softplus(pr[C + nv * DV + nv + hv] + dtb);
+    const float dec = __expf(g);
+    __syncthreads();
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      Sr[i] *= dec;
+      acc += Sr[i] * k_s[64 * half + i];
+    }
+    part[half][j] = acc;
+    __syncthreads();
+    const float vj = x[2 * nk * DK + hv * DV + j];
+    const float u = beta * (vj - (part[0][j] + part[1][j]));
+    float o = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      Sr[i] += k_s[64 * half + i] * u;
+      o += Sr[i] * q_s[64 * half + i];
+    }
+    __syncthreads();
+    part[half][j] = o;
+    __syncthreads();
+    const float oj = part[0][j] + part[1][j];
+    const float ss = block_sum(half == 0 ? oj * oj : 0.f, red);
+    if (half == 0) {
+      const float on = oj * rsqrtf(ss / DV + eps) * norm_w[j];
+      const float z = pr[C + hv * DV + j];
+      const float gz = gate_sigmoid ? sigm(z) : silu(z);
+      out[row * (nv * DV) + hv * DV + j] = __float2half_rn(on * gz);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 64; ++i) stf(&S[(int64_t)(64 * half + i) * DV + j], Sr[i]);
+}
+
+void gdn_step(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor conv_state, torch::Tensor ssm,
+              torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor norm_w, torch::Tensor slots, torch::Tensor out,
+              int64_t nk, int64_t nv, int64_t dk, int64_t dv, int64_t n_tok, double eps, int64_t gate_sigmoid) {
+  CK(dk == 128 && dv == 128);
+  CK(proj.scalar_type() == torch::kFloat && proj.is_contiguous());
+  CK(slots.scalar_type() == torch::kInt32);
+  const int rows = proj.size(0);
+  if (!rows) return;
+  const int B = rows / n_tok;
+  const int C = 2 * nk * dk + nv * dv;
+  const int kc = conv_w.size(1);
+  CK(kc >= 2 && kc <= 8);
+  auto qkv = torch::empty({rows, C}, proj.options());
+  const int64_t nthr = (int64_t)B * C;
+  gdn_conv_kernel<<<(nthr + 255) / 256, 256, 0, STREAM>>>(proj.data_ptr<float>(), proj.size(1),
+                                                          conv_w.data_ptr<float>(), conv_state.data_ptr<float>(),
+                                                          slots.data_ptr<int32_t>(), qkv.data_ptr<float>(), C, kc,
+                                                          n_tok, B);
+  dim3 grid(B, nv);
+  if (ssm.scalar_type() == torch::kBFloat16)
+    gdn_recur_kernel<__nv_bfloat16><<<grid, 256, 0, STREAM>>>(
+        qkv.data_ptr<float>(), proj.data_ptr<float>(), proj.size(1), (__nv_bfloat16*)ssm.data_ptr(),
+        slots.data_ptr<int32_t>(), A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), norm_w.data_ptr<float>(),
+        (__half*)out.data_ptr(), nk, nv, n_tok, (float)eps, gate_sigmoid);
+  else
+    gdn_recur_kernel<float><<<grid, 256, 0, STREAM>>>(
+        qkv.data_ptr<float>(), proj.data_ptr<float>(), proj.size(1), ssm.data_ptr<float>(), slots.data_ptr<int32_t>(),
+        A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), norm_w.data_ptr<float>(), (__half*)out.data_ptr(), nk,
+        nv, n_tok, (float)eps, gate_sigmoid);
+}
+
+// ============================================================================================ attention
+// RMSNorm(1+w) + partial RoPE (neox half split on the first rd dims) of one head vector held by `nthr` threads,
+// dims d = tid, tid + nthr, ... ; x in smem.
+__device__ void norm_rope_head(float* x, int D, const float* w, float eps, const float* cs_cos, const float* cs_sin,
+                               int rd, float* red) {
+  float ss = 0.f;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) ss += x[d] * x[d];
+  ss = block_sum(ss, red);
+  const float r = rsqrtf(ss / D + eps);
+  __syncthreads();
+  float tmp[4];
+  int n = 0;
+  for (int d = threadIdx.x; d < D; d += blockDim.x, ++n) {
+    const float v = x[d] * r * (1.f + w[d]);
+    float o = v;
+    if (d < rd) {
+      const int h2 = rd / 2;
+      const float other = d < h2 ? -(x[d + h2] * r * (1.f + w[d + h2])) : x[d - h2] * r * (1.f + w[d - h2]);
+      o = v * cs_cos[d] + other * cs_sin[d];
+    }
+    tmp[n] = o;
+  }
+  __syncthreads();
+  n = 0;
+  for (int d = threadIdx.x; d < D; d += blockDim.x, ++n) x[d] = tmp[n];
+  __syncthreads();
+}
+
+// One block per row: q heads (norm+rope) -> q, gate copy, k heads (norm+rope) -> k cache, v -> v cache,
+// indexer q heads (norm+rope) -> iq. 256 threads, D <= 1024.
+template <typename KT>
+__global__ void qsa_prep_kernel(const float* proj, int ldp, const float* qn, const float* kn, const float* iqn,
+                                const float* rope, int rope_len, KT* kc, KT* vc, const int* block_table, int max_blocks,
+                                int bs, const int* slots, const int* positions, float* q_out, float* gate_out,
+                                float* iq_out, int Hq, int KV, int D, int iH, int iD, int n_tok, float eps,
+                                int rdq) {
+  extern __shared__ float xs[];
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const int b = row / n_tok;
+  const int p = positions[b] + row % n_tok;
+  const int s = slots[b];
+  const float* P = proj + (int64_t)row * ldp;
+  const float* cs_c = rope + (int64_t)p * rdq;
+  const float* cs_s = rope + (int64_t)rope_len * rdq + (int64_t)p * rdq;
+  // q + gate
+  for (int h = 0; h < Hq; ++h) {
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      xs[d] = P[h * 2 * D + d];
+      gate_out[(int64_t)row * Hq * D + h * D + d] = P[h * 2 * D + D + d];
+    }
+    __syncthreads();
+    norm_rope_head(xs, D, qn, eps, cs_c, cs_s, rdq, red);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) q_out[((int64_t)row * Hq + h) * D + d] = xs[d];
+    __syncthreads();
+  }
+  const int blk = block_table[(int64_t)s * max_blocks + p / bs];
+  const int64_t coff = ((int64_t)blk * bs + (p % bs)) * KV * D;
+  for (int h = 0; h < KV; ++h) {
+    for (int d = threadIdx.x; d < D; d += blockDim.x) xs[d] = P[Hq * 2 * D + h * D + d];
+    __syncthreads();
+    norm_rope_head(xs, D, kn, eps, cs_c, cs_s, rdq, red);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      stf(&kc[coff + h * D + d], xs[d]);
+      stf(&vc[coff + h * D + d], P[Hq * 2 * D + KV * D + h * D + d]);
+    }
+    __syncthreads();
+  }
+  const int ib = Hq * 2 * D + 2 * KV * D;
+  for (int h = 0; h < iH; ++h) {
+    for (int d = threadIdx.x; d < iD; d += blockDim.x) xs[d] = P[ib + h * iD + d];
+    __syncthreads();
+    norm_rope_head(xs, iD, iqn, eps, cs_c, cs_s, rdq, red);
+    for (int d = threadIdx.x; d < iD; d += blockDim.x) iq_out[((int64_t)row * iH + h) * iD + d] = xs[d];
+    __syncthreads();
+  }
+}
+
+// One block per sequence: compressed indexer keys of every block that completes within this step, from the ring
+// of the previous raw keys plus this step's rows; then the ring is refreshed. Sequential per sequence (no race).
+template <typename CT>
+__global__ void qsa_compress_kernel(const float* proj, int ldp, int kr_off, float* ring, CT* comp, int max_comp,
+                                    const float* ikn, const float* rope, int rope_len, int rdq, const int* slots,
+                                    const int* positions, int r, int iD, int n_tok, float eps) {
+  extern __shared__ float sm[];
+  float* old = sm;             // [r][iD]
+  float* xs = sm + r * iD;     // [iD]
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const int s = slots[b];
+  const int p0 = positions[b];
+  float* rg = ring + (int64_t)s * r * iD;
+  for (int i = threadIdx.x; i < r * iD; i += blockDim.x) old[i] = rg[i];
+  __syncthreads();
+  for (int t = 0; t < n_tok; ++t) {
+    const int p = p0 + t;
+    if ((p + 1) % r) continue;
+    const int cb = (p + 1) / r - 1;
+    const int st = cb * r;
+    for (int d = threadIdx.x; d < iD; d += blockDim.x) {
+      float acc = 0.f;
+      for (int q = st; q <= p; ++q) {
+        const float v = q >= p0 ? proj[((int64_t)b * n_tok + (q - p0)) * ldp + kr_off + d] : old[(q % r) * iD + d];
+        acc += v;
+      }
+      xs[d] = acc / r;
+    }
+    __syncthreads();
+    norm_rope_head(xs, iD, ikn, eps, rope + (int64_t)st * rdq, rope + (int64_t)rope_len * rdq + (int64_t)st * rdq,
+                   rdq, red);
+    if (cb < max_comp)
+      for (int d = threadIdx.x; d < iD; d += blockDim.x) stf(&comp[((int64_t)s * max_comp + cb) * iD + d], xs[d]);
+    __syncthreads();
+  }
+  // refresh the ring with the last min(r, n_tok) raw keys of this step
+  const int first = max(0, n_tok - r);
+  for (int t = first; t < n_tok; ++t) {
+    const int p = p0 + t;
+    for (int d = threadIdx.x; d < iD; d += blockDim.x)
+      rg[(p % r) * iD + d] = proj[((int64_t)b * n_tok + t) * ldp + kr_off + d];
+  }
+}
+
+void qsa_prep(torch::Tensor proj, torch::Tensor qn, torch::Tensor kn, torch::Tensor iqn, torch::Tensor ikn,
+              torch::Tensor rope, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
+              torch::Tensor slots, torch::Tensor positions, torch::Tensor kr_ring, torch::Tensor comp_cache,
+              torch::Tensor q, torch::Tensor gate, torch::Tensor iq, int64_t Hq, int64_t KV, int64_t D, int64_t iH,
+              int64_t iD, int64_t ratio, int64_t n_tok, double eps) {
+  const int rows = proj.size(0);
+  if (!rows) return;
+  CK(proj.is_contiguous() && proj.scalar_type() == torch::kFloat);
+  CK(slots.scalar_type() == torch::kInt32 && positions.scalar_type() == torch::kInt32);
+  const int rd = rope.size(2), rope_len = rope.size(1);
+  CK(D <= 1024 && iD <= 1024 && rd <= D && rd <= iD);
+  const int bs = k_cache.size(1), max_blocks = block_table.size(1);
+  dim3 grid(rows);
+  const size_t sm = std::max(D, iD) * sizeof(float);
+#define PREP(KT)                                                                                                 \
+  qsa_prep_kernel<KT><<<grid, 256, sm, STREAM>>>(                                                                \
+      proj.data_ptr<float>(), proj.size(1), qn.data_ptr<float>(), kn.data_ptr<float>(), iqn.data_ptr<float>(),   \
+      rope.data_ptr<float>(), rope_len, (KT*)k_cache.data_ptr(), (KT*)v_cache.data_ptr(),                        \
+      block_table.data_ptr<int32_t>(), max_blocks, bs, slots.data_ptr<int32_t>(), positions.data_ptr<int32_t>(), \
+      q.data_ptr<float>(), gate.data_ptr<float>(), iq.data_ptr<float>(), Hq, KV, D, iH, iD, n_tok, (float)eps, rd)
+  if (k_cache.scalar_type() == torch::kFloat8_e4m3fn) PREP(__nv_fp8_e4m3);
+  else if (k_cache.scalar_type() == torch::kBFloat16) PREP(__nv_bfloat16);
+  else PREP(float);
+#undef PREP
+  const int B = rows / n_tok;
+  const int kr_off = Hq * 2 * D + 2 * KV * D + iH * iD;
+  const size_t smc = (ratio * iD + iD) * sizeof(float);
+  if (comp_cache.scalar_type() == torch::kBFloat16)
+    qsa_compress_kernel<__nv_bfloat16><<<B, 128, smc, STREAM>>>(
+        proj.data_ptr<float>(), proj.size(1), kr_off, kr_ring.data_ptr<float>(), (__nv_bfloat16*)comp_cache.data_ptr(),
+        comp_cache.size(1), ikn.data_ptr<float>(), rope.data_ptr<float>(), rope_len, rd, slots.data_ptr<int32_t>(),
+        positions.data_ptr<int32_t>(), ratio, iD, n_tok, (float)eps);
+  else
+    qsa_compress_kernel<float><<<B, 128, smc, STREAM>>>(
+        proj.data_ptr<float>(), proj.size(1), kr_off, kr_ring.data_ptr<float>(), comp_cache.data_ptr<float>(),
+        comp_cache.size(1), ikn.data_ptr<float>(), rope.data_ptr<float>(), rope_len, rd, slots.data_ptr<int32_t>(),
+        positions.data_ptr<int32_t>(), ratio, iD, n_tok, (float)eps);
+}
+
+// Indexer scores s[row, blk] = sum_h relu(iq[row,h] . comp[blk]) / sqrt(iD) for complete blocks, -inf beyond.
+// grid (rows, chunks of 256 blocks); 256 threads, one block key per thread.
+template <typename CT>
+__global__ void qsa_scores_kernel(const float* iq, const CT* comp, int max_comp, const int* slots,
+                                  const int* positions, float* scores, int ld_scores, int iH, int iD, int r,
+                                  int n_tok) {
+  extern __shared__ float qs[];  // [iH][iD]
+  const int row = blockIdx.x;
+  const int b = row / n_tok;
+  const int p = positions[b] + row % n_tok;
+  const int nc = (p + 1) / r;
+  const int blk = blockIdx.y * blockDim.x + threadIdx.x;
+  if (blockIdx.y * blockDim.x >= nc) return;
+  for (int i = threadIdx.x; i < iH * iD; i += blockDim.x) qs[i] = iq[(int64_t)row * iH * iD + i];
+  __syncthreads();
+  if (blk >= ld_scores) return;
+  float out = -FLT_MAX;
+  if (blk < nc && blk < max_comp) {
+    const CT* kb = comp + ((int64_t)slots[b] * max_comp + blk) * iD;
+    float acc[32];
+    const int nh = min(iH, 32);
+    for (int h = 0; h < nh; ++h) acc[h] = 0.f;
+    for (int d = 0; d < iD; ++d) {
+      const float kv = ldf(&kb[d]);
+      for (int h = 0; h < nh; ++h) acc[h] += qs[h * iD + d] * kv;
+    }
+    float s = 0.f;
+    for (int h = 0; h < nh; ++h) s += fmaxf(acc[h], 0.f);
+    out = s * rsqrtf((float)iD);
+  }
+  scores[(int64_t)row * ld_scores + blk] = out;
+}
+
+__device__ __forceinline__ uint32_t f2ord(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Exact top-k (k <= n) of one row by 4-pass 8-bit radix select on order-preserving keys; writes the indices of
+// the k largest (ties at the threshold broken by lower index) into sel[row, 0..k). 512 threads.
+__global__ void topk_rows_kernel(const float* scores, int ld, const int* n_valid_row, int n_fixed, int k, int* sel,
+                                 int* sparse_flag, const int* positions, int r, int n_tok) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t s_prefix, s_kleft, s_cnt_gt, s_eq_taken;
+  const int row = blockIdx.x;
+  int n;
+  if (positions) {
+    const int p = positions[row / n_tok] + row % n_tok;
+    n = (p + 1) / r;
+  } else {
+    n = n_valid_row ? n_valid_row[row] : n_fixed;
+  }
+  n = min(n, ld);
+  int* out = sel + (int64_t)row * k;
+  if (n <= k) {
+    for (int i = threadIdx.x; i < k; i += blockDim.x) out[i] = -1;
+    if (sparse_flag && threadIdx.x == 0) sparse_flag[row] = 0;
+    return;
+  }
+  if (sparse_flag && threadIdx.x == 0) sparse_flag[row] = 1;
+  const float* x = scores + (int64_t)row * ld;
+  uint32_t prefix = 0, mask = 0;
+  uint32_t kleft = k;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint32_t u = f2ord(x[i]);
+      if ((u & mask) == prefix) atomicAdd(&hist[(u >> shift) & 255], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t acc = 0;
+      int d = 255;
+      for (; d > 0; --d) {
+        if (acc + hist[d] >= kleft) break;
+        acc += hist[d];
+      }
+      s_prefix = prefix | ((uint32_t)d << shift);
+      s_kleft = kleft - acc;
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    kleft = s_kleft;
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  // prefix = threshold key; take all > threshold, then the first `kleft` equal ones by index
+  if (threadIdx.x == 0) {
+    s_cnt_gt = 0;
+    s_eq_taken = 0;
+  }
+  __syncthreads();
+  const uint32_t thr = prefix;
+  const uint32_t n_gt = k - kleft;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const uint32_t u = f2ord(x[i]);
+    if (u > thr) {
+      const uint32_t slot = atomicAdd(&s_cnt_gt, 1u);
+      out[slot] = i;
+    }
+  }
+  __syncthreads();
+  // equal elements in index order (sequential chunks keep the lowest indices)
+  for (int base = 0; base < n; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    const bool eq = i < n && f2ord(x[i]) == thr;
+    const unsigned ballot = __ballot_sync(0xffffffffu, eq);
+    __shared__ uint32_t wcnt[32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) wcnt[w] = __popc(ballot);
+    __syncthreads();
+    uint32_t before = 0;
+    for (int ww = 0; ww < w; ++ww) before += wcnt[ww];
+    const uint32_t rank = s_eq_taken + before + __popc(ballot & ((1u << lane) - 1));
+    if (eq && rank < kleft) out[n_gt + rank] = i;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t tot = 0;
+      for (int ww = 0; ww < (int)(blockDim.x >> 5); ++ww) tot += wcnt[ww];
+      s_eq_taken += tot;
+    }
+    __syncthreads();
+    if (s_eq_taken >= kleft) break;
+  }
+}
+
+void qsa_select(torch::Tensor iq, torch::Tensor comp, torch::Tensor slots, torch::Tensor positions, torch::Tensor sel,
+                torch::Tensor sparse, int64_t nblk, int64_t r, int64_t n_tok) {
+  const int rows = iq.size(0);
+  if (!rows) return;
+  const int iH = iq.size(1), iD = iq.size(2);
+  CK(iH <= 32);
+  const int max_comp = comp.size(1);
+  const int chunks = (max_comp + 255) / 256;
+  auto scores = torch::empty({rows, chunks * 256}, iq.options());
+  const size_t sm = iH * iD * sizeof(float);
+  if (comp.scalar_type() == torch::kBFloat16)
+    qsa_scores_kernel<__nv_bfloat16><<<dim3(rows, chunks), 256, sm, STREAM>>>(
+        iq.data_ptr<float>(), (const __nv_bfloat16*)comp.data_ptr(), max_comp, slots.data_ptr<int32_t>(),
+        positions.data_ptr<int32_t>(), scores.data_ptr<float>(), chunks * 256, iH, iD, r, n_tok);
+  else
+    qsa_scores_kernel<float><<<dim3(rows, chunks), 256, sm, STREAM>>>(
+        iq.data_ptr<float>(), comp.data_ptr<float>(), max_comp, slots.data_ptr<int32_t>(),
+        positions.data_ptr<int32_t>(), scores.data_ptr<float>(), chunks * 256, iH, iD, r, n_tok);
+  topk_rows_kernel<<<rows, 512, 0, STREAM>>>(scores.data_ptr<float>(), chunks * 256, nullptr, 0, nblk,
+                                             sel.data_ptr<int32_t>(), sparse.data_ptr<int32_t>(),
+                                             positions.data_ptr<int32_t>(), r, n_tok);
+}
+
+// Generic exact top-k over rows (the sharded-indexer local select and merge use it too).
+void topk_rows(torch::Tensor scores, torch::Tensor n_valid, int64_t k, torch::Tensor sel) {
+  const int rows = scores.size(0);
+  if (!rows) return;
+  topk_rows_kernel<<<rows, 512, 0, STREAM>>>(scores.data_ptr<float>(), scores.size(1),
+                                             n_valid.numel() ? n_valid.data_ptr<int32_t>() : nullptr, scores.size(1),
+                                             k, sel.data_ptr<int32_t>(), nullptr, nullptr, 1, 1);
+}
+
+// Split-K sparse GQA decode attention. Block = (row, kv head, split), 256 threads = 8 warps; G = Hq/KV <= 8 query
+// heads share the kv head. Keys are visited in chunks of 32: thread (h = tid/32, key = lane) scores, warp h does
+// the online softmax of head h, then thread (h, lane) accumulates dims lane + 32*i of head h.
+template <typename KT, int D>
+__global__ void __launch_bounds__(256) attn_split_kernel(const float* q, const KT* kc, const KT* vc,
+                                                         const int* block_table, int max_blocks, int bs,
+                                                         const int* slots, const int* positions, const int* sel,
+                                                         const int* sparse, int nblk, int r, int KV, int G, int n_tok,
+                                                         int n_split, float* part_o, float* part_ml) {
+  constexpr int NI = D / 32;
+  extern __shared__ float sm[];
+  float* qs = sm;                    // [G][D]
+  float* ks = qs + 8 * D;            // [32][D+1]
+  float* vs = ks + 32 * (D + 1);     // [32][D]
+  const int row = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  const int b = row / n_tok;
+  const int p = positions[b] + row % n_tok;
+  const int s = slots[b];
+  const int Hq = KV * G;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool is_sparse = sparse[row] != 0;
+  const int tail0 = ((p + 1) / r) * r;
+  const int n_keys = is_sparse ? nblk * r + (p + 1 - tail0) : p + 1;
+  const int per = (n_keys + n_split - 1) / n_split;
+  const int k0 = split * per, k1 = min(n_keys, k0 + per);
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) qs[i] = q[((int64_t)row * Hq + kvh * G) * D + i];
+  float m = -FLT_MAX, l = 0.f;
+  float acc[NI];
+#pragma unroll
+  for (int i = 0; i < NI; ++i) acc[i] = 0.f;
+  const float scale = rsqrtf((float)D);
+  for (int c0 = k0; c0 < k1; c0 += 32) {
+    __syncthreads();
+    // load 32 keys (token ids resolved through the selection and the block table)
+    for (int kk = warp; kk < 32; kk += 8) {
+      const int m_idx = c0 + kk;
+      int tok = -1;
+      if (m_idx < k1) {
+        if (is_sparse) {
+          tok = m_idx < nblk * r ? sel[(int64_t)row * nblk + m_idx / r] * r + m_idx % r : tail0 + (m_idx - nblk * r);
+        } else {
+          tok = m_idx;
+        }
+      }
+      if (tok >= 0) {
+        const int blk = block_table[(int64_t)s * max_blocks + tok / bs];
+        const int64_t off = (((int64_t)blk * bs + tok % bs) * KV + kvh) * D;
+        for (int d = lane; d < D; d += 32) {
+          ks[kk * (D + 1) + d] = ldf(&kc[off + d]);
+          vs[kk * D + d] = ldf(&vc[off + d]);
+        }
+      } else {
+        for (int d = lane; d < D; d += 32) {
+          ks[kk * (D + 1) + d] = 0.f;
+          vs[kk * D + d] = 0.f;
+        }
+      }
+    }
+    __syncthreads();
+    if (warp < G) {
+      const float* qh = qs + warp * D;
+      const float* kr = ks + lane * (D + 1);
+      float sc = 0.f;
+#pragma unroll 8
+      for (int d = 0; d < D; ++d) sc += qh[d] * kr[d];
+      sc = (c0 + lane < k1) ? sc * scale : -FLT_MAX;
+      const float cm = warp_max(sc);
+      const float mn = fmaxf(m, cm);
+      const float pe = (c0 + lane < k1) ? __expf(sc - mn) : 0.f;
+      const float corr = __expf(m - mn);
+      l = l * corr + warp_sum(pe);
+      m = mn;
+#pragma unroll
+      for (int i = 0; i < NI; ++i) acc[i] *= corr;
+      for (int kk = 0; kk < 32; ++kk) {
+        const float pk = __shfl_sync(0xffffffffu, pe, kk);
+        if (c0 + kk >= k1) break;
+#pragma unroll
+        for (int i = 0; i < NI; ++i) acc[i] += pk * vs[kk * D + lane + 32 * i];
+      }
+    }
+  }
+  if (warp < G) {
+    const int h = kvh * G + warp;
+    const int64_t base = ((int64_t)row * Hq + h) * n_split + split;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) part_o[base * D + lane + 32 * i] = acc[i];
+    if (lane == 0) {
+      part_ml[base * 2] = m;
+      part_ml[base * 2 + 1] = l;
+    }
+  }
+}
+
+// Merge the splits of each (row, head) and apply the sigmoid output gate; out fp16 [rows, Hq*D].
+__global__ void attn_combine_kernel(const float* part_o, const float* part_ml, const float* gate, __half* out, int Hq,
+                                    int D, int n_split) {
+  const int row = blockIdx.x, h = blockIdx.y;
+  const int64_t base = ((int64_t)row * Hq + h) * n_split;
+  float M = -FLT_MAX;
+  for (int i = 0; i < n_split; ++i) M = fmaxf(M, part_ml[(base + i) * 2]);
+  float L = 0.f;
+  for (int i = 0; i < n_split; ++i) {
+    const float mi = part_ml[(base + i) * 2];
+    if (mi > -FLT_MAX) L += part_ml[(base + i) * 2 + 1] * __expf(mi - M);
+  }
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float o = 0.f;
+    for (int i = 0; i < n_split; ++i) {
+      const float mi = part_ml[(base + i) * 2];
+      if (mi > -FLT_MAX) o += part_o[(base + i) * D + d] * __expf(mi - M);
+    }
+    o = L > 0.f ? o / L : 0.f;
+    const int64_t oi = (int64_t)row * Hq * D + h * D + d;
+    out[oi] = __float2half_rn(o * sigm(gate[oi]));
+  }
+}
+
+void attn_decode(torch::Tensor q, torch::Tensor gate, torch::Tensor k_cache, torch::Tensor v_cache,
+                 torch::Tensor block_table, torch::Tensor slots, torch::Tensor positions, torch::Tensor sel,
+                 torch::Tensor sparse, torch::Tensor out, int64_t KV, int64_t r, int64_t n_tok) {
+  const int rows = q.size(0), Hq = q.size(1), D = q.size(2);
+  if (!rows) return;
+  const int G = Hq / KV;
+  CK(G <= 8 && Hq % KV == 0);
+  CK(D == 64 || D == 128 || D == 256);
+  const int nblk = sel.size(1);
+  // enough blocks for the machine: rows * KV * split >= ~2 waves
+  int n_split = std::max(1, std::min(16, (int)((2 * 148 + rows * KV - 1) / (rows * KV))));
+  auto part_o = torch::empty({rows, Hq, n_split, D}, q.options());
+  auto part_ml = torch::empty({rows, Hq, n_split, 2}, q.options());
+  const size_t sm = (8 * D + 32 * (D + 1) + 32 * D) * sizeof(float);
+  dim3 grid(rows, KV, n_split);
+#define ATT(KT, DD)                                                                                                 \
+  {                                                                                                                 \
+    auto kern = attn_split_kernel<KT, DD>;                                                                         \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);                             \
+    kern<<<grid, 256, sm, STREAM>>>(q.data_ptr<float>(), (const KT*)k_cache.data_ptr(), (const KT*)v_cache.data_ptr(), \
+                                    block_table.data_ptr<int32_t>(), block_table.size(1), k_cache.size(1),          \
+                                    slots.data_ptr<int32_t>(), positions.data_ptr<int32_t>(), sel.data_ptr<int32_t>(), \
+                                    sparse.data_ptr<int32_t>(), nblk, r, KV, G, n_tok, n_split,                    \
+                                    part_o.data_ptr<float>(), part_ml.data_ptr<float>());                          \
+  }
+#define ATT_D(KT)            \
+  if (D == 64) ATT(KT, 64)   \
+  else if (D == 128) ATT(KT, 128) \
+  else ATT(KT, 256)
+  if (k_cache.scalar_type() == torch::kFloat8_e4m3fn) {
+    ATT_D(__nv_fp8_e4m3)
+  } else if (k_cache.scalar_type() == torch::kBFloat16) {
+    ATT_D(__nv_bfloat16)
+  } else {
+    ATT_D(float)
+  }
+#undef ATT_D
+#undef ATT
+  attn_combine_kernel<<<dim3(rows, Hq), 128, 0, STREAM>>>(part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
+                                                          gate.data_ptr<float>(), (__half*)out.data_ptr(), Hq, D,
+                                                          n_split);
+}
+
+// ================================================================================================== MoE
+// softmax over E logits, top-k (ties -> lower id), renormalize. One block (256 threads) per token.
+__global__ void moe_route_kernel(const float* logits, int ld, int32_t* ids, float* w, int E, int k) {
+  extern __shared__ float pr[];
+  __shared__ float red_v[32];
+  __shared__ int red_i[32];
+  __shared__ float s_sum;
+  const int t = blockIdx.x;
+  const float* x = logits + (int64_t)t * ld;
+  float mx = -FLT_MAX;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) mx = fmaxf(mx, x[e]);
+  mx = warp_max(mx);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) red_v[wid] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < nw ? red_v[threadIdx.x] : -FLT_MAX;
+    v = warp_max(v);
+    if (threadIdx.x == 0) red_v[0] = v;
+  }
+  __syncthreads();
+  mx = red_v[0];
+  __syncthreads();
+  float sum = 0.f;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const float v = __expf(x[e] - mx);
+    pr[e] = v;
+    sum += v;
+  }
+  __shared__ float sh[32];
+  sum = block_sum(sum, sh);
+  if (threadIdx.x == 0) s_sum = 0.f;
+  __syncthreads();
+  float wsum = 0.f;
+  for (int j = 0; j < k; ++j) {
+    float bv = -1.f;
+    int bi = 0x7fffffff;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      const float v = pr[e];
+      if (v > bv || (v == bv && e < bi)) {
+        bv = v;
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      red_v[wid] = bv;
+      red_i[wid] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float v = red_v[0];
+      int i = red_i[0];
+      for (int q = 1; q < nw; ++q)
+        if (red_v[q] > v || (red_v[q] == v && red_i[q] < i)) {
+          v = red_v[q];
+          i = red_i[q];
+        }
+      ids[t * k + j] = i;
+      w[t * k + j] = v / sum;
+      wsum += v / sum;
+      pr[i] = -2.f;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    for (int j = 0; j < k; ++j) w[t * k + j] /= wsum;
+  }
+}
+
+void moe_route(torch::Tensor logits, torch::Tensor ids, torch::Tensor w, int64_t E, int64_t k) {
+  const int T = logits.size(0);
+  if (!T) return;
+  moe_route_kernel<<<T, 256, E * sizeof(float), STREAM>>>(logits.data_ptr<float>(), logits.size(1),
+                                                          ids.data_ptr<int32_t>(), w.data_ptr<float>(), E, k);
+}
+
+// Stable expert sort of the T*k pairs and the tile item list, in one block of 1024 threads.
+__global__ void __launch_bounds__(1024) moe_plan_kernel(const int32_t* ids, int P, int32_t* pair_pos, int4* items,
+                                                        int32_t* n_items, int E, int n_tile, int max_items) {
+  extern __shared__ int smi[];
+  int* count = smi;             // [E]
+  int* start = count + E;       // [E]
+  int* wcnt = start + E;        // [32][E]
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) count[e] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < P; i += blockDim.x) atomicAdd(&count[ids[i]], 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0, it = 0;
+    for (int e = 0; e < E; ++e) {
+      start[e] = acc;
+      for (int s0 = 0; s0 < count[e]; s0 += n_tile) {
+        if (it < max_items) items[it] = make_int4(e, acc + s0, min(n_tile, count[e] - s0), 0);
+        ++it;
+      }
+      acc += count[e];
+    }
+    *n_items = min(it, max_items);
+  }
+  __syncthreads();
+  // running per-expert offset in start[]; chunks of 1024 pairs keep the flat order stable
+  for (int base = 0; base < P; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    const int e = i < P ? ids[i] : -1;
+    for (int q = threadIdx.x; q < 32 * E; q += blockDim.x) wcnt[q] = 0;
+    __syncthreads();
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    const int rank_w = __popc(same & ((1u << lane) - 1));
+    if (i < P && rank_w == 0) wcnt[w * E + e] = __popc(same);
+    __syncthreads();
+    if (i < P) {
+      int before = 0;
+      for (int ww = 0; ww < w; ++ww) before += wcnt[ww * E + e];
+      pair_pos[i] = start[e] + before + rank_w;
+    }
+    __syncthreads();
+    for (int q = threadIdx.x; q < E; q += blockDim.x) {
+      int tot = 0;
+      for (int ww = 0; ww < 32; ++ww) tot += wcnt[ww * E + q];
+      start[q] += tot;
+    }
+    __syncthreads();
+  }
+}
+
+void moe_plan(torch::Tensor ids, torch::Tensor pair_pos, torch::Tensor items, torch::Tensor n_items, int64_t E,
+              int64_t n_tile) {
+  const int P = ids.numel();
+  const size_t sm = (2 * E + 32 * E) * sizeof(int);
+  CK(sm <= 200 * 1024);
+  auto kern = moe_plan_kernel;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  kern<<<1, 1024, sm, STREAM>>>(ids.data_ptr<int32_t>(), P, pair_pos.data_ptr<int32_t>(),
+                                reinterpret_cast<int4*>(items.data_ptr<int32_t>()), n_items.data_ptr<int32_t>(), E,
+                                n_tile, items.size(0));
+}
+
+__global__ void moe_scatter_kernel(const uint4* x, const int32_t* pair_pos, uint4* xs, int k, int row_vec) {
+  const int pair = blockIdx.x;
+  const int t = pair / k;
+  const int dst = pair_pos[pair];
+  for (int i = threadIdx.x; i < row_vec; i += blockDim.x) xs[(int64_t)dst * row_vec + i] = x[(int64_t)t * row_vec + i];
+}
+
+void moe_scatter(torch::Tensor x, torch::Tensor pair_pos, torch::Tensor xs) {
+  const int P = pair_pos.numel(), k = pair_pos.size(1);
+  if (!P) return;
+  const int rb = x.size(1) * x.element_size();
+  CK(rb % 16 == 0);
+  moe_scatter_kernel<<<P, 128, 0, STREAM>>>((const uint4*)x.data_ptr(), pair_pos.data_ptr<int32_t>(),
+                                            (uint4*)xs.data_ptr(), k, rb / 16);
+}
+
+__global__ void moe_combine_kernel(float* h, const float* ypair, const int32_t* pair_pos, const float* w,
+                                   const float* ysh, const float* sg, int ld_sg, const float* inj, int k, int hc,
+                                   int H) {
+  const int t = blockIdx.x;
+  const float g = sigm(sg[(int64_t)t * ld_sg]);
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float y = g * ysh[(int64_t)t * H + i];
+    for (int j = 0; j < k; ++j) y += w[t * k + j] * ypair[(int64_t)pair_pos[t * k + j] * H + i];
+    for (int s = 0; s < hc; ++s) h[((int64_t)t * hc + s) * H + i] += y * inj[t * hc + s];
+  }
+}
+
+void moe_combine(torch::Tensor h, torch::Tensor ypair, torch::Tensor pair_pos, torch::Tensor w, torch::Tensor ysh,
+                 torch::Tensor sg, torch::Tensor inj) {
+  const int T = pair_pos.size(0), k = pair_pos.size(1);
+  if (!T) return;
+  const int H = ysh.size(1), hc = inj.size(1);
+  const int ld_sg = sg.dim() == 1 ? sg.stride(0) : sg.stride(0);
+  moe_combine_kernel<<<T, 256, 0, STREAM>>>(h.data_ptr<float>(), ypair.data_ptr<float>(), pair_pos.data_ptr<int32_t>(),
+                                            w.data_ptr<float>(), ysh.data_ptr<float>(), sg.data_ptr<float>(), ld_sg,
+                                            inj.data_ptr<float>(), k, hc, H);
+}
+
+// ============================================================================================= sampling
+__global__ void argmax_kernel(const float* x, int V, int32_t* out) {
+  __shared__ float bv_s[32];
+  __shared__ int bi_s[32];
+  const float* r = x + (int64_t)blockIdx.x * V;
+  float bv = -FLT_MAX;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = r[i];
+    if (v > bv) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) {
+    bv_s[w] = bv;
+    bi_s[w] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int q = 1; q < (int)(blockDim.x >> 5); ++q)
+      if (bv_s[q] > bv_s[0] || (bv_s[q] == bv_s[0] && bi_s[q] < bi_s[0])) {
+        bv_s[0] = bv_s[q];
+        bi_s[0] = bi_s[q];
+      }
+    out[blockIdx.x] = bi_s[0];
+  }
+}
+
+void argmax_rows(torch::Tensor logits, torch::Tensor out) {
+  const int R = logits.size(0);
+  if (!R) return;
+  argmax_kernel<<<R, 1024, 0, STREAM>>>(logits.data_ptr<float>(), logits.size(1), out.data_ptr<int32_t>());
+}
+
+}  // namespace
+
+void register_fn(pybind11::module& m) {
+  m.def("embed_hc", &embed_hc);
+  m.def("hc_prenorm", &hc_prenorm);
+  m.def("hc_act", &hc_act);
+  m.def("hc_mix", &hc_mix);
+  m.def("hc_residual", &hc_residual);
+  m.def("gdn_step", &gdn_step);
+  m.def("qsa_prep", &qsa_prep);
+  m.def("qsa_select", &qsa_select);
+  m.def("topk_rows", &topk_rows);
+  m.def("attn_decode", &attn_decode);
+  m.def("moe_route", &moe_route);
+  m.def("moe_plan", &moe_plan);
+  m.def("moe_scatter", &moe_scatter);
+  m.def("moe_combine", &moe_combine);
+  m.def("argmax_rows", &argmax_rows);
+}

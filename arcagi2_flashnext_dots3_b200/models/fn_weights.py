@@ -57,7 +57,7 @@ def random_dense(cfg, seed: int = 0, symmetric: bool = True) -> dict:
     Hq, KV, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
     iH, iD = cfg.indexer_heads, cfg.indexer_dim
     rd = lambda *s, std=STD: torch.randn(*s, generator=g) * std  # noqa: E731
-    W = {"embed": rd(cfg.vocab_size, H, std=1.0).half().float(),
+    W = {"embed": rd(cfg.vocab_size, H, std=1.0).bfloat16().float(),
          "lm_head": _round_dense(rd(cfg.vocab_size, H), cfg),
          "mixer": _hc_params(cfg, g, combine=False), "layers": []}
     if cfg.ple_layers:
