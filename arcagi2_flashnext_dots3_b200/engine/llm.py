@@ -1,0 +1,258 @@
+"""Public serving API: :class:`LLM` owns the model, the caches, the block allocator and the decode graphs.
+
+Replaces the reference's external vLLM engine (scheduler, KV manager, CUDA graphs; the reference runs vLLM
+0.30/0.32 with FULL_DECODE_ONLY graphs for batch sizes up to 128, flashnext/kaggle/code_dataset/kaggle_fn.sh:45).
+
+* ``add(prompt)`` claims a slot, allocates paged-KV blocks and prefills in chunks.
+* ``step()`` decodes one token for every running sequence: the input ids are copied host->device from pinned
+  memory, one CUDA graph (captured per batch bucket) runs the whole model + LM head + argmax, and the new tokens
+  come back device->host. Finished sequences (eos / max tokens) release their slot and blocks.
+* ``generate(prompts, max_new_tokens)`` = add + step until done.
+* ``synthesize_context(lengths)`` fills slots with random cache state of the given lengths (used by the bench
+  to measure decode at 6k-12k contexts without spending minutes on prefill).
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import torch
+
+from ..config import EngineConfig
+from ..ops import fn_ops as ops
+from ..ops import native
+from .block_manager import BlockAllocator
+
+
+@dataclass
+class Sequence:
+    slot: int
+    prompt: list
+    max_new: int
+    out: list = field(default_factory=list)
+    pos: int = 0          # tokens already in the cache
+    done: bool = False
+    t_first: float = 0.0
+    t_last: float = 0.0
+
+
+class DecodeGraph:
+    """Static-shape decode step for `batch` rows (one CUDA graph): ids/slots/positions in, next ids out.
+    ``advance=True`` also feeds the next ids back and bumps positions inside the graph (device-only loops)."""
+
+    def __init__(self, model, batch: int, advance: bool, use_graph: bool = True, scratch_slot: int = None):
+        dev = model.device
+        self.scratch_slot = scratch_slot
+        self.model = model
+        self.batch = batch
+        self.advance = advance
+        self.ids = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.slots = torch.arange(batch, dtype=torch.int32, device=dev)
+        self.positions = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.next_ids = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.graph = None
+        self.use_graph = use_graph and model.device.type == "cuda"
+
+    def _body(self):
+        m = self.model
+        x = m.step(self.ids, self.slots, self.positions)
+        nxt = ops.argmax(m.logits(x))
+        self.next_ids.copy_(nxt)
+        if self.advance:
+            self.ids.copy_(nxt)
+            self.positions.add_(1)
+
+    def capture(self):
+        """Run the step once eagerly (warm-up, allocations), then capture it. The warm-up is a real decode step:
+        callers capture before positions are meaningful or account for it."""
+        if not self.use_graph:
+            return
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        pos0, ids0, slots0 = self.positions.clone(), self.ids.clone(), self.slots.clone()
+        if self.scratch_slot is not None:  # warm up on the scratch slot so no live sequence state changes
+            self.slots.fill_(self.scratch_slot)
+            self.positions.zero_()
+        with torch.cuda.stream(s):
+            self._body()
+        torch.cuda.current_stream().wait_stream(s)
+        self.positions.copy_(pos0)
+        self.ids.copy_(ids0)
+        self.slots.copy_(slots0)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._body()
+        self.positions.copy_(pos0)
+        self.ids.copy_(ids0)
+
+    def run(self):
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._body()
+
+
+class LLM:
+    def __init__(self, cfg, weights: dict, device="cuda", engine: EngineConfig = None, model_cls=None):
+        from ..models.fn import FNModel, allocate_caches
+        self.cfg = cfg
+        self.ec = engine or EngineConfig()
+        self.device = torch.device(device)
+        ec = self.ec
+        # one extra slot: padding rows of a graph bucket decode into it (never shared with a live sequence)
+        self.scratch = ec.max_seqs
+        self.caches = allocate_caches(cfg, self.device, ec.max_seqs + 1, ec.max_model_len, ec.block_size,
+                                      kv_dtype=ec.kv_dtype, state_dtype=ec.state_dtype)
+        self.model = (model_cls or FNModel)(cfg, weights, self.caches, self.device)
+        self.alloc = BlockAllocator(self.caches.n_blocks, ec.max_seqs + 1)
+        self.model.assign_blocks(self.scratch, 1, self.alloc)
+        self.free_slots = list(range(ec.max_seqs - 1, -1, -1))
+        self.running: dict = {}
+        self.graphs: dict = {}
+        pin = self.device.type == "cuda"
+        nh = max([ec.max_seqs] + list(ec.graph_batch_sizes))
+        self.h_ids = torch.zeros(nh, dtype=torch.int32, pin_memory=pin)
+        self.h_pos = torch.zeros(nh, dtype=torch.int32, pin_memory=pin)
+        self.h_slots = torch.zeros(nh, dtype=torch.int32, pin_memory=pin)
+        self.h_out = torch.zeros(nh, dtype=torch.int32, pin_memory=pin)
+        self.eos = getattr(cfg, "eos_token_id", -1)
+        self.stats = {"steps": 0, "tokens": 0, "prefill_tokens": 0}
+
+    # ---------------------------------------------------------------------------------- admission
+    def add(self, prompt, max_new_tokens: int = 64, prefill_chunk: int = 2048) -> Sequence:
+        if not self.free_slots:
+            raise RuntimeError("no free sequence slot")
+        slot = self.free_slots.pop()
+        self.model.reset_slot(slot)
+        seq = Sequence(slot, list(map(int, prompt)), max_new_tokens)
+        need = len(seq.prompt) + max_new_tokens
+        if need > self.ec.max_model_len:
+            self.free_slots.append(slot)
+            raise ValueError(f"sequence needs {need} tokens > max_model_len {self.ec.max_model_len}")
+        self.model.assign_blocks(slot, need, self.alloc)
+        self._prefill(seq, prefill_chunk)
+        self.running[slot] = seq
+        return seq
+
+    def _prefill(self, seq: Sequence, chunk: int):
+        dev = self.device
+        ids = torch.tensor(seq.prompt, dtype=torch.int32)
+        last = None
+        for a in range(0, len(seq.prompt), chunk):
+            b = min(len(seq.prompt), a + chunk)
+            x = self.model.step(ids[a:b].to(dev), torch.tensor([seq.slot], dtype=torch.int32, device=dev),
+                                torch.tensor([a], dtype=torch.int32, device=dev), n_tok=b - a)
+            last = x[-1:]
+        nxt = int(ops.argmax(self.model.logits(last))[0])
+        seq.pos = len(seq.prompt)
+        seq.out.append(nxt)
+        seq.t_first = time.perf_counter()
+        self.stats["prefill_tokens"] += len(seq.prompt)
+
+    def extend(self, seq: Sequence, tokens: list, max_new_tokens: int = None):
+        """Append tokens to a live sequence (multi-turn sessions: the cache is kept, only new tokens prefill).
+        The previously sampled token that was never fed is dropped in favour of the pushed tokens."""
+        if max_new_tokens is not None:
+            seq.max_new = len(seq.out) + max_new_tokens
+        need = seq.pos + len(tokens) + (seq.max_new - len(seq.out)) + 1
+        self.model.assign_blocks(seq.slot, need, self.alloc)
+        dev = self.device
+        ids = torch.tensor(tokens, dtype=torch.int32, device=dev)
+        x = self.model.step(ids, torch.tensor([seq.slot], dtype=torch.int32, device=dev),
+                            torch.tensor([seq.pos], dtype=torch.int32, device=dev), n_tok=len(tokens))
+        seq.prompt += list(tokens)
+        seq.pos += len(tokens)
+        seq.out.append(int(ops.argmax(self.model.logits(x[-1:]))[0]))
+        seq.done = False
+        self.running[seq.slot] = seq
+
+    def release(self, seq: Sequence):
+        self.running.pop(seq.slot, None)
+        self.alloc.release(seq.slot)
+        self.free_slots.append(seq.slot)
+
+    # -------------------------------------------------------------------------------------- decode
+    def _graph_for(self, n: int) -> DecodeGraph:
+        bucket = next((b for b in self.ec.graph_batch_sizes if b >= n), n)
+        g = self.graphs.get(bucket)
+        if g is None:
+            g = DecodeGraph(self.model, bucket, advance=False, use_graph=self.ec.cuda_graphs,
+                            scratch_slot=self.scratch)
+            g.capture()
+            self.graphs[bucket] = g
+        return g
+
+    def step(self) -> dict:
+        """One decode step for all running sequences. Returns {slot: new token}."""
+        seqs = [s for s in self.running.values() if not s.done]
+        if not seqs:
+            return {}
+        n = len(seqs)
+        g = self._graph_for(n)
+        B = g.batch
+        for i in range(B):
+            if i < n:
+                s = seqs[i]
+                self.h_ids[i], self.h_pos[i], self.h_slots[i] = s.out[-1], s.pos, s.slot
+            else:  # padding row: scratch slot, position 0, output ignored
+                self.h_ids[i], self.h_pos[i], self.h_slots[i] = 0, 0, self.scratch
+        g.ids.copy_(self.h_ids[:B], non_blocking=True)
+        g.positions.copy_(self.h_pos[:B], non_blocking=True)
+        g.slots.copy_(self.h_slots[:B], non_blocking=True)
+        g.run()
+        self.h_out[:B].copy_(g.next_ids, non_blocking=True)
+        if self.device.type == "cuda":
+            torch.cuda.current_stream().synchronize()
+        now = time.perf_counter()
+        res = {}
+        for i, s in enumerate(seqs):
+            t = int(self.h_out[i])
+            s.pos += 1
+            s.t_last = now
+            if len(s.out) >= s.max_new or s.out[-1] == self.eos:
+                s.done = True
+                continue
+            s.out.append(t)
+            res[s.slot] = t
+        self.stats["steps"] += 1
+        self.stats["tokens"] += len(res)
+        return res
+
+    def generate(self, prompts, max_new_tokens: int = 64) -> list:
+        seqs = [self.add(p, max_new_tokens) for p in prompts]
+        while any(not s.done for s in seqs):
+            self.step()
+            for s in seqs:
+                if len(s.out) >= s.max_new:
+                    s.done = True
+        outs = [s.out[: s.max_new] for s in seqs]
+        for s in seqs:
+            self.release(s)
+        return outs
+
+    # ------------------------------------------------------------------------------------ synthetic
+    def synthesize_context(self, lengths, max_new_tokens: int, seed: int = 0) -> list:
+        """Claim len(lengths) slots whose caches hold random state for contexts of the given lengths."""
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        c = self.caches
+        for t in c.k + c.v:
+            t.copy_(torch.randn(t.shape, generator=g, device=self.device).to(t.dtype))
+        for t in c.comp:
+            t.copy_(torch.randn(t.shape, generator=g, device=self.device).to(t.dtype))
+        for t in c.kr_ring + c.conv:
+            t.copy_(torch.randn(t.shape, generator=g, device=self.device))
+        for t in c.ssm:
+            t.copy_((torch.randn(t.shape, generator=g, device=self.device) * 0.05).to(t.dtype))
+        seqs = []
+        for L in lengths:
+            slot = self.free_slots.pop()
+            seq = Sequence(slot, [], max_new_tokens)
+            self.model.assign_blocks(slot, int(L) + max_new_tokens + 2, self.alloc)
+            seq.pos = int(L)
+            seq.out.append(int(torch.randint(0, self.cfg.vocab_size, (1,), generator=g, device=self.device)))
+            self.running[slot] = seq
+            seqs.append(seq)
+        if self.device.type == "cuda":
+            torch.cuda.synchronize()
+            native.check_error(self.device)
+        return seqs

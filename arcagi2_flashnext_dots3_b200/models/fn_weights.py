@@ -185,3 +185,132 @@ def to_engine(W: dict, cfg, device) -> dict:
                         "conv": P["conv"].reshape(P["conv"].shape[0], -1).float().to(device)}
         E["layers"].append(M)
     return E
+
+
+# ------------------------------------------------------------------------- full-size, built on the device
+def _ws_chunks(chunks: list, fmts: list, rows: int, K: int, silu_pairs: bool, device) -> wgemm.WeightSet:
+    """WeightSet from per-chunk runtime blocks ([n_e * tiles, KG, bb] each, experts consecutive in a chunk)."""
+    tiles = (rows + 127) // 128
+    total = sum(c.numel() for c in chunks)
+    blob = torch.empty(total, dtype=torch.uint8, device=device)
+    offs, o = [], 0
+    fi = 0
+    for c in chunks:
+        n_e = c.shape[0] // tiles
+        per = c.numel() // n_e
+        blob[o: o + c.numel()] = c.reshape(-1)
+        for e in range(n_e):
+            offs.append(o + e * per)
+        o += c.numel()
+        fi += n_e
+    return wgemm.WeightSet(blob, torch.tensor(offs, dtype=torch.int64, device=device),
+                           torch.tensor(fmts, dtype=torch.int8, device=device), rows, K,
+                           tuple(int(f) for f in fmts), silu_pairs)
+
+
+def _random_experts(cfg, g, device, chunk=32, symmetric=False):
+    H, I, E = cfg.hidden_size, cfg.moe_inter, cfg.n_experts
+    perm = rt.gate_up_perm(I, device=device)
+    gu_chunks, d_chunks, fmts = [], [], []
+    e = 0
+    while e < E:
+        bits = cfg.bits_of(e)
+        n = 1
+        while e + n < E and n < chunk and cfg.bits_of(e + n) == bits:
+            n += 1
+        wgu = torch.randn(n, 2 * I, H, generator=g, device=device) * STD
+        wgu = wgu[:, perm].reshape(n * 2 * I, H)
+        q, s, z = planar.quantize_rtn(wgu, bits, symmetric)
+        gu_chunks.append(rt.pack_q(q, s, z, bits))
+        del wgu, q, s, z
+        wd = (torch.randn(n * H, I, generator=g, device=device) * STD)
+        q, s, z = planar.quantize_rtn(wd, bits, symmetric)
+        d_chunks.append(rt.pack_q(q, s, z, bits))
+        del wd, q, s, z
+        fmts += [bits] * n
+        e += n
+    return (_ws_chunks(gu_chunks, fmts, 2 * I, H, True, device), _ws_chunks(d_chunks, fmts, H, I, False, device))
+
+
+def random_engine(cfg, device, seed: int = 0, symmetric: bool = False) -> dict:
+    """Engine weights of the configured size, generated and packed on `device` (N(0, 0.02) dense weights stored
+    FP8 128x128 block-scaled, experts N(0, 0.02) RTN-quantized to their bit widths with group-128 scales)."""
+    dev = torch.device(device)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    H, hc = cfg.hidden_size, cfg.hc_count
+    nk, nv, dk, dv = cfg.lin_k_heads, cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim
+    Hq, KV, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    iH, iD = cfg.indexer_heads, cfg.indexer_dim
+    R = rank_pad(cfg)
+
+    def rn(*s, std=STD):
+        return torch.randn(*s, generator=g, device=dev) * std
+
+    def dense(rows, K, silu=False, std=STD):
+        w = rn(rows, K, std=std)
+        if silu:
+            w = w[rt.gate_up_perm(rows // 2, device=dev)]
+        return _ws(w, cfg, dev, silu_pairs=silu)
+
+    def hc_params(combine=True):
+        w1 = torch.cat([rn(cfg.hc_rank, hc * H), torch.zeros(R - cfg.hc_rank, hc * H, device=dev)] +
+                       ([rn(hc, hc * H)] if combine else []), 0)
+        up = torch.cat([rn(hc * H, cfg.hc_rank, std=cfg.hc_rank ** -0.5),
+                        torch.zeros(hc * H, R - cfg.hc_rank, device=dev)], 1)
+        return {"norm": rn(hc * H, std=0.1), "w1": _ws(w1, cfg, dev), "w2": _ws(up, cfg, dev)}
+
+    E = {"embed": rn(cfg.vocab_size, H, std=1.0).to(torch.bfloat16),
+         "lm_head": dense(cfg.vocab_size, H), "mixer": hc_params(False), "layers": []}
+    if cfg.ple_layers:
+        nh = (cfg.ngram_size - 1) * cfg.heads_per_ngram
+        E["ple_table"] = torch.empty(cfg.ple_rows, cfg.ple_dim, dtype=torch.uint8, device=dev)
+        for a in range(0, cfg.ple_rows, 1 << 24):
+            b = min(cfg.ple_rows, a + (1 << 24))
+            E["ple_table"][a:b] = rn(b - a, cfg.ple_dim, std=1.0).to(torch.float8_e4m3fn).view(torch.uint8)
+        E["ple_table"] = E["ple_table"].view(torch.float8_e4m3fn)
+        E["ple_scale"] = 0.05
+        E["ple_mult"] = (torch.randint(1, 1 << 20, (cfg.ngram_size,), generator=g, device=dev) * 2 + 1).long()
+        sizes = torch.randint(cfg.ple_rows // (2 * nh), cfg.ple_rows // nh, (nh,), generator=g, device=dev).long()
+        E["ple_sizes"] = sizes
+        E["ple_offs"] = torch.cumsum(torch.cat([torch.zeros(1, dtype=torch.long, device=dev), sizes[:-1]]), 0)
+    for l in range(cfg.num_layers):
+        M = {"ahc": hc_params(), "mhc": hc_params()}
+        if l in cfg.ple_layers:
+            M["ple"] = {"kp": dense(hc * H, nh * cfg.ple_dim), "vp": dense(H, nh * cfg.ple_dim),
+                        "nk": rn(hc * H, std=0.1), "nq": rn(hc * H, std=0.1), "nc": rn(hc * H, std=0.1),
+                        "conv": rn(hc * H, cfg.ple_conv, std=0.3)}
+        if cfg.layer_kind(l) == "linear":
+            C = 2 * nk * dk + nv * dv
+            M["mix"] = {"proj": dense(C + nv * dv + 2 * nv, H), "out": dense(H, nv * dv),
+                        "conv": rn(C, cfg.conv_kernel, std=0.3),
+                        "A_log": torch.log(torch.rand(nv, generator=g, device=dev) * 15 + 1),
+                        "dt_bias": rn(nv, std=0.5), "norm": 1.0 + rn(dv, std=0.1)}
+        else:
+            M["mix"] = {"proj": dense(Hq * 2 * D + 2 * KV * D + iH * iD + iD, H), "o": dense(H, Hq * D),
+                        "qn": rn(D, std=0.1), "kn": rn(D, std=0.1), "iqn": rn(iD, std=0.1), "ikn": rn(iD, std=0.1)}
+        gu, d = _random_experts(cfg, g, dev, symmetric=symmetric)
+        router = rn(cfg.n_experts + 1, H)
+        M["moe"] = {"router": wgemm.build_weight_set([rt.pack_f16(router)], [16], router.shape[0], H, device=dev),
+                    "gu": gu, "d": d, "sgu": dense(2 * cfg.shared_inter, H, silu=True),
+                    "sd": dense(H, cfg.shared_inter)}
+        E["layers"].append(M)
+    return E
+
+
+def engine_bytes(E: dict) -> dict:
+    """Bytes of the engine weights by kind (expert / dense / embedding)."""
+    out = {"experts": 0, "dense": 0, "embed": 0}
+
+    def walk(x, key):
+        if isinstance(x, wgemm.WeightSet):
+            out["experts" if key in ("gu", "d") else "dense"] += x.nbytes()
+        elif isinstance(x, dict):
+            for k, v in x.items():
+                walk(v, k)
+        elif isinstance(x, list):
+            for v in x:
+                walk(v, key)
+        elif torch.is_tensor(x):
+            out["embed" if key in ("embed", "ple_table") else "dense"] += x.numel() * x.element_size()
+    walk(E, "")
+    return out
