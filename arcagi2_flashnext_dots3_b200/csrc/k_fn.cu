@@ -13,6 +13,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 #include <cfloat>
+#include <atomic>
 #include "kernels.h"
 
 namespace {
@@ -1026,4 +1027,71 @@ void register_fn(pybind11::module& m) {
   m.def("moe_scatter", &moe_scatter);
   m.def("moe_combine", &moe_combine);
   m.def("argmax_rows", &argmax_rows);
+}
+
+// =============================================================================== allocation-free entry point
+// fw_qsa_select_noalloc: the indexer top-k select (block scores + exact radix top-k) for callers that cannot
+// allocate device memory, e.g. code running inside a foreign runtime's memory pool or a plugin host that owns
+// every allocation and forbids cudaMalloc/cudaFree from its extensions. It has no counterpart in the reference.
+//
+// It calls no cudaMalloc, cudaFree or allocating library routine. Its scratch (the fp32 score matrix,
+// rows x ceil(max_comp/256)*256 floats) lives in the file-scope array below, at most kNoAllocScoreFloats floats
+// (2 MiB); every GPU that loads this library holds that array until the process exits. Larger requests are
+// rejected with FW_NOALLOC_TOO_BIG before anything is launched.
+//
+// * Set-up: the first call on a device (with that device current) looks up the array's device address with
+//   cudaGetSymbolAddress and caches it per device; make that first call before any stream capture.
+// * Sharing: all calls on a device share the one array and it keeps the last call's contents. Nothing in it has
+//   to start at zero (every score a call reads is written by that call first). Calls that overlap on the GPU
+//   (different streams without ordering) race on the array: serialize them on one stream.
+// * Inputs/outputs are the caller's: iq [rows, iH, iD] fp32, comp [S, max_comp, iD] (bf16 if comp_bf16 else
+//   fp32), slots [rows / n_tok] int32, positions [rows / n_tok] int32, sel [rows, nblk] int32, sparse [rows] int32.
+// Returns 0 on success, FW_NOALLOC_INVALID / FW_NOALLOC_TOO_BIG, or 1000 + cudaError_t.
+namespace {
+constexpr size_t kNoAllocScoreFloats = (size_t)1 << 19;
+__device__ __align__(256) float g_noalloc_scores[kNoAllocScoreFloats];
+constexpr int kNoAllocMaxDevices = 64;
+std::atomic<float*> g_noalloc_ptr[kNoAllocMaxDevices];
+}  // namespace
+
+enum { FW_NOALLOC_OK = 0, FW_NOALLOC_INVALID = 1, FW_NOALLOC_TOO_BIG = 2 };
+
+extern "C" __attribute__((visibility("default"))) size_t fw_qsa_select_noalloc_max_floats() {
+  return kNoAllocScoreFloats;
+}
+
+extern "C" __attribute__((visibility("default"))) int fw_qsa_select_noalloc(
+    const float* iq, const void* comp, int comp_bf16, const int* slots, const int* positions, int* sel, int* sparse,
+    int rows, int iH, int iD, int max_comp, int nblk, int r, int n_tok, cudaStream_t stream) {
+  if (rows == 0) return FW_NOALLOC_OK;
+  if (rows < 0 || iH <= 0 || iH > 32 || iD <= 0 || max_comp <= 0 || nblk <= 0 || r <= 0 || n_tok <= 0 ||
+      rows % n_tok || !iq || !comp || !slots || !positions || !sel || !sparse)
+    return FW_NOALLOC_INVALID;
+  const size_t smem = (size_t)iH * iD * sizeof(float);
+  if (smem > 48 * 1024) return FW_NOALLOC_INVALID;
+  const int chunks = (max_comp + 255) / 256;
+  const size_t need = (size_t)rows * chunks * 256;
+  if (need > kNoAllocScoreFloats) return FW_NOALLOC_TOO_BIG;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return 1000 + (int)e;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return FW_NOALLOC_INVALID;
+  float* scores = g_noalloc_ptr[dev].load();
+  if (!scores) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scores);
+    if (e != cudaSuccess) return 1000 + (int)e;
+    scores = static_cast<float*>(p);
+    g_noalloc_ptr[dev].store(scores);
+  }
+  const int ld = chunks * 256;
+  if (comp_bf16)
+    qsa_scores_kernel<__nv_bfloat16><<<dim3(rows, chunks), 256, smem, stream>>>(
+        iq, static_cast<const __nv_bfloat16*>(comp), max_comp, slots, positions, scores, ld, iH, iD, r, n_tok);
+  else
+    qsa_scores_kernel<float><<<dim3(rows, chunks), 256, smem, stream>>>(
+        iq, static_cast<const float*>(comp), max_comp, slots, positions, scores, ld, iH, iD, r, n_tok);
+  topk_rows_kernel<<<rows, 512, 0, stream>>>(scores, ld, nullptr, 0, nblk, sel, sparse, positions, r, n_tok);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? FW_NOALLOC_OK : 1000 + (int)e;
 }
