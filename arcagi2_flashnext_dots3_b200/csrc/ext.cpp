@@ -23,12 +23,21 @@ int sm_count() {
   return n;
 }
 
+// Zero-initialised split-K arrival counters, one pool per device; kernels leave every counter at zero.
+int* counter_pool(const torch::Device& dev, int64_t need) {
+  static std::vector<torch::Tensor> pools(64);
+  const int i = dev.index();
+  TORCH_CHECK(i >= 0 && i < 64 && need <= (1 << 20), "split-K counter pool too small");
+  if (!pools[i].defined()) pools[i] = torch::zeros({1 << 20}, torch::TensorOptions().dtype(torch::kInt32).device(dev));
+  return pools[i].data_ptr<int32_t>();
+}
+
 // y = x @ W^T with W in runtime tile blocks. x: fp16 [rows, K] (token matrix, K-contiguous).
 void wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, int64_t row_tiles, int64_t kg,
            c10::optional<torch::Tensor> items, c10::optional<torch::Tensor> n_items, int64_t max_items,
            int64_t dense_T, torch::Tensor x, int64_t b_row0, torch::Tensor out, int64_t out_row0,
            int64_t out_cols, int64_t epi, bool accumulate, double alpha, int64_t n_tile, int64_t max_block_bytes,
-           torch::Tensor err, int64_t timeout_ns) {
+           torch::Tensor err, int64_t timeout_ns, int64_t k_splits) {
   CHECK_CUDA(wbase); CHECK_CUDA(x); CHECK_CUDA(out); CHECK_CUDA(err);
   CHECK_CONTIG(x); CHECK_CONTIG(out);
   CHECK_ALIGN16(wbase); CHECK_ALIGN16(x);
@@ -72,21 +81,49 @@ void wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, in
   a.alpha = (float)alpha;
   a.err = err.data_ptr<int32_t>();
   a.timeout_ns = (unsigned long long)timeout_ns;
+  static const int dbg = getenv("FW_WGEMM_DBG") ? atoi(getenv("FW_WGEMM_DBG")) : 0;
+  a.dbg = dbg;
 
-  const int ab_stages = n_tile >= 128 ? 2 : 3;
-  const size_t fixed = fw::wgemm_smem_bytes((int)n_tile, 0, 0, ab_stages) + 8 * 24;
+  static const int ab_env = getenv("FW_WGEMM_AB") ? atoi(getenv("FW_WGEMM_AB")) : 0;
+  int g2 = 1;
+  int ab_stages = n_tile >= 128 ? 2 : (n_tile >= 64 ? 3 : 4);
+  if (ab_env > 0) ab_stages = ab_env;
   const size_t budget = 232448;
-  int w_stages = (int)((budget - fixed) / (size_t)max_block_bytes);
+  size_t fixed = fw::wgemm_smem_bytes((int)n_tile, g2, 0, 0, ab_stages) + 8 * 24;
+  if (g2 == 2 && (budget - fixed) / (2 * (size_t)max_block_bytes) < 2) {  // e.g. fp16 weights: one group per stage
+    g2 = 1;
+    ab_stages = 4;
+    fixed = fw::wgemm_smem_bytes((int)n_tile, g2, 0, 0, ab_stages) + 8 * 24;
+  }
+  a.groups_per_stage = g2;
+  const size_t w_stage_bytes = (size_t)g2 * max_block_bytes;
+  int w_stages = (int)((budget - fixed) / w_stage_bytes);
   w_stages = std::min(w_stages, 12);
   TORCH_CHECK(w_stages >= 2, "not enough shared memory for two weight stages");
-  a.w_stage_bytes = (int)max_block_bytes;
+  a.w_stage_bytes = (int)w_stage_bytes;
   a.w_stages = w_stages;
   a.ab_stages = ab_stages;
+
+  // split-K for dense GEMMs that would leave most SMs idle
+  int ks = 1;
+  if (dense_T >= 0) {
+    const int64_t base = ((dense_T + n_tile - 1) / n_tile) * row_tiles;
+    if (base < sm_count()) ks = (int)std::min<int64_t>({kg, 16, (3 * sm_count() / 2 + base - 1) / base});
+    if (k_splits > 0) ks = (int)std::min<int64_t>(k_splits, kg);
+  }
+  a.k_splits = ks;
+  torch::Tensor ws_t;
+  if (ks > 1) {
+    const int64_t tiles = ((dense_T + n_tile - 1) / n_tile) * row_tiles;
+    ws_t = torch::empty({tiles * ks * n_tile * 128}, x.options().dtype(torch::kFloat));
+    a.workspace = ws_t.data_ptr<float>();
+    a.counters = counter_pool(x.device(), tiles);
+  }
 
   CUtensorMap bmap;
   int rc = fw::make_tmap_2d_f16(&bmap, x.data_ptr(), x.size(0), x.size(1), x.size(1), 64, (uint32_t)n_tile, true);
   TORCH_CHECK(rc == 0, "cuTensorMapEncodeTiled failed: ", rc);
-  const int64_t work = (dense_T >= 0 ? (dense_T + n_tile - 1) / n_tile : max_items) * row_tiles;
+  const int64_t work = (dense_T >= 0 ? (dense_T + n_tile - 1) / n_tile : max_items) * row_tiles * ks;
   if (work <= 0) return;
   const int grid = (int)std::min<int64_t>(sm_count(), work);
   rc = fw::wgemm_launch(a, bmap, grid, at::cuda::getCurrentCUDAStream());

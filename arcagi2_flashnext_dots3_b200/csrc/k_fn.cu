@@ -134,7 +134,7 @@ void hc_act(torch::Tensor z, torch::Tensor a, torch::Tensor inj, int64_t rank_pa
 __global__ void hc_mix_kernel(const float* u, const __half* hn, __half* out, int hc, int H) {
   const int t = blockIdx.x;
   const float inv = 1.f / hc;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+  for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < H; i += blockDim.x * gridDim.y) {
     float acc = 0.f;
     for (int s = 0; s < hc; ++s) {
       const int64_t o = ((int64_t)t * hc + s) * H + i;
@@ -147,13 +147,13 @@ __global__ void hc_mix_kernel(const float* u, const __half* hn, __half* out, int
 void hc_mix(torch::Tensor u, torch::Tensor hn, torch::Tensor out, int64_t hc, int64_t H) {
   const int T = u.size(0);
   if (!T) return;
-  hc_mix_kernel<<<T, 256, 0, STREAM>>>(u.data_ptr<float>(), (const __half*)hn.data_ptr(), (__half*)out.data_ptr(),
+  hc_mix_kernel<<<dim3(T, (H + 255) / 256), 256, 0, STREAM>>>(u.data_ptr<float>(), (const __half*)hn.data_ptr(), (__half*)out.data_ptr(),
                                        hc, H);
 }
 
 __global__ void hc_residual_kernel(float* h, const float* y, const float* inj, int hc, int H) {
   const int t = blockIdx.x;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+  for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < H; i += blockDim.x * gridDim.y) {
     const float v = y[(int64_t)t * H + i];
     for (int s = 0; s < hc; ++s) h[((int64_t)t * hc + s) * H + i] += v * inj[t * hc + s];
   }
@@ -162,7 +162,7 @@ __global__ void hc_residual_kernel(float* h, const float* y, const float* inj, i
 void hc_residual(torch::Tensor h, torch::Tensor y, torch::Tensor inj) {
   const int T = h.size(0), hc = inj.size(1), H = y.size(1);
   if (!T) return;
-  hc_residual_kernel<<<T, 256, 0, STREAM>>>(h.data_ptr<float>(), y.data_ptr<float>(), inj.data_ptr<float>(), hc, H);
+  hc_residual_kernel<<<dim3(T, (H + 255) / 256), 256, 0, STREAM>>>(h.data_ptr<float>(), y.data_ptr<float>(), inj.data_ptr<float>(), hc, H);
 }
 
 // ======================================================================================= Gated DeltaNet
@@ -946,7 +946,7 @@ __global__ void moe_combine_kernel(float* h, const float* ypair, const int32_t* 
                                    int H) {
   const int t = blockIdx.x;
   const float g = sigm(sg[(int64_t)t * ld_sg]);
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+  for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < H; i += blockDim.x * gridDim.y) {
     float y = g * ysh[(int64_t)t * H + i];
     for (int j = 0; j < k; ++j) y += w[t * k + j] * ypair[(int64_t)pair_pos[t * k + j] * H + i];
     for (int s = 0; s < hc; ++s) h[((int64_t)t * hc + s) * H + i] += y * inj[t * hc + s];
@@ -959,7 +959,7 @@ void moe_combine(torch::Tensor h, torch::Tensor ypair, torch::Tensor pair_pos, t
   if (!T) return;
   const int H = ysh.size(1), hc = inj.size(1);
   const int ld_sg = sg.dim() == 1 ? sg.stride(0) : sg.stride(0);
-  moe_combine_kernel<<<T, 256, 0, STREAM>>>(h.data_ptr<float>(), ypair.data_ptr<float>(), pair_pos.data_ptr<int32_t>(),
+  moe_combine_kernel<<<dim3(T, (H + 255) / 256), 256, 0, STREAM>>>(h.data_ptr<float>(), ypair.data_ptr<float>(), pair_pos.data_ptr<int32_t>(),
                                             w.data_ptr<float>(), ysh.data_ptr<float>(), sg.data_ptr<float>(), ld_sg,
                                             inj.data_ptr<float>(), k, hc, H);
 }

@@ -54,6 +54,8 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
+// try_wait with a suspend-time hint: a waiting thread is parked (no issue slots) until the phase completes or
+// about 0.5 ms pass, so spinning roles do not steal issue bandwidth from the compute warps.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -68,18 +70,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code,
                                           volatile int* abort_flag, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = globaltimer_ns();
+  uint64_t t0 = 0;
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63) == 0) {
+    if ((it & 255) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > limit_ns) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > limit_ns) {
         atomicCAS(err, 0, code);
         *abort_flag = 1;
         return false;
       }
     }
   }
+}
+
+// Warp-wide bounded wait: lane 0 polls the barrier, the outcome is broadcast. Polling from all 32 lanes makes
+// 32 same-address barrier operations per poll, which serialize; one poller keeps hand-offs cheap. The shuffle
+// (a warp-synchronous operation) orders the other lanes' later shared-memory reads after lane 0's acquire.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, int* err, int code,
+                                               volatile int* abort_flag, uint64_t limit_ns) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, err, code, abort_flag, limit_ns) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
 }
 
 // ------------------------------------------------------------------------------------------ fences

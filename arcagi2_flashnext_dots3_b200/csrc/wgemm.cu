@@ -210,6 +210,25 @@ __device__ __forceinline__ void dequant_block(uint32_t wb, int r, int h, uint32_
     dequant_half<FMT, 1>(wb, r, a_stage + 16384);
 }
 
+struct Work {
+  int e, t0, nt, item, tile, split, g0, g1;
+};
+
+__device__ __forceinline__ void item_of(const WGemmArgs& a, int idx, int& e, int& t0, int& nt);
+
+// Work index -> (token item, 128-row tile, K split); splits of one tile are consecutive.
+__device__ __forceinline__ Work decode_work(const WGemmArgs& a, int w, int KS) {
+  Work wk;
+  wk.split = w % KS;
+  const int rest = w / KS;
+  wk.tile = rest % a.row_tiles;
+  wk.item = rest / a.row_tiles;
+  item_of(a, wk.item, wk.e, wk.t0, wk.nt);
+  wk.g0 = wk.split * a.kg / KS;
+  wk.g1 = (wk.split + 1) * a.kg / KS;
+  return wk;
+}
+
 __device__ __forceinline__ void item_of(const WGemmArgs& a, int idx, int& e, int& t0, int& nt) {
   if (a.dense_T >= 0) {
     e = 0;
@@ -281,7 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int n_items = a.dense_T >= 0 ? (a.dense_T + a.n_tile - 1) / a.n_tile : min(*a.n_items, a.max_items);
-  const int total = n_items * a.row_tiles;
+  const int KS = a.k_splits > 1 ? a.k_splits : 1;
+  const int total = n_items * a.row_tiles * KS;
   const uint64_t lim = a.timeout_ns;
   int* err = a.err;
 
@@ -291,17 +311,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol = l2_policy_evict_first();
       uint32_t k = 0;
       for (int w = blockIdx.x; w < total && !*abort_flag; w += gridDim.x) {
-        int e, t0, nt;
-        item_of(a, w / a.row_tiles, e, t0, nt);
-        const int tile = w % a.row_tiles;
-        const int fmt = a.exp_fmt[e];
+        const Work wk = decode_work(a, w, KS);
+        const int fmt = a.exp_fmt[wk.e];
         const uint32_t bb = wgemm_block_bytes(fmt);
-        const uint8_t* src = a.wbase + a.exp_off[e] + (size_t)tile * a.kg * bb;
-        for (int g = 0; g < a.kg; ++g, ++k) {
+        const uint8_t* src = a.wbase + a.exp_off[wk.e] + (size_t)wk.tile * a.kg * bb;
+        for (int g = wk.g0; g < wk.g1; ++g, ++k) {
           const int s = k % S;
           if (!mbar_wait(bar_w_empty + 8 * s, ((k / S) & 1) ^ 1, err, 1001, abort_flag, lim)) break;
-          mbar_arrive_expect_tx(bar_w_full + 8 * s, bb);
-          tma_bulk_g2s(base + w_off + s * a.w_stage_bytes, src + (size_t)g * bb, bb, bar_w_full + 8 * s, pol);
+          if (a.dbg & 8) {
+            mbar_arrive(bar_w_full + 8 * s);
+          } else {
+            mbar_arrive_expect_tx(bar_w_full + 8 * s, bb);
+            tma_bulk_g2s(base + w_off + s * a.w_stage_bytes, src + (size_t)g * bb, bb, bar_w_full + 8 * s, pol);
+          }
         }
       }
       // drain: the last S copies must have landed before the CTA may exit
@@ -314,15 +336,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one()) {
       uint32_t j = 0;
       for (int w = blockIdx.x; w < total && !*abort_flag; w += gridDim.x) {
-        int e, t0, nt;
-        item_of(a, w / a.row_tiles, e, t0, nt);
-        for (int g = 0; g < a.kg; ++g, ++j) {
+        const Work wk = decode_work(a, w, KS);
+        for (int g = wk.g0; g < wk.g1; ++g, ++j) {
           const int p = j % P;
           if (!mbar_wait(bar_ab_empty + 8 * p, ((j / P) & 1) ^ 1, err, 2001, abort_flag, lim)) break;
+          if (a.dbg & 16) {
+            mbar_arrive(bar_b_full + 8 * p);
+            continue;
+          }
           const uint32_t bdst = base + p * ab_stage + a_bytes;
           mbar_arrive_expect_tx(bar_b_full + 8 * p, b_bytes);
-          tma_load_2d(bdst, &bmap, g * 128, a.b_row0 + t0, bar_b_full + 8 * p);
-          tma_load_2d(bdst + N * 128, &bmap, g * 128 + 64, a.b_row0 + t0, bar_b_full + 8 * p);
+          tma_load_2d(bdst, &bmap, g * 128, a.b_row0 + wk.t0, bar_b_full + 8 * p);
+          tma_load_2d(bdst + N * 128, &bmap, g * 128 + 64, a.b_row0 + wk.t0, bar_b_full + 8 * p);
         }
       }
       volatile int no_abort = 0;
@@ -336,12 +361,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t j = 0;
       int it = 0;
       for (int w = blockIdx.x; w < total && !*abort_flag; w += gridDim.x, ++it) {
+        const Work wk = decode_work(a, w, KS);
         const int buf = it & 1;
         if (!mbar_wait(bar_acc_empty + 8 * buf, ((it >> 1) & 1) ^ 1, err, 3001, abort_flag, lim)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + buf * N;
         bool ok = true;
-        for (int g = 0; g < a.kg; ++g, ++j) {
+        for (int g = wk.g0; g < wk.g1; ++g, ++j) {
           const int p = j % P;
           const uint32_t par = (j / P) & 1;
           if (!mbar_wait(bar_b_full + 8 * p, par, err, 3002, abort_flag, lim) ||
@@ -352,11 +378,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t as = base + p * ab_stage;
           const uint32_t bs = as + a_bytes;
+          if (!(a.dbg & 2)) {
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t ad = umma_desc_sw128(as + (kk >> 2) * 16384 + (kk & 3) * 32);
-            const uint64_t bd = umma_desc_sw128(bs + (kk >> 2) * (N * 128) + (kk & 3) * 32);
-            umma_f16(d, ad, bd, idesc, (g | kk) != 0);
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint64_t ad = umma_desc_sw128(as + (kk >> 2) * 16384 + (kk & 3) * 32);
+              const uint64_t bd = umma_desc_sw128(bs + (kk >> 2) * (N * 128) + (kk & 3) * 32);
+              umma_f16(d, ad, bd, idesc, (g != wk.g0 || kk != 0) ? 1u : 0u);
+            }
           }
           umma_commit(bar_ab_empty + 8 * p);
         }
@@ -373,11 +401,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = d & 127, h = d >> 7;
     uint32_t k = 0, j = 0;
     for (int w = blockIdx.x; w < total && !*abort_flag; w += gridDim.x) {
-      int e, t0, nt;
-      item_of(a, w / a.row_tiles, e, t0, nt);
-      const int fmt = a.exp_fmt[e];
+      const Work wk = decode_work(a, w, KS);
+      const int fmt = a.exp_fmt[wk.e];
       bool ok = true;
-      for (int g = 0; g < a.kg; ++g, ++k, ++j) {
+      for (int g = wk.g0; g < wk.g1; ++g, ++k, ++j) {
         const int s = k % S, p = j % P;
         if (!mbar_wait(bar_w_full + 8 * s, (k / S) & 1, err, 4001, abort_flag, lim) ||
             !mbar_wait(bar_ab_empty + 8 * p, ((j / P) & 1) ^ 1, err, 4002, abort_flag, lim)) {
@@ -386,14 +413,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint32_t wb = base + w_off + s * a.w_stage_bytes;
         const uint32_t as = base + p * ab_stage;
-        switch (fmt) {
-          case 4: dequant_block<4>(wb, r, h, as); break;
-          case 3: dequant_block<3>(wb, r, h, as); break;
-          case 2: dequant_block<2>(wb, r, h, as); break;
-          case 8: dequant_block<8>(wb, r, h, as); break;
-          default: dequant_block<16>(wb, r, h, as); break;
+        if (!(a.dbg & 1)) {
+          switch (fmt) {
+            case 4: dequant_block<4>(wb, r, h, as); break;
+            case 3: dequant_block<3>(wb, r, h, as); break;
+            case 2: dequant_block<2>(wb, r, h, as); break;
+            case 8: dequant_block<8>(wb, r, h, as); break;
+            default: dequant_block<16>(wb, r, h, as); break;
+          }
         }
-        fence_proxy_async_smem();
+        if (!(a.dbg & 4)) fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(bar_w_empty + 8 * s);
@@ -407,74 +436,116 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int row = q * 32 + lane;
     float* xch = reinterpret_cast<float*>(base_ptr + epi_off);  // [64 rows][17] fp32
+    volatile int* last_flag = reinterpret_cast<volatile int*>(base_ptr + misc_off + 8);
     int it = 0;
     for (int w = blockIdx.x; w < total && !*abort_flag; w += gridDim.x, ++it) {
-      int e, t0, nt;
-      item_of(a, w / a.row_tiles, e, t0, nt);
-      const int tile = w % a.row_tiles;
+      const Work wk = decode_work(a, w, KS);
       const int buf = it & 1;
       if (!mbar_wait(bar_acc_full + 8 * buf, (it >> 1) & 1, err, 5001, abort_flag, lim)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * N;
-      const size_t orow0 = (size_t)(a.out_row0 + t0);
-      if (a.epi == WGEMM_EPI_STORE) {
-        const int col = tile * 128 + row;
-#pragma unroll
-        for (int c = 0; c < N / 16; ++c) {
-          uint32_t v[16];
-          tmem_ld16(taddr + c * 16, v);
-          tmem_ld_wait();
-          if (col < a.out_cols) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int n = c * 16 + i;
-              if (n < nt) {
-                const float f = __uint_as_float(v[i]) * a.alpha;
-                const size_t o = (orow0 + n) * a.out_ld + col;
-                if (a.out_dtype == WGEMM_OUT_F32) {
-                  float* op = reinterpret_cast<float*>(a.out) + o;
-                  *op = a.accumulate ? *op + f : f;
-                } else if (a.out_dtype == WGEMM_OUT_BF16) {
-                  reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(f);
-                } else {
-                  reinterpret_cast<__half*>(a.out)[o] = __float2half_rn(f);
-                }
-              }
-            }
-          }
-        }
-      } else {
-        // silu(gate) * up: tile rows 0-63 are gate features 64*tile.., rows 64-127 the matching up rows
+      bool emit = !(a.dbg & 32);
+      float* part = nullptr;
+      if (KS > 1 && emit) {
+        // park this split's partial; the last split to arrive for the tile does the epilogue
+        const size_t tile_id = (size_t)wk.item * a.row_tiles + wk.tile;
+        part = a.workspace + tile_id * (size_t)KS * N * 128;
 #pragma unroll 1
         for (int c = 0; c < N / 16; ++c) {
           uint32_t v[16];
           tmem_ld16(taddr + c * 16, v);
           tmem_ld_wait();
-          if (q >= 2) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) xch[(row - 64) * 17 + i] = __uint_as_float(v[i]);
-          }
-          named_barrier(1, kEpiThreads);
-          if (q < 2) {
-            const int f = tile * 64 + row;
+          for (int i = 0; i < 16; ++i) part[((size_t)wk.split * N + c * 16 + i) * 128 + row] = __uint_as_float(v[i]);
+        }
+        __threadfence();
+        named_barrier(1, kEpiThreads);
+        if (threadIdx.x == 384) {
+          const int old = atomicAdd(a.counters + tile_id, 1);
+          const int last = old == KS - 1;
+          if (last) a.counters[tile_id] = 0;
+          *last_flag = last;
+        }
+        named_barrier(1, kEpiThreads);
+        emit = *last_flag != 0;
+        if (emit) __threadfence();
+      }
+      if (emit) {
+        const size_t orow0 = (size_t)(a.out_row0 + wk.t0);
+#pragma unroll 1
+        for (int c = 0; c < N / 16; ++c) {
+          float v[16];
+          if (KS > 1) {
+            // the loads of two splits are issued before their adds (latency overlap); the adds stay in split
+            // order, so the sum is the same whichever split arrived last
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int n = c * 16 + i;
-              if (n < nt && f < a.out_cols) {
-                const float g = __uint_as_float(v[i]);
-                const float u = xch[row * 17 + i];
-                const float y = silu_f(g) * u;
-                const size_t o = (orow0 + n) * a.out_ld + f;
-                if (a.out_dtype == WGEMM_OUT_BF16)
-                  reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(y);
-                else if (a.out_dtype == WGEMM_OUT_F32)
-                  reinterpret_cast<float*>(a.out)[o] = y;
-                else
-                  reinterpret_cast<__half*>(a.out)[o] = __float2half_rn(y);
+            for (int i = 0; i < 16; ++i) v[i] = 0.f;
+            for (int s2 = 0; s2 < KS; s2 += 2) {
+              float t0v[16], t1v[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                t0v[i] = __ldcg(part + ((size_t)s2 * N + c * 16 + i) * 128 + row);
+                t1v[i] = (s2 + 1 < KS) ? __ldcg(part + ((size_t)(s2 + 1) * N + c * 16 + i) * 128 + row) : 0.f;
+              }
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                v[i] += t0v[i];
+                if (s2 + 1 < KS) v[i] += t1v[i];
               }
             }
+          } else {
+            uint32_t u[16];
+            tmem_ld16(taddr + c * 16, u);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(u[i]);
           }
-          named_barrier(1, kEpiThreads);
+          if (a.epi == WGEMM_EPI_STORE) {
+            const int col = wk.tile * 128 + row;
+            if (col < a.out_cols) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int n = c * 16 + i;
+                if (n < wk.nt) {
+                  const float f = v[i] * a.alpha;
+                  const size_t o = (orow0 + n) * a.out_ld + col;
+                  if (a.out_dtype == WGEMM_OUT_F32) {
+                    float* op = reinterpret_cast<float*>(a.out) + o;
+                    *op = a.accumulate ? *op + f : f;
+                  } else if (a.out_dtype == WGEMM_OUT_BF16) {
+                    reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(f);
+                  } else {
+                    reinterpret_cast<__half*>(a.out)[o] = __float2half_rn(f);
+                  }
+                }
+              }
+            }
+          } else {
+            // silu(gate) * up: tile rows 0-63 are gate features 64*tile.., rows 64-127 the matching up rows
+            if (q >= 2) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) xch[(row - 64) * 17 + i] = v[i];
+            }
+            named_barrier(1, kEpiThreads);
+            if (q < 2) {
+              const int f = wk.tile * 64 + row;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int n = c * 16 + i;
+                if (n < wk.nt && f < a.out_cols) {
+                  const float y = silu_f(v[i]) * xch[row * 17 + i];
+                  const size_t o = (orow0 + n) * a.out_ld + f;
+                  if (a.out_dtype == WGEMM_OUT_BF16)
+                    reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(y);
+                  else if (a.out_dtype == WGEMM_OUT_F32)
+                    reinterpret_cast<float*>(a.out)[o] = y;
+                  else
+                    reinterpret_cast<__half*>(a.out)[o] = __float2half_rn(y);
+                }
+              }
+            }
+            named_barrier(1, kEpiThreads);
+          }
         }
       }
       tc_fence_before();
@@ -516,7 +587,9 @@ int make_tmap_2d_f16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t 
   return (int)r;
 }
 
-size_t wgemm_smem_bytes(int n_tile, int w_stage_bytes, int w_stages, int ab_stages) {
+int wgemm_groups_per_stage(int) { return 1; }
+
+size_t wgemm_smem_bytes(int n_tile, int g2, int w_stage_bytes, int w_stages, int ab_stages) {
   size_t ab = (size_t)ab_stages * (32768 + 2 * n_tile * 128);
   size_t w = (size_t)w_stages * w_stage_bytes;
   size_t bars = 8 * (2 * w_stages + 3 * ab_stages + 5) + 16;
@@ -534,7 +607,7 @@ static int launch_n(const WGemmArgs& a, const CUtensorMap& map, int grid, size_t
 }
 
 int wgemm_launch(const WGemmArgs& a, const CUtensorMap& bmap, int grid, cudaStream_t st) {
-  size_t smem = wgemm_smem_bytes(a.n_tile, a.w_stage_bytes, a.w_stages, a.ab_stages);
+  size_t smem = wgemm_smem_bytes(a.n_tile, 1, a.w_stage_bytes, a.w_stages, a.ab_stages);
   switch (a.n_tile) {
     case 16: return launch_n<16>(a, bmap, grid, smem, st);
     case 32: return launch_n<32>(a, bmap, grid, smem, st);

@@ -51,17 +51,30 @@ struct WGemmArgs {
   int epi;
   int accumulate;           // fp32 store only: out += result
   float alpha;
+  // split-K (deterministic): k_splits CTAs share one (item, tile); each writes its fp32 partial
+  // [N x 128] to workspace, bumps counters[item * row_tiles + tile]; the last one sums the partials in split
+  // order, runs the epilogue and resets the counter to zero (so a captured graph can replay).
+  int k_splits;
+  float* workspace;
+  int* counters;
   // pipeline
+  int groups_per_stage;     // 128-column groups per pipeline stage (1, or 2 for token tiles <= 32)
   int w_stage_bytes;
   int w_stages;
   int ab_stages;
   int* err;
   unsigned long long timeout_ns;
+  // diagnostics (FW_WGEMM_DBG): bit 0 = dequant warps skip the math (stage handshakes only),
+  // bit 1 = the MMA issuer skips tcgen05.mma (commits only), bit 2 = no generic->async proxy fence after the
+  // dequant stores, bit 3 = no weight bulk copies (the weight stage barrier is armed with 0 bytes).
+  // Results are garbage when set.
+  int dbg;
 };
 
 int make_tmap_2d_f16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
                      uint32_t box_cols, uint32_t box_rows, bool swizzle128);
-size_t wgemm_smem_bytes(int n_tile, int w_stage_bytes, int w_stages, int ab_stages);
+size_t wgemm_smem_bytes(int n_tile, int g2, int w_stage_bytes, int w_stages, int ab_stages);
+int wgemm_groups_per_stage(int n_tile);
 int wgemm_launch(const WGemmArgs& a, const CUtensorMap& bmap, int grid, cudaStream_t st);
 
 }  // namespace fw

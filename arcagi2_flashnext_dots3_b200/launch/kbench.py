@@ -1,0 +1,160 @@
+"""Kernel microbenchmarks (CUDA-event timed, warm-up, max over repetitions reported as median).
+
+    python -m arcagi2_flashnext_dots3_b200.launch.kbench moe   [--tokens 64] [--experts 320] [--reps 20]
+    python -m arcagi2_flashnext_dots3_b200.launch.kbench dense [--tokens 64] [--reps 20]
+    python -m arcagi2_flashnext_dots3_b200.launch.kbench attn  [--tokens 64] [--ctx 9000] [--reps 20]
+    python -m arcagi2_flashnext_dots3_b200.launch.kbench gdn   [--tokens 64] [--reps 20]
+
+Counterpart of the reference's micro-benchmarks and startup gates (dotsnote/kaggle/runtime_dataset/bench_*.py,
+run_l4.py:435 `run_bench`): each case prints one JSON line with the median device time and the achieved
+bandwidth against the bytes the kernel must move. Inputs are larger than L2 where the case streams weights.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+
+import torch
+
+
+def _time(fn, reps, warm=3):
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    return statistics.median(ts)
+
+
+def bench_moe(args):
+    from ..config import fn_config
+    from ..models.fn_weights import _random_experts
+    from ..ops import fn_ops as ops
+    from ..ops import native, wgemm
+    cfg = fn_config(n_experts=args.experts)
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    gu, d = _random_experts(cfg, g, dev)
+    T, E, k = args.tokens, cfg.n_experts, cfg.top_k
+    logits = torch.randn(T, E + 1, device=dev, generator=g)
+    ids, w = ops.moe_route(logits, E, k)
+    P = T * k
+    n_tile = wgemm.pick_n_tile(max(1, 2 * P // E))
+    max_items = (P + n_tile - 1) // n_tile + E
+    pp, items, n_items = ops.moe_plan(ids, E, n_tile, max_items)
+    x = torch.randn(T, cfg.hidden_size, device=dev, generator=g).half()
+    xs = ops.moe_scatter(x, pp)
+    act = torch.empty(P, cfg.moe_inter, dtype=torch.float16, device=dev)
+    yp = torch.empty(P, cfg.hidden_size, dtype=torch.float32, device=dev)
+    touched = torch.unique(ids).tolist()
+    bytes_gu = sum(gu.row_tiles * gu.kg * (8576 if cfg.bits_of(e) == 4 else 7040) for e in touched)
+    bytes_d = sum(d.row_tiles * d.kg * (8576 if cfg.bits_of(e) == 4 else 7040) for e in touched)
+    t_gu = _time(lambda: wgemm.grouped(xs, gu, items, n_items, max_items, act, epi=wgemm.EPI_SILU_MUL,
+                                       n_tile=n_tile), args.reps)
+    t_d = _time(lambda: wgemm.grouped(act, d, items, n_items, max_items, yp, n_tile=n_tile), args.reps)
+    native.check_error()
+    for name, t, b in (("moe_gate_up", t_gu, bytes_gu), ("moe_down", t_d, bytes_d)):
+        print(json.dumps({"case": name, "tokens": T, "experts": E, "touched": len(touched), "n_tile": n_tile,
+                          "ms": round(t, 4), "MB": round(b / 1e6, 1), "GBps": round(b / t / 1e6, 1)}))
+
+
+def bench_dense(args):
+    from ..ops import native, wgemm
+    dev = torch.device("cuda")
+    T = args.tokens
+    shapes = [("hc_down", 388, 10240), ("hc_up", 10240, 384), ("gdn_proj", 16480, 2560), ("gdn_out", 2560, 6144),
+              ("attn_proj", 11904, 2560), ("attn_o", 2560, 4096), ("router", 321, 2560), ("lm_head", 151936, 2560)]
+    for name, R, K in shapes:
+        wt = torch.randn(R, K, device=dev) * 0.02
+        ws = wgemm.dense_fp8(wt)
+        x = torch.randn(T, K, device=dev).half()
+        out = torch.empty(T, R, device=dev)
+        t = _time(lambda: wgemm.matmul(x, ws, out=out), args.reps)
+        t1 = _time(lambda: wgemm.matmul(x, ws, out=out, k_splits=1), args.reps)
+        b = ws.nbytes()
+        print(json.dumps({"case": name, "rows": R, "K": K, "tokens": T, "ms": round(t, 4), "ms_no_split": round(t1, 4),
+                          "MB": round(b / 1e6, 2), "GBps": round(b / t / 1e6, 1)}))
+    native.check_error()
+
+
+def bench_attn(args):
+    from ..config import fn_config
+    from ..models.fn import allocate_caches
+    from ..ops import fn_ops as ops
+    from ..ops import native
+    cfg = fn_config()
+    dev = torch.device("cuda")
+    B = args.tokens
+    one_attn = fn_config(num_layers=cfg.full_attn_interval)  # exactly one attention layer's caches
+    c = allocate_caches(one_attn, dev, B, args.ctx + 64, block_size=64)
+    nb = c.block_table.shape[1]
+    c.block_table.copy_(torch.arange(B * nb, dtype=torch.int32, device=dev).view(B, nb))
+    for t in (c.k[0], c.v[0]):
+        t.copy_(torch.randn(t.shape, device=dev).to(t.dtype))
+    c.comp[0].copy_(torch.randn(c.comp[0].shape, device=dev).to(c.comp[0].dtype))
+    slots = torch.arange(B, dtype=torch.int32, device=dev)
+    pos = torch.full((B,), args.ctx, dtype=torch.int32, device=dev)
+    q = torch.randn(B, cfg.n_heads, cfg.head_dim, device=dev)
+    gate = torch.randn(B, cfg.n_heads * cfg.head_dim, device=dev)
+    iq = torch.randn(B, cfg.indexer_heads, cfg.indexer_dim, device=dev)
+    sel, sp = ops.qsa_select(iq, c.comp[0], slots, pos, cfg)
+    t_sel = _time(lambda: ops.qsa_select(iq, c.comp[0], slots, pos, cfg), args.reps)
+    t_att = _time(lambda: ops.attn_decode(q, gate, c.k[0], c.v[0], c.block_table, slots, pos, sel, sp, cfg),
+                  args.reps)
+    native.check_error()
+    keys = cfg.indexer_budget + cfg.indexer_ratio
+    kv_bytes = B * cfg.n_kv_heads * keys * cfg.head_dim * 2
+    comp_bytes = B * (args.ctx // cfg.indexer_ratio) * cfg.indexer_dim * 2
+    print(json.dumps({"case": "indexer_select", "rows": B, "ctx": args.ctx, "ms": round(t_sel, 4),
+                      "GBps": round(comp_bytes / t_sel / 1e6, 1)}))
+    print(json.dumps({"case": "sparse_attn_decode", "rows": B, "ctx": args.ctx, "ms": round(t_att, 4),
+                      "GBps": round(kv_bytes / t_att / 1e6, 1)}))
+
+
+def bench_gdn(args):
+    from ..config import fn_config
+    from ..ops import fn_ops as ops
+    from ..ops import native
+    cfg = fn_config()
+    dev = torch.device("cuda")
+    B = args.tokens
+    nk, nv, dk, dv = cfg.lin_k_heads, cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim
+    C = 2 * nk * dk + nv * dv
+    proj = torch.randn(B, C + nv * dv + 2 * nv, device=dev)
+    conv_w = torch.randn(C, cfg.conv_kernel, device=dev) * 0.3
+    conv_state = torch.randn(B, C, cfg.conv_kernel - 1, device=dev)
+    ssm = (torch.randn(B, nv, dk, dv, device=dev) * 0.05).bfloat16()
+    A_log = torch.randn(nv, device=dev)
+    dt = torch.randn(nv, device=dev)
+    nw = torch.randn(dv, device=dev)
+    slots = torch.arange(B, dtype=torch.int32, device=dev)
+    t = _time(lambda: ops.gdn_step(proj, conv_w, conv_state, ssm, A_log, dt, nw, slots, cfg), args.reps)
+    native.check_error()
+    b = 2 * ssm.numel() * 2
+    print(json.dumps({"case": "gdn_decode", "rows": B, "ms": round(t, 4), "state_MB": round(b / 1e6, 1),
+                      "GBps": round(b / t / 1e6, 1)}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["moe", "dense", "attn", "gdn", "all"])
+    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--experts", type=int, default=320)
+    ap.add_argument("--ctx", type=int, default=9000)
+    ap.add_argument("--reps", type=int, default=20)
+    args = ap.parse_args()
+    cases = {"moe": bench_moe, "dense": bench_dense, "attn": bench_attn, "gdn": bench_gdn}
+    for name, fn in cases.items():
+        if args.case in (name, "all"):
+            fn(args)
+
+
+if __name__ == "__main__":
+    main()

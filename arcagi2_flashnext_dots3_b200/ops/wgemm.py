@@ -105,8 +105,21 @@ def pick_n_tile(max_tokens: int) -> int:
     return 128
 
 
+SMALL_WEIGHT_BYTES = 8 << 20
+
+
+def dense_n_tile(T: int, ws: WeightSet) -> int:
+    """Token tile for a dense GEMM. Large weights use the widest tile that covers T (each weight byte is read
+    from HBM once); weights that fit in L2 use 16-token tiles when that is what fills the SMs, since re-reading
+    them per token tile hits L2 and the extra tiles replace split-K partial reductions."""
+    n = pick_n_tile(T)
+    if ws.nbytes() <= SMALL_WEIGHT_BYTES and ws.row_tiles * ((T + n - 1) // n) < 148:
+        return 16
+    return n
+
+
 def matmul(x16: torch.Tensor, ws: WeightSet, out: torch.Tensor = None, epi: int = EPI_STORE,
-           out_dtype=torch.float32, accumulate=False, alpha=1.0, n_tile=None) -> torch.Tensor:
+           out_dtype=torch.float32, accumulate=False, alpha=1.0, n_tile=None, k_splits: int = 0) -> torch.Tensor:
     """Dense y = x @ W^T (or silu(gate)*up for a silu_pairs weight). x16: fp16 [T, K]."""
     T = x16.shape[0]
     cols = ws.rows // 2 if epi == EPI_SILU_MUL else ws.rows
@@ -120,10 +133,10 @@ def matmul(x16: torch.Tensor, ws: WeightSet, out: torch.Tensor = None, epi: int 
         else:
             out.copy_(y.to(out.dtype))
         return out
-    n = n_tile or pick_n_tile(T)
+    n = n_tile or dense_n_tile(T, ws)
     native.C().wgemm(ws.blob, ws.exp_off, ws.exp_fmt, ws.row_tiles, ws.kg, None, None, 0, T, x16, 0, out, 0,
                      cols, epi, accumulate, alpha, n, ws.max_block_bytes, native.err_word(x16.device),
-                     native.DEFAULT_TIMEOUT_NS)
+                     native.DEFAULT_TIMEOUT_NS, k_splits)
     return out
 
 
@@ -140,7 +153,7 @@ def grouped(xs16: torch.Tensor, ws: WeightSet, items: torch.Tensor, n_items: tor
         return out
     native.C().wgemm(ws.blob, ws.exp_off, ws.exp_fmt, ws.row_tiles, ws.kg, items, n_items, max_items, -1, xs16, 0,
                      out, 0, cols, epi, False, 1.0, n_tile, ws.max_block_bytes, native.err_word(xs16.device),
-                     native.DEFAULT_TIMEOUT_NS)
+                     native.DEFAULT_TIMEOUT_NS, 1)
     return out
 
 

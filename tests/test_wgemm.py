@@ -97,3 +97,32 @@ def test_grouped_mixed_bits_silu():
         ref = wgemm._ref_apply(x[t0:t0 + c].float() @ ws.dense(e).cpu().t(), wgemm.EPI_SILU_MUL)
         assert torch.allclose(out[t0:t0 + c].float().cpu(), ref, atol=2e-2, rtol=2e-2)
         t0 += c
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("R,K,T,ks", [(388, 10240, 64, 0), (2560, 6144, 64, 0), (256, 1024, 20, 3), (300, 2560, 1, 0)])
+def test_dense_split_k_deterministic(R, K, T, ks):
+    g = torch.Generator().manual_seed(R + T)
+    w = torch.randn(R, K, generator=g) * 0.02
+    ws = wgemm.dense_fp8(w).to("cuda")
+    x = torch.randn(T, K, generator=g).half()
+    ref = x.float() @ ws.dense(0).cpu().t()
+    y1 = wgemm.matmul(x.cuda(), ws, k_splits=ks)
+    y2 = wgemm.matmul(x.cuda(), ws, k_splits=ks)
+    torch.cuda.synchronize()
+    native.check_error()
+    assert torch.equal(y1, y2), "split-K result is not reproducible"
+    assert torch.allclose(y1.cpu(), ref, atol=3e-3, rtol=3e-3), (y1.cpu() - ref).abs().max()
+
+
+@pytest.mark.gpu
+def test_split_k_silu_epilogue():
+    g = torch.Generator().manual_seed(3)
+    I, K, T = 128, 4096, 9
+    w = torch.randn(2 * I, K, generator=g) * 0.02
+    ws = wgemm.dense_f16(w[rt.gate_up_perm(I)], silu_pairs=True).to("cuda")
+    x = torch.randn(T, K, generator=g).half()
+    ref = wgemm._ref_apply(x.float() @ ws.dense(0).cpu().t(), wgemm.EPI_SILU_MUL)
+    y = wgemm.matmul(x.cuda(), ws, epi=wgemm.EPI_SILU_MUL, out_dtype=torch.float32, k_splits=8)
+    torch.cuda.synchronize()
+    assert torch.allclose(y.cpu(), ref, atol=3e-3, rtol=3e-3)
