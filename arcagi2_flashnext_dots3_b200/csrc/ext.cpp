@@ -85,22 +85,26 @@ void wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, in
   a.dbg = dbg;
 
   static const int ab_env = getenv("FW_WGEMM_AB") ? atoi(getenv("FW_WGEMM_AB")) : 0;
-  int g2 = 1;
-  int ab_stages = n_tile >= 128 ? 2 : (n_tile >= 64 ? 3 : 4);
-  if (ab_env > 0) ab_stages = ab_env;
+  // Pipeline shape: `teams` dequant teams take stages round-robin. Both ring depths must be multiples of the
+  // team count (see the kernel's note on parity waits); pick the most teams that leave >= 2 weight stages.
   const size_t budget = 232448;
-  size_t fixed = fw::wgemm_smem_bytes((int)n_tile, g2, 0, 0, ab_stages) + 8 * 24;
-  if (g2 == 2 && (budget - fixed) / (2 * (size_t)max_block_bytes) < 2) {  // e.g. fp16 weights: one group per stage
-    g2 = 1;
-    ab_stages = 4;
-    fixed = fw::wgemm_smem_bytes((int)n_tile, g2, 0, 0, ab_stages) + 8 * 24;
+  int teams = 0, ab_stages = 0, w_stages = 0;
+  for (int t = fw::kWgemmMaxTeams; t >= 1 && !teams; --t) {
+    int P = ab_env > 0 ? ab_env : t;
+    if (P % t) continue;
+    const size_t fixed = fw::wgemm_smem_bytes((int)n_tile, 1, 0, 0, P) + 8 * 32;
+    if (fixed >= budget) continue;
+    int S = (int)std::min<size_t>(12, (budget - fixed) / (size_t)max_block_bytes);
+    S -= S % t;
+    if (S < 2) continue;
+    teams = t;
+    ab_stages = P;
+    w_stages = S;
   }
-  a.groups_per_stage = g2;
-  const size_t w_stage_bytes = (size_t)g2 * max_block_bytes;
-  int w_stages = (int)((budget - fixed) / w_stage_bytes);
-  w_stages = std::min(w_stages, 12);
-  TORCH_CHECK(w_stages >= 2, "not enough shared memory for two weight stages");
-  a.w_stage_bytes = (int)w_stage_bytes;
+  TORCH_CHECK(teams > 0, "no pipeline configuration fits in shared memory");
+  a.groups_per_stage = 1;
+  a.teams = teams;
+  a.w_stage_bytes = (int)max_block_bytes;
   a.w_stages = w_stages;
   a.ab_stages = ab_stages;
 

@@ -68,9 +68,9 @@ __device__ __forceinline__ void stf<__nv_fp8_e4m3>(__nv_fp8_e4m3* p, float v) { 
 
 // ============================================================================================ embedding
 template <typename IT>
-__global__ void embed_hc_kernel(const IT* ids, const __nv_bfloat16* table, float* out, int H, int hc) {
+__global__ void embed_hc_kernel(const IT* ids, const __nv_bfloat16* table, float* out, int H, int hc, int64_t V) {
   const int t = blockIdx.x;
-  const int64_t id = (int64_t)ids[t];
+  const int64_t id = min(max((int64_t)ids[t], (int64_t)0), V - 1);  // out-of-range ids never index past the table
   const __nv_bfloat16* row = table + id * H;
   float* o = out + (int64_t)t * hc * H;
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
@@ -86,10 +86,10 @@ void embed_hc(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t
   if (!T) return;
   if (ids.scalar_type() == torch::kInt64)
     embed_hc_kernel<<<T, 256, 0, STREAM>>>(ids.data_ptr<int64_t>(), (const __nv_bfloat16*)table.data_ptr(),
-                                           out.data_ptr<float>(), H, hc);
+                                           out.data_ptr<float>(), H, hc, table.size(0));
   else
     embed_hc_kernel<<<T, 256, 0, STREAM>>>(ids.data_ptr<int32_t>(), (const __nv_bfloat16*)table.data_ptr(),
-                                           out.data_ptr<float>(), H, hc);
+                                           out.data_ptr<float>(), H, hc, table.size(0));
 }
 
 // ===================================================================================== hyper-connections
@@ -803,7 +803,8 @@ __global__ void moe_route_kernel(const float* logits, int ld, int32_t* ids, floa
   __syncthreads();
   float sum = 0.f;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    const float v = __expf(x[e] - mx);
+    float v = __expf(x[e] - mx);
+    if (!(v >= 0.f)) v = 0.f;  // NaN logits must still yield valid expert ids below
     pr[e] = v;
     sum += v;
   }
@@ -873,7 +874,8 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(const int32_t* ids, int 
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   for (int e = threadIdx.x; e < E; e += blockDim.x) count[e] = 0;
   __syncthreads();
-  for (int i = threadIdx.x; i < P; i += blockDim.x) atomicAdd(&count[ids[i]], 1);
+  // expert ids are clamped into [0, E): a bad id can only misroute a token, never index out of bounds
+  for (int i = threadIdx.x; i < P; i += blockDim.x) atomicAdd(&count[min(max(ids[i], 0), E - 1)], 1);
   __syncthreads();
   if (threadIdx.x == 0) {
     int acc = 0, it = 0;
@@ -891,7 +893,7 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(const int32_t* ids, int 
   // running per-expert offset in start[]; chunks of 1024 pairs keep the flat order stable
   for (int base = 0; base < P; base += blockDim.x) {
     const int i = base + threadIdx.x;
-    const int e = i < P ? ids[i] : -1;
+    const int e = i < P ? min(max(ids[i], 0), E - 1) : -1;
     for (int q = threadIdx.x; q < 32 * E; q += blockDim.x) wcnt[q] = 0;
     __syncthreads();
     const unsigned same = __match_any_sync(0xffffffffu, e);

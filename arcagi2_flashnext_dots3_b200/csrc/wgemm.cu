@@ -14,8 +14,9 @@
 //   warp 0      TMA: 1-D bulk copies of the packed weight block of each 128-column group into a smem ring
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma (8 x K16 per group) into TMEM
 //   warp 2      TMA: 2-D tiled loads of the token tile (fp16, SWIZZLE_128B) + TMEM allocation
-//   warps 4-11  dequant: packed codes -> fp16 s*(q-z) in registers -> SWIZZLE_128B smem A tile
-//   warps 12-15 epilogue: tcgen05.ld of the double-buffered accumulator, store or silu(gate)*up
+//   warps 4-15  dequant: packed codes -> fp16 s*(q-z) in registers -> SWIZZLE_128B smem A tile (3 teams of
+//               4 warps on alternating stages; a thread converts one row of its team's 128-column group)
+//   warps 16-19 epilogue: tcgen05.ld of the double-buffered accumulator, store or silu(gate)*up
 // Every mbarrier wait is bounded (%globaltimer); a timeout records an error code and all roles drain out.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -28,9 +29,12 @@
 
 namespace fw {
 
-constexpr int kThreads = 512;
-constexpr int kDqThreads = 256;
-constexpr int kEpiThreads = 128;
+constexpr int kTeams = 3;                         // dequant teams of 4 warps (maximum), alternating stages
+constexpr int kDqThreads = 128 * kTeams;          // warps 4 .. 4 + 4 * kTeams - 1
+constexpr int kEpiThreads = 128;                  // the last 4 warps
+constexpr int kEpiWarp0 = 4 + 4 * kTeams;
+constexpr int kEpiFirst = 32 * kEpiWarp0;
+constexpr int kThreads = kEpiFirst + kEpiThreads;
 
 struct WGemmSmem {
   // offsets relative to the 1024-aligned dynamic smem base
@@ -275,11 +279,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(bar_w_full + 8 * s, 1);
-      mbar_init(bar_w_empty + 8 * s, kDqThreads / 32);
+      mbar_init(bar_w_empty + 8 * s, 4);  // one dequant team (4 warps) per stage
     }
     for (int p = 0; p < P; ++p) {
       mbar_init(bar_b_full + 8 * p, 1);
-      mbar_init(bar_a_ready + 8 * p, kDqThreads / 32);
+      mbar_init(bar_a_ready + 8 * p, 4);
       mbar_init(bar_ab_empty + 8 * p, 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -395,16 +399,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       volatile int no_abort = 0;
       mbar_wait(bar_done, 0, err, 3004, &no_abort, lim);
     }
-  } else if (warp >= 4 && warp < 12) {
-    // ---------------------------------------------------------------- dequant (256 threads)
+  } else if (warp >= 4 && warp < kEpiWarp0) {
+    // ---------------------------------------------------------------- dequant (kTeams x 128 threads)
+    // kTeams teams of 4 warps take stages round-robin, each thread converting one full row of its team's
+    // group, so kTeams groups are converted concurrently: a group's latency chain (wait, convert,
+    // signal) is per warp, and with every warp on every group that chain bounded the group rate.
+    // Safety of the parity waits: a team may start waiting for use u of a stage only if use u-1 of that stage
+    // was its own (parity waits cannot tell use u-1 from u+1); the host makes both ring depths multiples of
+    // a.teams, so stage j % P and j % S always recur on the same team (j % a.teams).
     const int d = threadIdx.x - 128;
-    const int r = d & 127, h = d >> 7;
+    const int r = d & 127, team = d >> 7;
+    const int teams = a.teams;
     uint32_t k = 0, j = 0;
-    for (int w = blockIdx.x; w < total && !*abort_flag; w += gridDim.x) {
+    for (int w = blockIdx.x; w < total && !*abort_flag && team < teams; w += gridDim.x) {
       const Work wk = decode_work(a, w, KS);
       const int fmt = a.exp_fmt[wk.e];
       bool ok = true;
       for (int g = wk.g0; g < wk.g1; ++g, ++k, ++j) {
+        if ((int)(j % teams) != team) continue;
         const int s = k % S, p = j % P;
         if (!mbar_wait(bar_w_full + 8 * s, (k / S) & 1, err, 4001, abort_flag, lim) ||
             !mbar_wait(bar_ab_empty + 8 * p, ((j / P) & 1) ^ 1, err, 4002, abort_flag, lim)) {
@@ -415,11 +427,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t as = base + p * ab_stage;
         if (!(a.dbg & 1)) {
           switch (fmt) {
-            case 4: dequant_block<4>(wb, r, h, as); break;
-            case 3: dequant_block<3>(wb, r, h, as); break;
-            case 2: dequant_block<2>(wb, r, h, as); break;
-            case 8: dequant_block<8>(wb, r, h, as); break;
-            default: dequant_block<16>(wb, r, h, as); break;
+            case 4: dequant_block<4>(wb, r, 0, as); dequant_block<4>(wb, r, 1, as); break;
+            case 3: dequant_block<3>(wb, r, 0, as); dequant_block<3>(wb, r, 1, as); break;
+            case 2: dequant_block<2>(wb, r, 0, as); dequant_block<2>(wb, r, 1, as); break;
+            case 8: dequant_block<8>(wb, r, 0, as); dequant_block<8>(wb, r, 1, as); break;
+            default: dequant_block<16>(wb, r, 0, as); dequant_block<16>(wb, r, 1, as); break;
           }
         }
         if (!(a.dbg & 4)) fence_proxy_async_smem();
@@ -431,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
     }
-  } else if (warp >= 12) {
+  } else if (warp >= kEpiWarp0) {
     // ---------------------------------------------------------------- epilogue (128 threads)
     const int q = warp & 3;
     const int row = q * 32 + lane;
@@ -460,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __threadfence();
         named_barrier(1, kEpiThreads);
-        if (threadIdx.x == 384) {
+        if (threadIdx.x == kEpiFirst) {
           const int old = atomicAdd(a.counters + tile_id, 1);
           const int last = old == KS - 1;
           if (last) a.counters[tile_id] = 0;

@@ -58,7 +58,8 @@ struct WGemmArgs {
   float* workspace;
   int* counters;
   // pipeline
-  int groups_per_stage;     // 128-column groups per pipeline stage (1, or 2 for token tiles <= 32)
+  int groups_per_stage;     // 128-column groups per pipeline stage (always 1 in this version)
+  int teams;                // active dequant teams (<= 3); w_stages and ab_stages are multiples of it
   int w_stage_bytes;
   int w_stages;
   int ab_stages;
@@ -75,6 +76,7 @@ int make_tmap_2d_f16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t 
                      uint32_t box_cols, uint32_t box_rows, bool swizzle128);
 size_t wgemm_smem_bytes(int n_tile, int g2, int w_stage_bytes, int w_stages, int ab_stages);
 int wgemm_groups_per_stage(int n_tile);
+constexpr int kWgemmMaxTeams = 3;
 int wgemm_launch(const WGemmArgs& a, const CUtensorMap& bmap, int grid, cudaStream_t st);
 
 }  // namespace fw
