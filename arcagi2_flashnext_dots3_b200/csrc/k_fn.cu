@@ -14,6 +14,7 @@
 #include <cuda_fp8.h>
 #include <cfloat>
 #include <atomic>
+#include <cub/block/block_scan.cuh>
 #include "kernels.h"
 
 namespace {
@@ -65,6 +66,36 @@ template <>
 __device__ __forceinline__ void stf<__half>(__half* p, float v) { *p = __float2half_rn(v); }
 template <>
 __device__ __forceinline__ void stf<__nv_fp8_e4m3>(__nv_fp8_e4m3* p, float v) { *p = __nv_fp8_e4m3(v); }
+
+// 8 consecutive cache elements -> fp32.
+__device__ __forceinline__ void load8f(const __nv_fp8_e4m3* p, float (&o)[8]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const uint32_t w[2] = {u.x, u.y};
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const __half2_raw h2 = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)((w[j] >> (16 * hh)) & 0xFFFF), __NV_E4M3);
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+      o[4 * j + 2 * hh] = f.x;
+      o[4 * j + 2 * hh + 1] = f.y;
+    }
+  }
+}
+__device__ __forceinline__ void load8f(const __nv_bfloat16* p, float (&o)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(b[i]);
+    o[2 * i] = f.x;
+    o[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void load8f(const float* p, float (&o)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
 
 // ============================================================================================ embedding
 template <typename IT>
@@ -458,34 +489,43 @@ void qsa_prep(torch::Tensor proj, torch::Tensor qn, torch::Tensor kn, torch::Ten
 }
 
 // Indexer scores s[row, blk] = sum_h relu(iq[row,h] . comp[blk]) / sqrt(iD) for complete blocks, -inf beyond.
-// grid (rows, chunks of 256 blocks); 256 threads, one block key per thread.
-template <typename CT>
-__global__ void qsa_scores_kernel(const float* iq, const CT* comp, int max_comp, const int* slots,
-                                  const int* positions, float* scores, int ld_scores, int iH, int iD, int r,
-                                  int n_tok) {
-  extern __shared__ float qs[];  // [iH][iD]
+// grid (rows, chunks of 256 blocks); 256 threads, one block key per thread; IH = index heads (accumulators in
+// registers), the key row read 8 elements at a time, the query broadcast from shared memory.
+template <typename CT, int IH>
+__global__ void __launch_bounds__(256) qsa_scores_kernel(const float* iq, const CT* comp, int max_comp,
+                                                         const int* slots, const int* positions, float* scores,
+                                                         int ld_scores, int iD, int r, int n_tok) {
+  extern __shared__ float qs[];  // [IH][iD]
   const int row = blockIdx.x;
   const int b = row / n_tok;
   const int p = positions[b] + row % n_tok;
   const int nc = (p + 1) / r;
   const int blk = blockIdx.y * blockDim.x + threadIdx.x;
   if (blockIdx.y * blockDim.x >= nc) return;
-  for (int i = threadIdx.x; i < iH * iD; i += blockDim.x) qs[i] = iq[(int64_t)row * iH * iD + i];
+  for (int i = threadIdx.x; i < IH * iD; i += blockDim.x) qs[i] = iq[(int64_t)row * IH * iD + i];
   __syncthreads();
   if (blk >= ld_scores) return;
   float out = -FLT_MAX;
   if (blk < nc && blk < max_comp) {
     const CT* kb = comp + ((int64_t)slots[b] * max_comp + blk) * iD;
-    float acc[32];
-    const int nh = min(iH, 32);
-    for (int h = 0; h < nh; ++h) acc[h] = 0.f;
-    for (int d = 0; d < iD; ++d) {
-      const float kv = ldf(&kb[d]);
-      for (int h = 0; h < nh; ++h) acc[h] += qs[h * iD + d] * kv;
+    float acc[IH];
+#pragma unroll
+    for (int h = 0; h < IH; ++h) acc[h] = 0.f;
+    for (int d0 = 0; d0 < iD; d0 += 8) {
+      float kf[8];
+      load8f(kb + d0, kf);
+#pragma unroll
+      for (int h = 0; h < IH; ++h) {
+        const float4 qa = *reinterpret_cast<const float4*>(qs + h * iD + d0);
+        const float4 qb = *reinterpret_cast<const float4*>(qs + h * iD + d0 + 4);
+        acc[h] += qa.x * kf[0] + qa.y * kf[1] + qa.z * kf[2] + qa.w * kf[3] + qb.x * kf[4] + qb.y * kf[5] +
+                  qb.z * kf[6] + qb.w * kf[7];
+      }
     }
-    float s = 0.f;
-    for (int h = 0; h < nh; ++h) s += fmaxf(acc[h], 0.f);
-    out = s * rsqrtf((float)iD);
+    float sum = 0.f;
+#pragma unroll
+    for (int h = 0; h < IH; ++h) sum += fmaxf(acc[h], 0.f);
+    out = sum * rsqrtf((float)iD);
   }
   scores[(int64_t)row * ld_scores + blk] = out;
 }
@@ -585,24 +625,46 @@ __global__ void topk_rows_kernel(const float* scores, int ld, const int* n_valid
   }
 }
 
+template <int IH>
+void launch_scores_ih(const float* iq, const void* comp, bool bf16, int max_comp, const int* slots, const int* pos,
+                      float* scores, int ld, int rows, int chunks, int iD, int r, int n_tok, cudaStream_t st) {
+  const size_t sm = (size_t)IH * iD * sizeof(float);
+  if (bf16)
+    qsa_scores_kernel<__nv_bfloat16, IH><<<dim3(rows, chunks), 256, sm, st>>>(
+        iq, static_cast<const __nv_bfloat16*>(comp), max_comp, slots, pos, scores, ld, iD, r, n_tok);
+  else
+    qsa_scores_kernel<float, IH><<<dim3(rows, chunks), 256, sm, st>>>(iq, static_cast<const float*>(comp), max_comp,
+                                                                      slots, pos, scores, ld, iD, r, n_tok);
+}
+
+// Index-head counts with compiled kernels (FN: 20; tests: 2, 4; Dots3: 64).
+bool launch_scores(const float* iq, const void* comp, bool bf16, int max_comp, const int* slots, const int* pos,
+                   float* scores, int ld, int rows, int chunks, int iH, int iD, int r, int n_tok, cudaStream_t st) {
+  switch (iH) {
+    case 1: launch_scores_ih<1>(iq, comp, bf16, max_comp, slots, pos, scores, ld, rows, chunks, iD, r, n_tok, st); return true;
+    case 2: launch_scores_ih<2>(iq, comp, bf16, max_comp, slots, pos, scores, ld, rows, chunks, iD, r, n_tok, st); return true;
+    case 4: launch_scores_ih<4>(iq, comp, bf16, max_comp, slots, pos, scores, ld, rows, chunks, iD, r, n_tok, st); return true;
+    case 8: launch_scores_ih<8>(iq, comp, bf16, max_comp, slots, pos, scores, ld, rows, chunks, iD, r, n_tok, st); return true;
+    case 16: launch_scores_ih<16>(iq, comp, bf16, max_comp, slots, pos, scores, ld, rows, chunks, iD, r, n_tok, st); return true;
+    case 20: launch_scores_ih<20>(iq, comp, bf16, max_comp, slots, pos, scores, ld, rows, chunks, iD, r, n_tok, st); return true;
+    case 32: launch_scores_ih<32>(iq, comp, bf16, max_comp, slots, pos, scores, ld, rows, chunks, iD, r, n_tok, st); return true;
+    default: return false;
+  }
+}
+
 void qsa_select(torch::Tensor iq, torch::Tensor comp, torch::Tensor slots, torch::Tensor positions, torch::Tensor sel,
                 torch::Tensor sparse, int64_t nblk, int64_t r, int64_t n_tok) {
   const int rows = iq.size(0);
   if (!rows) return;
   const int iH = iq.size(1), iD = iq.size(2);
-  CK(iH <= 32);
+  CK(iH == 1 || iH == 2 || iH == 4 || iH == 8 || iH == 16 || iH == 20 || iH == 32);
   const int max_comp = comp.size(1);
   const int chunks = (max_comp + 255) / 256;
   auto scores = torch::empty({rows, chunks * 256}, iq.options());
-  const size_t sm = iH * iD * sizeof(float);
-  if (comp.scalar_type() == torch::kBFloat16)
-    qsa_scores_kernel<__nv_bfloat16><<<dim3(rows, chunks), 256, sm, STREAM>>>(
-        iq.data_ptr<float>(), (const __nv_bfloat16*)comp.data_ptr(), max_comp, slots.data_ptr<int32_t>(),
-        positions.data_ptr<int32_t>(), scores.data_ptr<float>(), chunks * 256, iH, iD, r, n_tok);
-  else
-    qsa_scores_kernel<float><<<dim3(rows, chunks), 256, sm, STREAM>>>(
-        iq.data_ptr<float>(), comp.data_ptr<float>(), max_comp, slots.data_ptr<int32_t>(),
-        positions.data_ptr<int32_t>(), scores.data_ptr<float>(), chunks * 256, iH, iD, r, n_tok);
+  CK(iD % 8 == 0);
+  launch_scores(iq.data_ptr<float>(), comp.data_ptr(), comp.scalar_type() == torch::kBFloat16, max_comp,
+                slots.data_ptr<int32_t>(), positions.data_ptr<int32_t>(), scores.data_ptr<float>(), chunks * 256, rows,
+                chunks, iH, iD, r, n_tok, STREAM);
   topk_rows_kernel<<<rows, 512, 0, STREAM>>>(scores.data_ptr<float>(), chunks * 256, nullptr, 0, nblk,
                                              sel.data_ptr<int32_t>(), sparse.data_ptr<int32_t>(),
                                              positions.data_ptr<int32_t>(), r, n_tok);
@@ -617,20 +679,21 @@ void topk_rows(torch::Tensor scores, torch::Tensor n_valid, int64_t k, torch::Te
                                              k, sel.data_ptr<int32_t>(), nullptr, nullptr, 1, 1);
 }
 
-// Split-K sparse GQA decode attention. Block = (row, kv head, split), 256 threads = 8 warps; G = Hq/KV <= 8 query
-// heads share the kv head. Keys are visited in chunks of 32: thread (h = tid/32, key = lane) scores, warp h does
-// the online softmax of head h, then thread (h, lane) accumulates dims lane + 32*i of head h.
+// Split-K sparse GQA decode attention on CUDA cores. Block = (row, kv head, split), 4 warps; the G <= 8 query
+// heads of the kv head share every loaded key. Per chunk of 32 keys a warp: each lane scores its own key
+// against all G heads (q broadcast from shared memory, the key row read 8 elements at a time), the warp runs
+// the online softmax of every head with shuffles, then each lane accumulates P.V for its D/32 dims. The four
+// warps' (m, l, acc) are merged in shared memory and written as this split's partial.
 template <typename KT, int D>
-__global__ void __launch_bounds__(256) attn_split_kernel(const float* q, const KT* kc, const KT* vc,
+__global__ void __launch_bounds__(128) attn_split_kernel(const float* q, const KT* kc, const KT* vc,
                                                          const int* block_table, int max_blocks, int bs,
                                                          const int* slots, const int* positions, const int* sel,
                                                          const int* sparse, int nblk, int r, int KV, int G, int n_tok,
                                                          int n_split, float* part_o, float* part_ml) {
   constexpr int NI = D / 32;
   extern __shared__ float sm[];
-  float* qs = sm;                    // [G][D]
-  float* ks = qs + 8 * D;            // [32][D+1]
-  float* vs = ks + 32 * (D + 1);     // [32][D]
+  float* qs = sm;                       // [8][D]
+  float* mrg = qs + 8 * D;              // [4 warps][8 heads][D + 2]
   const int row = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int b = row / n_tok;
   const int p = positions[b] + row % n_tok;
@@ -642,71 +705,118 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* q, const K
   const int n_keys = is_sparse ? nblk * r + (p + 1 - tail0) : p + 1;
   const int per = (n_keys + n_split - 1) / n_split;
   const int k0 = split * per, k1 = min(n_keys, k0 + per);
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) qs[i] = q[((int64_t)row * Hq + kvh * G) * D + i];
-  float m = -FLT_MAX, l = 0.f;
-  float acc[NI];
-#pragma unroll
-  for (int i = 0; i < NI; ++i) acc[i] = 0.f;
+  for (int i = threadIdx.x; i < 8 * D; i += blockDim.x)
+    qs[i] = i < G * D ? q[((int64_t)row * Hq + kvh * G) * D + i] : 0.f;
+  __syncthreads();
   const float scale = rsqrtf((float)D);
-  for (int c0 = k0; c0 < k1; c0 += 32) {
-    __syncthreads();
-    // load 32 keys (token ids resolved through the selection and the block table)
-    for (int kk = warp; kk < 32; kk += 8) {
-      const int m_idx = c0 + kk;
-      int tok = -1;
-      if (m_idx < k1) {
-        if (is_sparse) {
-          tok = m_idx < nblk * r ? sel[(int64_t)row * nblk + m_idx / r] * r + m_idx % r : tail0 + (m_idx - nblk * r);
-        } else {
-          tok = m_idx;
-        }
-      }
-      if (tok >= 0) {
-        const int blk = block_table[(int64_t)s * max_blocks + tok / bs];
-        const int64_t off = (((int64_t)blk * bs + tok % bs) * KV + kvh) * D;
-        for (int d = lane; d < D; d += 32) {
-          ks[kk * (D + 1) + d] = ldf(&kc[off + d]);
-          vs[kk * D + d] = ldf(&vc[off + d]);
-        }
-      } else {
-        for (int d = lane; d < D; d += 32) {
-          ks[kk * (D + 1) + d] = 0.f;
-          vs[kk * D + d] = 0.f;
+  float m[8], l[8], acc[8][NI];
+#pragma unroll
+  for (int h = 0; h < 8; ++h) {
+    m[h] = -FLT_MAX;
+    l[h] = 0.f;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) acc[h][i] = 0.f;
+  }
+  for (int c0 = k0 + warp * 32; c0 < k1; c0 += 128) {
+    const int mk = c0 + lane;
+    const bool valid = mk < k1;
+    int64_t off = 0;
+    if (valid) {
+      int tok = mk;
+      if (is_sparse) tok = mk < nblk * r ? sel[(int64_t)row * nblk + mk / r] * r + mk % r : tail0 + (mk - nblk * r);
+      const int blk = block_table[(int64_t)s * max_blocks + tok / bs];
+      off = (((int64_t)blk * bs + tok % bs) * KV + kvh) * D;
+    }
+    float sc[8];
+#pragma unroll
+    for (int h = 0; h < 8; ++h) sc[h] = 0.f;
+    if (valid) {
+#pragma unroll 4
+      for (int d0 = 0; d0 < D; d0 += 8) {
+        float kf[8];
+        load8f(kc + off + d0, kf);
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          const float4 qa = *reinterpret_cast<const float4*>(qs + h * D + d0);
+          const float4 qb = *reinterpret_cast<const float4*>(qs + h * D + d0 + 4);
+          sc[h] += qa.x * kf[0] + qa.y * kf[1] + qa.z * kf[2] + qa.w * kf[3] + qb.x * kf[4] + qb.y * kf[5] +
+                   qb.z * kf[6] + qb.w * kf[7];
         }
       }
     }
-    __syncthreads();
-    if (warp < G) {
-      const float* qh = qs + warp * D;
-      const float* kr = ks + lane * (D + 1);
-      float sc = 0.f;
-#pragma unroll 8
-      for (int d = 0; d < D; ++d) sc += qh[d] * kr[d];
-      sc = (c0 + lane < k1) ? sc * scale : -FLT_MAX;
-      const float cm = warp_max(sc);
-      const float mn = fmaxf(m, cm);
-      const float pe = (c0 + lane < k1) ? __expf(sc - mn) : 0.f;
-      const float corr = __expf(m - mn);
-      l = l * corr + warp_sum(pe);
-      m = mn;
+    float pr[8];
 #pragma unroll
-      for (int i = 0; i < NI; ++i) acc[i] *= corr;
-      for (int kk = 0; kk < 32; ++kk) {
-        const float pk = __shfl_sync(0xffffffffu, pe, kk);
-        if (c0 + kk >= k1) break;
+    for (int h = 0; h < 8; ++h) {
+      const float sh = valid ? sc[h] * scale : -FLT_MAX;
+      const float mn = fmaxf(m[h], warp_max(sh));
+      pr[h] = valid ? __expf(sh - mn) : 0.f;
+      const float corr = __expf(m[h] - mn);
+      l[h] = l[h] * corr + warp_sum(pr[h]);
+      m[h] = mn;
 #pragma unroll
-        for (int i = 0; i < NI; ++i) acc[i] += pk * vs[kk * D + lane + 32 * i];
+      for (int i = 0; i < NI; ++i) acc[h][i] *= corr;
+    }
+    // P.V, 8 keys at a time: the 8 value rows are loaded before any is used, so their latencies overlap
+    const int n_here = min(32, k1 - c0);
+    for (int k8 = 0; k8 < n_here; k8 += 8) {
+      float vf[8][NI];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int kk = k8 + u;
+        const int64_t ok = __shfl_sync(0xffffffffu, off, kk & 31);
+        if (kk < n_here) {
+          if constexpr (NI == 8) {
+            load8f(vc + ok + lane * 8, vf[u]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < NI; ++i) vf[u][i] = ldf(&vc[ok + lane * NI + i]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < NI; ++i) vf[u][i] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          const float pk = __shfl_sync(0xffffffffu, pr[h], (k8 + u) & 31);
+#pragma unroll
+          for (int i = 0; i < NI; ++i) acc[h][i] += pk * vf[u][i];
+        }
       }
     }
   }
-  if (warp < G) {
-    const int h = kvh * G + warp;
-    const int64_t base = ((int64_t)row * Hq + h) * n_split + split;
+  // merge the 4 warps
+  float* mw = mrg + warp * 8 * (D + 2);
 #pragma unroll
-    for (int i = 0; i < NI; ++i) part_o[base * D + lane + 32 * i] = acc[i];
+  for (int h = 0; h < 8; ++h) {
+#pragma unroll
+    for (int i = 0; i < NI; ++i) mw[h * (D + 2) + lane * NI + i] = acc[h][i];
     if (lane == 0) {
-      part_ml[base * 2] = m;
-      part_ml[base * 2 + 1] = l;
+      mw[h * (D + 2) + D] = m[h];
+      mw[h * (D + 2) + D + 1] = l[h];
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int h = idx / D, d = idx % D;
+    float M = -FLT_MAX;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, mrg[(w * 8 + h) * (D + 2) + D]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float* mh = mrg + (w * 8 + h) * (D + 2);
+      const float f = mh[D] > -FLT_MAX ? __expf(mh[D] - M) : 0.f;
+      L += mh[D + 1] * f;
+      O += mh[d] * f;
+    }
+    const int64_t base = ((int64_t)row * Hq + kvh * G + h) * n_split + split;
+    part_o[base * D + d] = O;
+    if (d == 0) {
+      part_ml[base * 2] = M;
+      part_ml[base * 2 + 1] = L;
     }
   }
 }
@@ -745,16 +855,16 @@ void attn_decode(torch::Tensor q, torch::Tensor gate, torch::Tensor k_cache, tor
   CK(D == 64 || D == 128 || D == 256);
   const int nblk = sel.size(1);
   // enough blocks for the machine: rows * KV * split >= ~2 waves
-  int n_split = std::max(1, std::min(16, (int)((2 * 148 + rows * KV - 1) / (rows * KV))));
+  int n_split = std::max(1, std::min(32, (int)((4 * 148 + rows * KV - 1) / (rows * KV))));
   auto part_o = torch::empty({rows, Hq, n_split, D}, q.options());
   auto part_ml = torch::empty({rows, Hq, n_split, 2}, q.options());
-  const size_t sm = (8 * D + 32 * (D + 1) + 32 * D) * sizeof(float);
+  const size_t sm = (8 * D + 4 * 8 * (D + 2)) * sizeof(float);
   dim3 grid(rows, KV, n_split);
 #define ATT(KT, DD)                                                                                                 \
   {                                                                                                                 \
     auto kern = attn_split_kernel<KT, DD>;                                                                         \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);                             \
-    kern<<<grid, 256, sm, STREAM>>>(q.data_ptr<float>(), (const KT*)k_cache.data_ptr(), (const KT*)v_cache.data_ptr(), \
+    kern<<<grid, 128, sm, STREAM>>>(q.data_ptr<float>(), (const KT*)k_cache.data_ptr(), (const KT*)v_cache.data_ptr(), \
                                     block_table.data_ptr<int32_t>(), block_table.size(1), k_cache.size(1),          \
                                     slots.data_ptr<int32_t>(), positions.data_ptr<int32_t>(), sel.data_ptr<int32_t>(), \
                                     sparse.data_ptr<int32_t>(), nblk, r, KV, G, n_tok, n_split,                    \
@@ -877,17 +987,23 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(const int32_t* ids, int 
   // expert ids are clamped into [0, E): a bad id can only misroute a token, never index out of bounds
   for (int i = threadIdx.x; i < P; i += blockDim.x) atomicAdd(&count[min(max(ids[i], 0), E - 1)], 1);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0, it = 0;
-    for (int e = 0; e < E; ++e) {
-      start[e] = acc;
-      for (int s0 = 0; s0 < count[e]; s0 += n_tile) {
-        if (it < max_items) items[it] = make_int4(e, acc + s0, min(n_tile, count[e] - s0), 0);
-        ++it;
-      }
-      acc += count[e];
+  {
+    // thread e owns expert e (E <= 1024): exclusive scans give its first row and its first item
+    using Scan = cub::BlockScan<int, 1024>;
+    __shared__ typename Scan::TempStorage scan_tmp;
+    const int e = threadIdx.x;
+    const int c = e < E ? count[e] : 0;
+    const int nch = (c + n_tile - 1) / n_tile;
+    int row0, item0, total_items;
+    Scan(scan_tmp).ExclusiveSum(c, row0);
+    __syncthreads();
+    Scan(scan_tmp).ExclusiveSum(nch, item0, total_items);
+    if (e < E) {
+      start[e] = row0;
+      for (int q = 0; q < nch; ++q)
+        if (item0 + q < max_items) items[item0 + q] = make_int4(e, row0 + q * n_tile, min(n_tile, c - q * n_tile), 0);
     }
-    *n_items = min(it, max_items);
+    if (threadIdx.x == 0) *n_items = min(total_items, max_items);
   }
   __syncthreads();
   // running per-expert offset in start[]; chunks of 1024 pairs keep the flat order stable
@@ -919,7 +1035,7 @@ void moe_plan(torch::Tensor ids, torch::Tensor pair_pos, torch::Tensor items, to
               int64_t n_tile) {
   const int P = ids.numel();
   const size_t sm = (2 * E + 32 * E) * sizeof(int);
-  CK(sm <= 200 * 1024);
+  CK(E <= 1024 && sm <= 200 * 1024);
   auto kern = moe_plan_kernel;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   kern<<<1, 1024, sm, STREAM>>>(ids.data_ptr<int32_t>(), P, pair_pos.data_ptr<int32_t>(),
@@ -1087,12 +1203,9 @@ extern "C" __attribute__((visibility("default"))) int fw_qsa_select_noalloc(
     g_noalloc_ptr[dev].store(scores);
   }
   const int ld = chunks * 256;
-  if (comp_bf16)
-    qsa_scores_kernel<__nv_bfloat16><<<dim3(rows, chunks), 256, smem, stream>>>(
-        iq, static_cast<const __nv_bfloat16*>(comp), max_comp, slots, positions, scores, ld, iH, iD, r, n_tok);
-  else
-    qsa_scores_kernel<float><<<dim3(rows, chunks), 256, smem, stream>>>(
-        iq, static_cast<const float*>(comp), max_comp, slots, positions, scores, ld, iH, iD, r, n_tok);
+  if (iD % 8 || !launch_scores(iq, comp, comp_bf16 != 0, max_comp, slots, positions, scores, ld, rows, chunks, iH, iD,
+                               r, n_tok, stream))
+    return FW_NOALLOC_INVALID;
   topk_rows_kernel<<<rows, 512, 0, stream>>>(scores, ld, nullptr, 0, nblk, sel, sparse, positions, r, n_tok);
   e = cudaGetLastError();
   return e == cudaSuccess ? FW_NOALLOC_OK : 1000 + (int)e;

@@ -54,8 +54,7 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
-// try_wait with a suspend-time hint: a waiting thread is parked (no issue slots) until the phase completes or
-// about 0.5 ms pass, so spinning roles do not steal issue bandwidth from the compute warps.
+// One poll of phase `parity` (no suspend-time hint: the latency-critical roles poll tightly).
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -83,6 +82,32 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
         *abort_flag = 1;
         return false;
       }
+    }
+  }
+}
+
+// Bounded wait for roles off the critical path (producers, epilogue): try_wait with a suspend-time hint parks
+// the thread until the phase completes (or ~20 us pass), so its polling does not take issue slots from the
+// dequant and MMA warps.
+__device__ __forceinline__ bool mbar_wait_sleepy(uint32_t bar, uint32_t parity, int* err, int code,
+                                                 volatile int* abort_flag, uint64_t limit_ns) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(20000u)
+        : "memory");
+    if (ok) return true;
+    if (*abort_flag) return false;
+    const uint64_t now = globaltimer_ns();
+    if (t0 == 0) {
+      t0 = now;
+    } else if (now - t0 > limit_ns) {
+      atomicCAS(err, 0, code);
+      *abort_flag = 1;
+      return false;
     }
   }
 }

@@ -52,6 +52,9 @@ __device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) 
   return h2_as_u32(__hfma2(u32_as_h2(a), u32_as_h2(b), u32_as_h2(c)));
 }
 __device__ __forceinline__ uint32_t h2c(float v) { return h2_as_u32(__float2half2_rn(v)); }
+// fp16x2 bit patterns of the exact power-of-two field multipliers (no runtime conversion in the dequant loop)
+constexpr uint32_t kH2_1_4 = 0x34003400u, kH2_1_8 = 0x30003000u, kH2_1_16 = 0x2C002C00u, kH2_1_64 = 0x24002400u,
+                   kH2_1_256 = 0x1C001C00u;
 
 __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
@@ -73,7 +76,7 @@ struct DqConst {
 
 // 4-bit: word = 4 pairs, pair k at bits 4k / 16+4k.
 __device__ __forceinline__ void dq4_word(uint32_t w, const DqConst& K, uint32_t (&o)[4]) {
-  const uint32_t m16 = h2c(1.0f / 16.0f);
+  const uint32_t m16 = kH2_1_16;
   uint32_t v0 = (w & 0x000F000Fu) | FW_MAGIC;
   uint32_t v1 = (w & 0x00F000F0u) | FW_MAGIC;
   uint32_t w8 = w >> 8;
@@ -95,10 +98,10 @@ __device__ __forceinline__ uint32_t dq3_pair(uint32_t w, int k, const DqConst& K
     return hmul2_u(hadd2_u(v, K.c[0]), K.s2);
   } else if (kk == 1) {
     v = (ww & 0x00380038u) | FW_MAGIC;
-    return hmul2_u(hfma2_u(v, h2c(1.0f / 8.0f), K.c[1]), K.s2);
+    return hmul2_u(hfma2_u(v, kH2_1_8, K.c[1]), K.s2);
   } else {
     v = (ww & 0x01C001C0u) | FW_MAGIC;
-    return hmul2_u(hfma2_u(v, h2c(1.0f / 64.0f), K.c[2]), K.s2);
+    return hmul2_u(hfma2_u(v, kH2_1_64, K.c[2]), K.s2);
   }
 }
 
@@ -107,10 +110,10 @@ __device__ __forceinline__ uint32_t dq2_pair(uint32_t w, int k, const DqConst& K
   uint32_t ww = k >= 5 ? (w >> 10) : w;
   int kk = k >= 5 ? k - 5 : k;
   const uint32_t masks[5] = {0x00030003u, 0x000C000Cu, 0x00300030u, 0x00C000C0u, 0x03000300u};
-  const float mul[5] = {1.f, 0.25f, 1.f / 16.f, 1.f / 64.f, 1.f / 256.f};
+  const uint32_t mul[5] = {0x3C003C00u, kH2_1_4, kH2_1_16, kH2_1_64, kH2_1_256};
   uint32_t v = (ww & masks[kk]) | FW_MAGIC;
   if (kk == 0) return hmul2_u(hadd2_u(v, K.c[0]), K.s2);
-  return hmul2_u(hfma2_u(v, h2c(mul[kk]), K.c[kk]), K.s2);
+  return hmul2_u(hfma2_u(v, mul[kk], K.c[kk]), K.s2);
 }
 
 __device__ __forceinline__ uint32_t cvt_e4m3x2_f16x2(uint16_t v) {
@@ -321,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t* src = a.wbase + a.exp_off[wk.e] + (size_t)wk.tile * a.kg * bb;
         for (int g = wk.g0; g < wk.g1; ++g, ++k) {
           const int s = k % S;
-          if (!mbar_wait(bar_w_empty + 8 * s, ((k / S) & 1) ^ 1, err, 1001, abort_flag, lim)) break;
+          if (!mbar_wait_sleepy(bar_w_empty + 8 * s, ((k / S) & 1) ^ 1, err, 1001, abort_flag, lim)) break;
           if (a.dbg & 8) {
             mbar_arrive(bar_w_full + 8 * s);
           } else {
@@ -343,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Work wk = decode_work(a, w, KS);
         for (int g = wk.g0; g < wk.g1; ++g, ++j) {
           const int p = j % P;
-          if (!mbar_wait(bar_ab_empty + 8 * p, ((j / P) & 1) ^ 1, err, 2001, abort_flag, lim)) break;
+          if (!mbar_wait_sleepy(bar_ab_empty + 8 * p, ((j / P) & 1) ^ 1, err, 2001, abort_flag, lim)) break;
           if (a.dbg & 16) {
             mbar_arrive(bar_b_full + 8 * p);
             continue;
@@ -453,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = blockIdx.x; w < total && !*abort_flag; w += gridDim.x, ++it) {
       const Work wk = decode_work(a, w, KS);
       const int buf = it & 1;
-      if (!mbar_wait(bar_acc_full + 8 * buf, (it >> 1) & 1, err, 5001, abort_flag, lim)) break;
+      if (!mbar_wait_sleepy(bar_acc_full + 8 * buf, (it >> 1) & 1, err, 5001, abort_flag, lim)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * N;
       bool emit = !(a.dbg & 32);
