@@ -37,7 +37,7 @@ void wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, in
            c10::optional<torch::Tensor> items, c10::optional<torch::Tensor> n_items, int64_t max_items,
            int64_t dense_T, torch::Tensor x, int64_t b_row0, torch::Tensor out, int64_t out_row0,
            int64_t out_cols, int64_t epi, bool accumulate, double alpha, int64_t n_tile, int64_t max_block_bytes,
-           torch::Tensor err, int64_t timeout_ns, int64_t k_splits) {
+           torch::Tensor err, int64_t timeout_ns, int64_t k_splits, c10::optional<torch::Tensor> row_dst) {
   CHECK_CUDA(wbase); CHECK_CUDA(x); CHECK_CUDA(out); CHECK_CUDA(err);
   CHECK_CONTIG(x); CHECK_CONTIG(out);
   CHECK_ALIGN16(wbase); CHECK_ALIGN16(x);
@@ -80,6 +80,11 @@ void wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, in
   a.accumulate = accumulate ? 1 : 0;
   a.alpha = (float)alpha;
   a.err = err.data_ptr<int32_t>();
+  if (row_dst.has_value()) {
+    TORCH_CHECK(row_dst->scalar_type() == torch::kInt64 && epi == fw::WGEMM_EPI_STORE && !accumulate,
+                "row_dst needs int64 addresses and the plain store epilogue");
+    a.row_dst = row_dst->data_ptr<int64_t>();
+  }
   a.timeout_ns = (unsigned long long)timeout_ns;
   static const int dbg = getenv("FW_WGEMM_DBG") ? atoi(getenv("FW_WGEMM_DBG")) : 0;
   a.dbg = dbg;

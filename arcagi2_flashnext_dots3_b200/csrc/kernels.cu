@@ -5,5 +5,9 @@
 #include "kernels.h"
 
 void register_fn(pybind11::module& m);
+void register_ep(pybind11::module& m);
 
-void register_kernels(pybind11::module& m) { register_fn(m); }
+void register_kernels(pybind11::module& m) {
+  register_fn(m);
+  register_ep(m);
+}

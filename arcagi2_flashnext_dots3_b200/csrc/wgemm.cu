@@ -524,7 +524,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (n < wk.nt) {
                   const float f = v[i] * a.alpha;
                   const size_t o = (orow0 + n) * a.out_ld + col;
-                  if (a.out_dtype == WGEMM_OUT_F32) {
+                  if (a.row_dst) {
+                    // per-row destination (may be a peer GPU's buffer): the expert-parallel combine's
+                    // data movement happens here, one store per output element straight into its source
+                    reinterpret_cast<float*>(a.row_dst[orow0 + n])[col] = f;
+                  } else if (a.out_dtype == WGEMM_OUT_F32) {
                     float* op = reinterpret_cast<float*>(a.out) + o;
                     *op = a.accumulate ? *op + f : f;
                   } else if (a.out_dtype == WGEMM_OUT_BF16) {

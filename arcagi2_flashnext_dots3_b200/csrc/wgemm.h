@@ -51,6 +51,7 @@ struct WGemmArgs {
   int epi;
   int accumulate;           // fp32 store only: out += result
   float alpha;
+  const int64_t* row_dst;   // optional: fp32 destination address of every output row (store epilogue only)
   // split-K (deterministic): k_splits CTAs share one (item, tile); each writes its fp32 partial
   // [N x 128] to workspace, bumps counters[item * row_tiles + tile]; the last one sums the partials in split
   // order, runs the epilogue and resets the counter to zero (so a captured graph can replay).

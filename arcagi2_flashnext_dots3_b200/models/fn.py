@@ -80,8 +80,9 @@ class FNModel:
     sequence b at positions[b] + j) through all layers, updating the caches of `slots`, and returns the final
     hidden state [rows, H] (act dtype); ``logits`` applies the LM head."""
 
-    def __init__(self, cfg, weights: dict, caches: FNCaches, device):
+    def __init__(self, cfg, weights: dict, caches: FNCaches, device, ep=None):
         self.cfg = cfg
+        self.ep = ep  # parallel.ep.EPGroup: expert-parallel MoE across GPUs (None = all experts local)
         self.W = weights
         self.c = caches
         self.device = torch.device(device)
@@ -126,6 +127,9 @@ class FNModel:
         return self._mm(o, p["o"])
 
     def _moe(self, x, p, h, inj):
+        if self.ep is not None:
+            self.ep.moe(self, x, p, h, inj)
+            return
         cfg = self.cfg
         T = x.shape[0]
         E = cfg.n_experts

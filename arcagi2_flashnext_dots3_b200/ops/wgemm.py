@@ -136,14 +136,15 @@ def matmul(x16: torch.Tensor, ws: WeightSet, out: torch.Tensor = None, epi: int 
     n = n_tile or dense_n_tile(T, ws)
     native.C().wgemm(ws.blob, ws.exp_off, ws.exp_fmt, ws.row_tiles, ws.kg, None, None, 0, T, x16, 0, out, 0,
                      cols, epi, accumulate, alpha, n, ws.max_block_bytes, native.err_word(x16.device),
-                     native.DEFAULT_TIMEOUT_NS, k_splits)
+                     native.DEFAULT_TIMEOUT_NS, k_splits, None)
     return out
 
 
 def grouped(xs16: torch.Tensor, ws: WeightSet, items: torch.Tensor, n_items: torch.Tensor, max_items: int,
-            out: torch.Tensor, epi: int = EPI_STORE, n_tile: int = 16) -> torch.Tensor:
+            out: torch.Tensor, epi: int = EPI_STORE, n_tile: int = 16, row_dst: torch.Tensor = None) -> torch.Tensor:
     """Grouped (MoE) GEMM: for each item (expert e, token start t0, count n) computes rows t0..t0+n of out
-    from rows t0..t0+n of xs16 with expert e's weights."""
+    from rows t0..t0+n of xs16 with expert e's weights. With `row_dst` (int64 [rows] device addresses, fp32
+    rows of out's width) every output row is stored at its own address instead (possibly on a peer GPU)."""
     cols = ws.rows // 2 if epi == EPI_SILU_MUL else ws.rows
     if not xs16.is_cuda:
         it = items[: int(n_items.reshape(-1)[0])].tolist()
@@ -153,7 +154,7 @@ def grouped(xs16: torch.Tensor, ws: WeightSet, items: torch.Tensor, n_items: tor
         return out
     native.C().wgemm(ws.blob, ws.exp_off, ws.exp_fmt, ws.row_tiles, ws.kg, items, n_items, max_items, -1, xs16, 0,
                      out, 0, cols, epi, False, 1.0, n_tile, ws.max_block_bytes, native.err_word(xs16.device),
-                     native.DEFAULT_TIMEOUT_NS, 1)
+                     native.DEFAULT_TIMEOUT_NS, 1, row_dst)
     return out
 
 
