@@ -93,7 +93,7 @@ class DecodeGraph:
 
 
 class LLM:
-    def __init__(self, cfg, weights: dict, device="cuda", engine: EngineConfig = None, model_cls=None):
+    def __init__(self, cfg, weights: dict, device="cuda", engine: EngineConfig = None, model_cls=None, ep=None):
         from ..models.fn import FNModel, allocate_caches
         self.cfg = cfg
         self.ec = engine or EngineConfig()
@@ -103,7 +103,7 @@ class LLM:
         self.scratch = ec.max_seqs
         self.caches = allocate_caches(cfg, self.device, ec.max_seqs + 1, ec.max_model_len, ec.block_size,
                                       kv_dtype=ec.kv_dtype, state_dtype=ec.state_dtype)
-        self.model = (model_cls or FNModel)(cfg, weights, self.caches, self.device)
+        self.model = (model_cls or FNModel)(cfg, weights, self.caches, self.device, ep=ep)
         self.alloc = BlockAllocator(self.caches.n_blocks, ec.max_seqs + 1)
         self.model.assign_blocks(self.scratch, 1, self.alloc)
         self.free_slots = list(range(ec.max_seqs - 1, -1, -1))
@@ -185,10 +185,11 @@ class LLM:
     def step(self) -> dict:
         """One decode step for all running sequences. Returns {slot: new token}."""
         seqs = [s for s in self.running.values() if not s.done]
-        if not seqs:
+        if not seqs and self.model.ep is None:
             return {}
+        # expert parallel: every rank steps in lockstep, a rank without sequences runs padding rows only
         n = len(seqs)
-        g = self._graph_for(n)
+        g = self._graph_for(max(n, 1))
         B = g.batch
         for i in range(B):
             if i < n:

@@ -208,11 +208,13 @@ def _ws_chunks(chunks: list, fmts: list, rows: int, K: int, silu_pairs: bool, de
                            tuple(int(f) for f in fmts), silu_pairs)
 
 
-def _random_experts(cfg, g, device, chunk=32, symmetric=False):
-    H, I, E = cfg.hidden_size, cfg.moe_inter, cfg.n_experts
+def _random_experts(cfg, g, device, chunk=32, symmetric=False, lo=0, hi=None):
+    """Experts [lo, hi) (default: all) of one layer, random N(0, STD) weights quantized to each expert's bits."""
+    H, I = cfg.hidden_size, cfg.moe_inter
+    E = cfg.n_experts if hi is None else hi
     perm = rt.gate_up_perm(I, device=device)
     gu_chunks, d_chunks, fmts = [], [], []
-    e = 0
+    e = lo
     while e < E:
         bits = cfg.bits_of(e)
         n = 1
@@ -232,9 +234,14 @@ def _random_experts(cfg, g, device, chunk=32, symmetric=False):
     return (_ws_chunks(gu_chunks, fmts, 2 * I, H, True, device), _ws_chunks(d_chunks, fmts, H, I, False, device))
 
 
-def random_engine(cfg, device, seed: int = 0, symmetric: bool = False) -> dict:
+def random_engine(cfg, device, seed: int = 0, symmetric: bool = False, expert_shard=None) -> dict:
     """Engine weights of the configured size, generated and packed on `device` (N(0, 0.02) dense weights stored
-    FP8 128x128 block-scaled, experts N(0, 0.02) RTN-quantized to their bit widths with group-128 scales)."""
+    FP8 128x128 block-scaled, experts N(0, 0.02) RTN-quantized to their bit widths with group-128 scales).
+    ``expert_shard=(rank, world)`` builds only that rank's experts (expert parallelism)."""
+    e_lo, e_hi = 0, cfg.n_experts
+    if expert_shard is not None:
+        r, w = expert_shard
+        e_lo, e_hi = r * cfg.n_experts // w, (r + 1) * cfg.n_experts // w
     dev = torch.device(device)
     g = torch.Generator(device=dev).manual_seed(seed)
     H, hc = cfg.hidden_size, cfg.hc_count
@@ -288,7 +295,7 @@ def random_engine(cfg, device, seed: int = 0, symmetric: bool = False) -> dict:
         else:
             M["mix"] = {"proj": dense(Hq * 2 * D + 2 * KV * D + iH * iD + iD, H), "o": dense(H, Hq * D),
                         "qn": rn(D, std=0.1), "kn": rn(D, std=0.1), "iqn": rn(iD, std=0.1), "ikn": rn(iD, std=0.1)}
-        gu, d = _random_experts(cfg, g, dev, symmetric=symmetric)
+        gu, d = _random_experts(cfg, g, dev, symmetric=symmetric, lo=e_lo, hi=e_hi)
         router = rn(cfg.n_experts + 1, H)
         M["moe"] = {"router": wgemm.build_weight_set([rt.pack_f16(router)], [16], router.shape[0], H, device=dev),
                     "gu": gu, "d": d, "sgu": dense(2 * cfg.shared_inter, H, silu=True),

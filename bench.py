@@ -77,7 +77,7 @@ def count_launches(model, step_fn):
     of this repository's kernels per step."""
     from arcagi2_flashnext_dots3_b200.ops import native
     C = native.C()
-    per_call = {"gdn_step": 2, "qsa_prep": 2, "qsa_select": 2, "attn_decode": 2}
+    per_call = {"gdn_step": 2, "qsa_prep": 2, "qsa_select": 2, "attn_decode": 2, "ep_gather": 2}
     names = [n for n in dir(C) if not n.startswith("_") and callable(getattr(C, n)) and n != "sm_count"]
     counts = {}
     orig = {}
@@ -108,6 +108,9 @@ def main():
     ap.add_argument("--ctx-max", type=int, default=12288)
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
     ap.add_argument("--layers", type=int, default=0, help="debug only: fewer layers (result marked invalid)")
+    ap.add_argument("--ep", default="auto", choices=["auto", "on", "off"],
+                    help="expert parallelism across the GPUs (auto: on when more than one GPU)")
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl"], help="EP exchange: in-kernel NVLink or NCCL")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -119,6 +122,7 @@ def main():
     from arcagi2_flashnext_dots3_b200.engine.llm import LLM, DecodeGraph
     from arcagi2_flashnext_dots3_b200.models.fn_weights import engine_bytes, random_engine
     from arcagi2_flashnext_dots3_b200.ops import native
+    from arcagi2_flashnext_dots3_b200.parallel.ep import EPGroup
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -132,8 +136,9 @@ def main():
     if args.layers:
         kw["num_layers"] = args.layers
     cfg = fn_config(**kw)
+    use_ep = world > 1 and args.ep != "off" or args.ep == "on"
     t0 = time.time()
-    W = random_engine(cfg, dev, seed=1234)
+    W = random_engine(cfg, dev, seed=1234 + rank, expert_shard=(rank, world) if use_ep else None)
     torch.cuda.synchronize()
     t_w = time.time() - t0
     nbytes = engine_bytes(W)
@@ -142,7 +147,9 @@ def main():
     max_new = Wm + K + E2E + 8
     ec = EngineConfig(max_seqs=args.batch, max_model_len=args.ctx_max + max_new + 64, block_size=64,
                       kv_dtype="fp8", graph_batch_sizes=(args.batch,))
-    llm = LLM(cfg, W, dev, ec)
+    ep = EPGroup(cfg, rank, world, dev, max_tokens=args.batch, comm=args.comm,
+                 timeout_ns=int(20e9)) if use_ep else None
+    llm = LLM(cfg, W, dev, ec, ep=ep)
     g = torch.Generator().manual_seed(100 + rank)
     lengths = torch.randint(args.ctx_min, args.ctx_max + 1, (args.batch,), generator=g).tolist()
     seqs = llm.synthesize_context(lengths, max_new)
@@ -221,7 +228,9 @@ def main():
             "config": {"model": f"flashnext-shaped {cfg.num_layers}L h{cfg.hidden_size} {cfg.n_experts}/"
                                  f"{cfg.n_experts_orig} experts top-{cfg.top_k} 4/3-bit g128 + FP8 128x128 dense",
                        "global_batch": total_batch, "seq_len": f"{args.ctx_min}-{args.ctx_max} context",
-                       "parallelism": f"dp{world}", "kv_cache": "fp8 paged, block 64",
+                       "parallelism": (f"dp{world} attention + ep{world} experts ({args.comm} exchange)" if use_ep
+                                       else f"dp{world}"),
+                       "kv_cache": "fp8 paged, block 64",
                        "l2": "inputs larger than L2 (weights streamed per step >> 126 MB)",
                        "ple": "off (n-gram embedding layer not in this measurement)",
                        "compute": "fp16 tensor-core MMA, fp32 accumulate; activations fp16/fp32",
@@ -238,6 +247,9 @@ def main():
         print(json.dumps(out))
         sys.stdout.flush()
     if world > 1:
+        llm.graphs.clear()
+        del llm
+        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
 

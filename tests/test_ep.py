@@ -27,3 +27,10 @@ def test_ep_fused_two_gpus():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     _run(2, "fused", 29633, {"NCCL_NVLS_ENABLE": "0"})
+
+
+@pytest.mark.gpu
+def test_ep_nccl_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    _run(2, "nccl", 29635, {"NCCL_NVLS_ENABLE": "0", "EP_DEVICE": "cuda"})
