@@ -160,3 +160,28 @@ def unpack_blocks(blob: torch.Tensor, fmt: int, R: int, K: int) -> torch.Tensor:
     z = zb.permute(0, 2, 1).reshape(T * TILE, KG).float()
     w = (pairs.float() - z[..., None]) * s[..., None]
     return w.reshape(T * TILE, K)[:R]
+
+
+def unpack_qz(blob: torch.Tensor, fmt: int, R: int, K: int) -> torch.Tensor:
+    """(q - z) as fp32 [R, K] of an integer-format expert's blocks [tiles, KG, bytes] (scales not applied)."""
+    T, KG, _ = blob.shape
+    NW = FMT_WORDS[fmt]
+    words = blob[..., : NW * 512].contiguous().view(torch.int32).view(T, KG, NW, TILE).to(torch.int64) & 0xFFFFFFFF
+    words = words.permute(0, 3, 1, 2).reshape(T * TILE, KG, NW)
+    ppw = {4: 4, 3: 5, 2: 8}[fmt]
+    sh = (fmt * torch.arange(ppw, device=words.device)).view(1, 1, 1, ppw)
+    mask = (1 << fmt) - 1
+    lo = (words[..., None] >> sh) & mask
+    hi = (words[..., None] >> (sh + 16)) & mask
+    q = torch.stack([lo, hi], -1).reshape(T * TILE, KG, NW * ppw * 2)[..., :128]
+    zb = blob[..., NW * 512 + 256: NW * 512 + 384].contiguous().view(T, KG, TILE)
+    z = zb.permute(0, 2, 1).reshape(T * TILE, KG).float()
+    return (q.float() - z[..., None]).reshape(T * TILE, K)[:R]
+
+
+def block_scales(blob: torch.Tensor, fmt: int, R: int) -> torch.Tensor:
+    """fp32 [R, KG] scales stored in an integer-format expert's blocks."""
+    T, KG, _ = blob.shape
+    NW = FMT_WORDS[fmt]
+    sb = blob[..., NW * 512: NW * 512 + 256].contiguous().view(torch.float16).view(T, KG, TILE)
+    return sb.permute(0, 2, 1).reshape(T * TILE, KG)[:R].float()

@@ -163,11 +163,12 @@ def ngram_ids(ids: torch.Tensor, cfg, mult, offs, sizes):
     """xor-hash n-gram row ids [T, heads] (student_fn.py:413-433); n-grams restart after each eos."""
     n, hpn, eos = cfg.ngram_size, cfg.heads_per_ngram, cfg.eos_token_id
     ctx = n - 1
-    hist = torch.cat([torch.full((ctx,), eos, dtype=torch.long), ids.long()])
+    dev = ids.device
+    hist = torch.cat([torch.full((ctx,), eos, dtype=torch.long, device=dev), ids.long()])
     L = hist.shape[0]
-    pos = torch.arange(L)
+    pos = torch.arange(L, device=dev)
     eosp = torch.where(hist == eos, pos, -1)
-    prev = torch.cat([torch.tensor([-1]), torch.cummax(eosp, 0).values[:-1]])
+    prev = torch.cat([torch.tensor([-1], device=dev), torch.cummax(eosp, 0).values[:-1]])
     pis = pos - (prev + 1)
     sh = []
     for s in range(n):

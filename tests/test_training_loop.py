@@ -1,0 +1,83 @@
+"""Repair-training loop on CPU: sharded Adam equals torch Adam at world 1, a 2-rank gloo run steps, resumes
+and exports a delta that rebuilds into a build whose scales are the trained ones."""
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+import torch
+
+from arcagi2_flashnext_dots3_b200.config import fn_small_config
+from arcagi2_flashnext_dots3_b200.formats import deltas, lowbit_file
+from arcagi2_flashnext_dots3_b200.models import fn_loader, fn_weights
+from arcagi2_flashnext_dots3_b200.parallel.zero import ShardedAdam
+from arcagi2_flashnext_dots3_b200.training import rl
+from arcagi2_flashnext_dots3_b200.training.train_rl import write_records
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_loo_advantages():
+    a = rl.loo_advantages([[1.0, 0.0, 0.0, 1.0]], clip=None)
+    assert np.allclose(a, [[1 - 1 / 3, -2 / 3, -2 / 3, 1 - 1 / 3]])
+    assert np.abs(rl.loo_advantages([[10.0, 0.0]])).max() == 2.0
+
+
+def test_sharded_adam_matches_torch_adam():
+    g = torch.Generator().manual_seed(0)
+    p1 = [torch.randn(5, 7, generator=g).requires_grad_(), torch.randn(11, generator=g).requires_grad_()]
+    p2 = [p.detach().clone().requires_grad_() for p in p1]
+    opt1 = ShardedAdam([{"params": p1, "lr": 1e-2}], bucket_elems=40)
+    opt2 = torch.optim.Adam(p2, lr=1e-2)
+    for it in range(4):
+        x = torch.randn(7, generator=g)
+        opt1.zero_grad()
+        opt2.zero_grad()
+        opt1.last_backward = True
+        ((p1[0] @ x).pow(2).sum() + p1[1].sin().sum()).backward()
+        ((p2[0] @ x).pow(2).sum() + p2[1].sin().sum()).backward()
+        opt1.step()
+        opt2.step()
+    for a, b in zip(p1, p2):
+        assert torch.allclose(a, b, atol=1e-6)
+
+
+def test_train_two_ranks_resume_and_export(tmp_path):
+    cfg = fn_small_config(num_layers=2, ple_layers=())
+    W = fn_weights.random_dense(cfg, seed=1, symmetric=False)
+    build = fn_loader.save_build(W, cfg, tmp_path / "build")
+    rng = np.random.default_rng(0)
+    recs = []
+    for i in range(8):
+        ids = rng.integers(0, cfg.vocab_size, 40)
+        recs.append((ids, np.arange(20, 40), float(rng.normal())))
+    write_records(tmp_path / "data", recs)
+    out = tmp_path / "out"
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29651", "-m",
+           "arcagi2_flashnext_dots3_b200.training.train_rl", "--data", str(tmp_path / "data"), "--build", str(build),
+           "--out", str(out), "--per-step", "4", "--steps", "2", "--chunk", "8"]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", PYTHONPATH=ROOT)
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-3000:]
+    log = [json.loads(x) for x in open(out / "log.jsonl")]
+    assert [x["step"] for x in log] == [1, 2] and all(np.isfinite(x["grad_norm"]) for x in log)
+    t1 = torch.load(out / "trained.pt", weights_only=False)
+    assert t1["step"] == 2
+    assert any(float(v.abs().sum()) > 0 for k, v in t1["params"].items() if "t_gu" in k)
+    # resume for one more step
+    r = subprocess.run(cmd[:-4] + ["--per-step", "4", "--steps", "3", "--chunk", "8", "--resume"], env=env,
+                       capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-3000:]
+    log = [json.loads(x) for x in open(out / "log.jsonl")]
+    assert [x["step"] for x in log] == [1, 2, 3]
+    # the exported delta rebuilds into a build whose scales are fp16(s0 * exp(t))
+    deltas.verify_manifest(out / "delta")
+    deltas.build(build, [out / "delta"], tmp_path / "rebuilt")
+    t3 = torch.load(out / "trained.pt", weights_only=False)["params"]
+    lay = lowbit_file.load_layer(tmp_path / "rebuilt", 1)
+    base = lowbit_file.load_layer(build, 1)
+    e = 3
+    want = (base.blobs[e].gu_s.float() * t3["moe.1.t_gu"][e].exp()).half()
+    assert torch.equal(lay.blobs[e].gu_s, want)
