@@ -136,6 +136,11 @@ class D3Config:
     qk_rope_dim: int = 64
     v_head_dim: int = 128
     swa_window: int = 513
+    swa_n_heads: int = 64                # SWA layers have their own head count (16 per TP4 rank)
+    swa_rope_theta: float = 10000.0
+    kv_rescale: bool = True              # MLA q/kv LoRA rescale sqrt(hidden / rank)
+    dense_fp8: bool = True               # dense weights block-FP8 128x128
+    eos_token_id: int = 1
     dsa_pattern: str = "FFSFSFSFSFFSF"   # index-share pattern over the DSA layers
     dsa_every: int = 0                   # 0: DSA layers spread evenly (13 of 46)
     n_dsa_layers: int = 13
@@ -151,6 +156,15 @@ class D3Config:
     expert_bits: tuple = (3, 2)
     route_scale: float = 2.5
     mtp_layers: int = 1
+
+    def heads_of(self, l: int) -> int:
+        return self.n_heads if self.layer_kind(l) == "dsa" else self.swa_n_heads
+
+    def latent_of(self, l: int) -> int:
+        return self.kv_lora_rank if self.layer_kind(l) == "dsa" else self.swa_kv_lora_rank
+
+    def is_moe(self, l: int) -> bool:
+        return l >= self.n_dense_layers
 
     def layer_kind(self, l: int) -> str:
         step = self.num_layers / self.n_dsa_layers
@@ -168,6 +182,17 @@ def fn_config(**kw) -> FNConfig:
 
 def d3_config(**kw) -> D3Config:
     return apply_env(D3Config(**kw), "FW_D3_")
+
+
+def d3_small_config(**kw) -> D3Config:
+    """A small D3-shaped model for tests: both attention kinds, dense + MoE layers, tiny dims."""
+    base = dict(name="d3-small", vocab_size=4096, hidden_size=256, num_layers=4, n_dense_layers=1, dense_inter=256,
+                n_heads=4, swa_n_heads=2, q_lora_rank=128, kv_lora_rank=128, swa_kv_lora_rank=256, qk_nope_dim=32,
+                qk_rope_dim=64, v_head_dim=64, swa_window=9, n_dsa_layers=2, index_heads=2, index_dim=128,
+                index_topk=16, n_experts_orig=16, n_experts=8, top_k=2, moe_inter=128, shared_inter=128,
+                expert_bits=(3, 2), route_scale=2.5)
+    base.update(kw)
+    return D3Config(**base)
 
 
 def tiny_config(**kw) -> FNConfig:

@@ -101,8 +101,9 @@ class LLM:
         ec = self.ec
         # one extra slot: padding rows of a graph bucket decode into it (never shared with a live sequence)
         self.scratch = ec.max_seqs
-        self.caches = allocate_caches(cfg, self.device, ec.max_seqs + 1, ec.max_model_len, ec.block_size,
-                                      kv_dtype=ec.kv_dtype, state_dtype=ec.state_dtype)
+        alloc = getattr(model_cls, "allocate", None) or allocate_caches
+        self.caches = alloc(cfg, self.device, ec.max_seqs + 1, ec.max_model_len, ec.block_size,
+                            kv_dtype=ec.kv_dtype, state_dtype=ec.state_dtype)
         self.model = (model_cls or FNModel)(cfg, weights, self.caches, self.device, ep=ep)
         self.alloc = BlockAllocator(self.caches.n_blocks, ec.max_seqs + 1)
         self.model.assign_blocks(self.scratch, 1, self.alloc)
@@ -236,14 +237,10 @@ class LLM:
         """Claim len(lengths) slots whose caches hold random state for contexts of the given lengths."""
         g = torch.Generator(device=self.device).manual_seed(seed)
         c = self.caches
-        for t in c.k + c.v:
-            t.copy_(torch.randn(t.shape, generator=g, device=self.device).to(t.dtype))
-        for t in c.comp:
-            t.copy_(torch.randn(t.shape, generator=g, device=self.device).to(t.dtype))
-        for t in c.kr_ring + c.conv:
-            t.copy_(torch.randn(t.shape, generator=g, device=self.device))
-        for t in c.ssm:
-            t.copy_((torch.randn(t.shape, generator=g, device=self.device) * 0.05).to(t.dtype))
+        if hasattr(self.model, "randomize_caches"):
+            self.model.randomize_caches(g)
+        else:
+            self._randomize_fn_caches(g)
         seqs = []
         for L in lengths:
             slot = self.free_slots.pop()
@@ -257,3 +254,14 @@ class LLM:
             torch.cuda.synchronize()
             native.check_error(self.device)
         return seqs
+
+    def _randomize_fn_caches(self, g):
+        c = self.caches
+        for t in c.k + c.v:
+            t.copy_(torch.randn(t.shape, generator=g, device=self.device).to(t.dtype))
+        for t in c.comp:
+            t.copy_(torch.randn(t.shape, generator=g, device=self.device).to(t.dtype))
+        for t in c.kr_ring + c.conv:
+            t.copy_(torch.randn(t.shape, generator=g, device=self.device))
+        for t in c.ssm:
+            t.copy_((torch.randn(t.shape, generator=g, device=self.device) * 0.05).to(t.dtype))

@@ -1,0 +1,150 @@
+"""Dots3-Note-shaped model on the engine path: incremental prefill + decode over paged FP8 latent caches.
+
+Layer (pre-norm, the reference's dotsnote/training/finetune/student.py:353-362 and the served vLLM model
+dotsnote/engine/vllm_patch/vllm/models/dots3_note/nvidia/model.py:513):
+
+    x = rms(h, ln1)                                   (fused with the previous residual add)
+    P = x @ [q_a | kv_a | g | idx_k | idx_w]^T        one tcgen05 GEMM
+    prep: q latent norm, FP8 latent row (kv norm + RoPE'd key) into the paged cache, index key into its cache
+    Q = q_latent @ [q_b | idx_q]^T                    one tcgen05 GEMM
+    q_lat[h] = q_nope[h] @ W_UK[h]                    per-head absorption (batched GEMM)
+    DSA layers: indexer logits -> exact top-2048 key positions; SWA layers: the last `swa_window` positions
+    o_lat = latent attention over the selected FP8 rows (shared by all heads)
+    o[h] = o_lat[h] @ W_UV[h]^T, times sigmoid(g)     absorption back + gate
+    h += o @ W_o^T ; x = rms(h, ln2) ; h += MoE(x) (sigmoid router + bias, 3/2-bit experts, shared expert)
+
+Every projection runs on the tcgen05 weight-dequant GEMM; the two per-head absorption products are batched
+cuBLAS GEMMs (small dense bf16 matrices); the rest are the kernels of csrc/k_d3.cu and the FN MoE kernels.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from ..ops import d3_ops as d3
+from ..ops import fn_ops as ops
+from ..ops import wgemm
+
+
+@dataclass
+class D3Caches:
+    latent: list        # per layer [n_blocks, block_size, kvr + dr]
+    idx: list           # per layer [S, max_len, iD] (DSA layers) or None
+    block_table: torch.Tensor
+    block_size: int
+    n_blocks: int
+    max_len: int
+
+
+def allocate_caches(cfg, device, n_slots: int, max_len: int, block_size: int = 64, n_blocks: int = None,
+                    kv_dtype: str = "fp8", state_dtype: str = "bf16") -> D3Caches:
+    dev = torch.device(device)
+    cpu = dev.type == "cpu"
+    max_blocks = (max_len + block_size - 1) // block_size
+    n_blocks = n_blocks or n_slots * max_blocks
+    latent, idx = [], []
+    for l in range(cfg.num_layers):
+        D = cfg.latent_of(l) + cfg.qk_rope_dim
+        latent.append(torch.zeros(n_blocks, block_size, D, dtype=torch.float32 if cpu else torch.float8_e4m3fn,
+                                  device=dev))
+        idx.append(torch.zeros(n_slots, max_len, cfg.index_dim, dtype=torch.float32 if cpu else torch.bfloat16,
+                               device=dev) if cfg.layer_kind(l) == "dsa" else None)
+    return D3Caches(latent, idx, torch.zeros(n_slots, max_blocks, dtype=torch.int32, device=dev), block_size,
+                    n_blocks, max_len)
+
+
+class D3Model:
+    allocate = staticmethod(allocate_caches)
+
+    def __init__(self, cfg, weights: dict, caches: D3Caches, device, ep=None):
+        self.cfg, self.W, self.c = cfg, weights, caches
+        self.ep = ep
+        self.device = torch.device(device)
+        self.act = ops.act_dtype(self.device)
+        self.rope = d3.rope_table(caches.max_len + 8, cfg.qk_rope_dim, cfg.rope_theta, self.device)
+        self.scale = (cfg.qk_nope_dim + cfg.qk_rope_dim) ** -0.5
+
+    def _mm(self, x, ws, epi=wgemm.EPI_STORE, out_dtype=torch.float32):
+        if not x.is_cuda:
+            return wgemm.matmul(x.float(), ws, epi=epi, out_dtype=torch.float32)
+        return wgemm.matmul(x, ws, epi=epi, out_dtype=out_dtype)
+
+    def _bmm(self, a, b):
+        """[H, T, k] x [H, k, n] -> [H, T, n] (bf16 on GPU)."""
+        return torch.bmm(a, b)
+
+    def _attn(self, x, p, l, slots, positions, n_tok):
+        cfg, c = self.cfg, self.c
+        P = self._mm(x, p["a"])
+        qc, gate, iw = d3.mla_prep(P, cfg, l, p, self.rope, c.latent[l], c.block_table, c.idx[l], slots, positions,
+                                   n_tok)
+        Q = self._mm(qc, p["qb"])
+        q_nope, q_pe, iq = d3.mla_qsplit(Q, cfg, l, self.rope, positions, n_tok)
+        q_lat = self._bmm(q_nope, p["uk"])                      # [H, T, kvr]
+        if cfg.layer_kind(l) == "dsa":
+            sel = d3.dsa_select(iq, iw, c.idx[l], slots, positions, n_tok, cfg.index_topk, c.max_len)
+            window = 0
+        else:
+            sel, window = None, cfg.swa_window
+        o_lat = d3.mla_attn(q_lat, q_pe, c.latent[l], c.block_table, slots, positions, n_tok, sel, window,
+                            self.scale)
+        o = self._bmm(o_lat, p["uv"].transpose(1, 2))           # [H, T, dv]
+        return self._mm(d3.mla_out(o, gate), p["o"])
+
+    def _moe(self, x, p, h):
+        cfg = self.cfg
+        T, E = x.shape[0], cfg.n_experts
+        logits = self._mm(x, p["router"])
+        ids, w = d3.route(logits, E, p["bias"], cfg.top_k, cfg.route_scale)
+        P = T * cfg.top_k
+        n_tile = wgemm.pick_n_tile(max(1, (2 * P) // E)) if x.is_cuda else 16
+        max_items = (P + n_tile - 1) // n_tile + E
+        pair_pos, items, n_items = ops.moe_plan(ids, E, n_tile, max_items)
+        xs = ops.moe_scatter(x, pair_pos)
+        act = torch.empty(P, cfg.moe_inter, dtype=self.act, device=x.device)
+        wgemm.grouped(xs, p["gu"], items, n_items, max_items, act, epi=wgemm.EPI_SILU_MUL, n_tile=n_tile)
+        ypair = torch.empty(P, cfg.hidden_size, dtype=torch.float32, device=x.device)
+        wgemm.grouped(act, p["d"], items, n_items, max_items, ypair, n_tile=n_tile)
+        sact = self._mm(x, p["sgu"], epi=wgemm.EPI_SILU_MUL, out_dtype=self.act)
+        ysh = self._mm(sact, p["sd"])
+        ones = torch.ones(T, 1, dtype=torch.float32, device=x.device)
+        ops.moe_combine(h, ypair, pair_pos, w, ysh, torch.full((T,), float("inf"), device=x.device), ones)
+
+    def step(self, ids: torch.Tensor, slots: torch.Tensor, positions: torch.Tensor, n_tok: int = 1):
+        cfg, W = self.cfg, self.W
+        h = W["embed"][ids.long()].float()
+        y = None
+        for l, L in enumerate(W["layers"]):
+            x = d3.add_rms(h, y, L["ln1"], cfg.rms_eps, self.act)
+            y = self._attn(x, L["attn"], l, slots, positions, n_tok)
+            x = d3.add_rms(h, y, L["ln2"], cfg.rms_eps, self.act)
+            if cfg.is_moe(l):
+                self._moe(x, L["moe"], h)
+                y = None
+            else:
+                sact = self._mm(x, L["mlp"]["gu"], epi=wgemm.EPI_SILU_MUL, out_dtype=self.act)
+                y = self._mm(sact, L["mlp"]["d"])
+        return d3.add_rms(h, y, W["norm"], cfg.rms_eps, self.act)
+
+    def logits(self, x: torch.Tensor) -> torch.Tensor:
+        return self._mm(x, self.W["lm_head"])
+
+    # ------------------------------------------------------------------------------------------- engine hooks
+    def assign_blocks(self, slot: int, n_tokens: int, allocator):
+        bs = self.c.block_size
+        need = (n_tokens + bs - 1) // bs
+        have = allocator.n_blocks_of(slot)
+        if need > have:
+            new = allocator.allocate(slot, need - have)
+            self.c.block_table[slot, have:need] = torch.tensor(new, dtype=torch.int32, device=self.device)
+
+    def reset_slot(self, slot: int):
+        pass  # attention-only state: the block table and positions define what is visible
+
+    def randomize_caches(self, g: torch.Generator):
+        for t in self.c.latent:
+            t.copy_((torch.randn(t.shape, generator=g, device=self.device)).to(t.dtype))
+        for t in self.c.idx:
+            if t is not None:
+                t.copy_(torch.randn(t.shape, generator=g, device=self.device).to(t.dtype))

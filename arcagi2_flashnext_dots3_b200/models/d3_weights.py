@@ -1,0 +1,105 @@
+"""Random-init weights of the Dots3-Note-shaped model in oracle (dense) form and engine form.
+
+Dense weights are rounded to their storage format first (block FP8 when ``cfg.dense_fp8``), so the oracle and
+the engine multiply the same values; experts are RTN-quantized to ``cfg.bits_of(e)`` bits (3/2 in the shipped
+build, dotsnote/training/README.md:218-224) and kept as planar checkpoint blobs plus dequantized copies.
+
+Engine form: the MLA down projections, the gate projection and (DSA layers) the indexer key/weight
+projections fuse into one GEMM ``a`` (the reference merges ``g_proj`` into the q/kv-a GEMM,
+dotsnote/engine/arcstats_pkg/arcstats/gmerge.py:1-20); ``q_b`` and the indexer query projection (both read the
+normalized q latent) fuse into ``qb``; ``kv_b`` is split into the per-head absorption matrices ``uk`` [H, dn, r]
+and ``uv`` [H, dv, r] of latent-space decode attention.
+"""
+from __future__ import annotations
+
+import torch
+
+from ..formats import lowbit_file
+from ..formats import runtime as rt
+from ..ops import wgemm
+from .fn_weights import STD, _round_dense, _round_permuted, _silu_perm_rows, _ws
+
+
+def random_dense(cfg, seed: int = 0, symmetric: bool = False) -> dict:
+    g = torch.Generator().manual_seed(seed)
+    Hd = cfg.hidden_size
+    rd = lambda *s, std=STD: torch.randn(*s, generator=g) * std  # noqa: E731
+    dn, dr, dv, qr = cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim, cfg.q_lora_rank
+    W = {"embed": rd(cfg.vocab_size, Hd, std=1.0).bfloat16().float(),
+         "lm_head": _round_dense(rd(cfg.vocab_size, Hd), cfg), "norm": 1.0 + rd(Hd, std=0.1), "layers": []}
+    for l in range(cfg.num_layers):
+        H, kvr = cfg.heads_of(l), cfg.latent_of(l)
+        # q_a / kv_a / g / indexer k,w fuse into one fp16 GEMM (fp16-rounded); the rest is block FP8
+        a = {"q_a": rd(qr, Hd).half().float(), "kv_a": rd(kvr + dr, Hd).half().float(),
+             "q_ln": 1.0 + rd(qr, std=0.1), "kv_ln": 1.0 + rd(kvr, std=0.1), "kr_ln": 1.0 + rd(dr, std=0.1),
+             "q_b": _round_dense(rd(H * (dn + dr), qr), cfg),
+             "kv_b": rd(H * (dn + dv), kvr, std=0.05).bfloat16().float(),
+             "o": _round_dense(rd(Hd, H * dv), cfg), "g": rd(H, Hd).half().float()}
+        if cfg.layer_kind(l) == "dsa":
+            iH, iD = cfg.index_heads, cfg.index_dim
+            a.update({"iq": _round_dense(rd(iH * iD, qr), cfg), "ik": rd(iD, Hd).half().float(),
+                      "ik_w": 1.0 + rd(iD, std=0.1), "ik_b": rd(iD, std=0.1), "iw": rd(iH, Hd).half().float()})
+        L = {"ln1": 1.0 + rd(Hd, std=0.1), "ln2": 1.0 + rd(Hd, std=0.1), "attn": a}
+        if cfg.is_moe(l):
+            lay = lowbit_file.random_layer(cfg.n_experts, Hd, cfg.moe_inter,
+                                           [cfg.bits_of(e) for e in range(cfg.n_experts)], g, std=STD,
+                                           symmetric=symmetric, n_orig=cfg.n_experts_orig)
+            L["moe"] = {"gate": lay.router.float().half().float(), "bias": rd(cfg.n_experts, std=0.1),
+                        "lowbit": lay, "experts_dense": [b.dense() for b in lay.blobs],
+                        "shared": {"gu": _round_permuted(rd(2 * cfg.shared_inter, Hd), cfg),
+                                   "d": _round_dense(rd(Hd, cfg.shared_inter), cfg)}}
+        else:
+            L["mlp"] = {"gu": _round_permuted(rd(2 * cfg.dense_inter, Hd), cfg),
+                        "d": _round_dense(rd(Hd, cfg.dense_inter), cfg)}
+        W["layers"].append(L)
+    return W
+
+
+def _f32(t, device):
+    return t.float().to(device)
+
+
+def to_engine(W: dict, cfg, device) -> dict:
+    dev = torch.device(device)
+    dn, dr, dv = cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim
+    low = torch.float32 if dev.type == "cpu" else torch.bfloat16
+    E = {"embed": W["embed"].to(dev, torch.float32 if dev.type == "cpu" else torch.bfloat16),
+         "lm_head": _ws(W["lm_head"], cfg, dev), "norm": _f32(W["norm"], dev), "layers": []}
+    for l, L in enumerate(W["layers"]):
+        a = L["attn"]
+        H, kvr = cfg.heads_of(l), cfg.latent_of(l)
+        dsa = cfg.layer_kind(l) == "dsa"
+        rows_a = [a["q_a"], a["kv_a"], a["g"]] + ([a["ik"], a["iw"]] if dsa else [])
+        rows_b = [a["q_b"]] + ([a["iq"]] if dsa else [])
+        kvb = a["kv_b"].view(H, dn + dv, kvr)
+        M = {"ln1": _f32(L["ln1"], dev), "ln2": _f32(L["ln2"], dev),
+             "attn": {"a": wgemm.build_weight_set([rt.pack_f16(torch.cat(rows_a, 0))], [16],
+                                                  sum(r.shape[0] for r in rows_a), cfg.hidden_size, device=dev),
+                      "qb": _ws(torch.cat(rows_b, 0), cfg, dev),
+                      "uk": kvb[:, :dn, :].contiguous().to(dev, low),
+                      "uv": kvb[:, dn:, :].contiguous().to(dev, low),
+                      "o": _ws(a["o"], cfg, dev),
+                      **{k: _f32(a[k], dev) for k in ("q_ln", "kv_ln", "kr_ln")}}}
+        if dsa:
+            M["attn"].update({"ik_w": _f32(a["ik_w"], dev), "ik_b": _f32(a["ik_b"], dev)})
+        if cfg.is_moe(l):
+            mo = L["moe"]
+            perm = rt.gate_up_perm(cfg.moe_inter)
+            gu, d, fmts = [], [], []
+            for b in mo["lowbit"].blobs:
+                gu.append(rt.pack_planar_blob(b.gu, b.gu_s, b.gu_z, b.bits, row_perm=perm))
+                d.append(rt.pack_planar_blob(b.d, b.d_s, b.d_z, b.bits))
+                fmts.append(b.bits)
+            M["moe"] = {"router": wgemm.build_weight_set([rt.pack_f16(mo["gate"].float())], [16], cfg.n_experts,
+                                                         cfg.hidden_size, device=dev),
+                        "bias": _f32(mo["bias"], dev),
+                        "gu": wgemm.build_weight_set(gu, fmts, 2 * cfg.moe_inter, cfg.hidden_size, silu_pairs=True,
+                                                     device=dev),
+                        "d": wgemm.build_weight_set(d, fmts, cfg.hidden_size, cfg.moe_inter, device=dev),
+                        "sgu": _ws(_silu_perm_rows(mo["shared"]["gu"], cfg.shared_inter), cfg, dev, silu_pairs=True),
+                        "sd": _ws(mo["shared"]["d"], cfg, dev)}
+        else:
+            M["mlp"] = {"gu": _ws(_silu_perm_rows(L["mlp"]["gu"], cfg.dense_inter), cfg, dev, silu_pairs=True),
+                        "d": _ws(L["mlp"]["d"], cfg, dev)}
+        E["layers"].append(M)
+    return E
