@@ -8,10 +8,12 @@ void register_fn(pybind11::module& m);
 void register_ep(pybind11::module& m);
 void register_train(pybind11::module& m);
 void register_d3(pybind11::module& m);
+void register_sample(pybind11::module& m);
 
 void register_kernels(pybind11::module& m) {
   register_fn(m);
   register_ep(m);
   register_train(m);
   register_d3(m);
+  register_sample(m);
 }

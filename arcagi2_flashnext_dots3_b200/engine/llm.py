@@ -5,8 +5,9 @@ Replaces the reference's external vLLM engine (scheduler, KV manager, CUDA graph
 
 * ``add(prompt)`` claims a slot, allocates paged-KV blocks and prefills in chunks.
 * ``step()`` decodes one token for every running sequence: the input ids are copied host->device from pinned
-  memory, one CUDA graph (captured per batch bucket) runs the whole model + LM head + argmax, and the new tokens
-  come back device->host. Finished sequences (eos / max tokens) release their slot and blocks.
+  memory, one CUDA graph (captured per batch bucket) runs the whole model + LM head + sampler, and the new tokens
+  (and their log-probabilities) come back device->host. Finished sequences (eos / stop ids / max tokens) stop.
+  Sampling parameters are per sequence (:class:`..ops.sampling.SamplingParams`; default greedy).
 * ``generate(prompts, max_new_tokens)`` = add + step until done.
 * ``synthesize_context(lengths)`` fills slots with random cache state of the given lengths (used by the bench
   to measure decode at 6k-12k contexts without spending minutes on prefill).
@@ -21,7 +22,13 @@ import torch
 from ..config import EngineConfig
 from ..ops import fn_ops as ops
 from ..ops import native
+from ..ops import sampling
+from ..ops.sampling import SamplingParams
 from .block_manager import BlockAllocator
+
+
+class ContextFull(ValueError):
+    """A push would exceed max_model_len."""
 
 
 @dataclass
@@ -34,29 +41,44 @@ class Sequence:
     done: bool = False
     t_first: float = 0.0
     t_last: float = 0.0
+    sp: SamplingParams = field(default_factory=SamplingParams)
+    lps: list = field(default_factory=list)   # log-probabilities of the generated tokens
+    finish: str = ""                          # "stop" / "length" once done
+    ctx_full: bool = False                    # stopped because the context reached max_model_len
 
 
 class DecodeGraph:
     """Static-shape decode step for `batch` rows (one CUDA graph): ids/slots/positions in, next ids out.
     ``advance=True`` also feeds the next ids back and bumps positions inside the graph (device-only loops)."""
 
-    def __init__(self, model, batch: int, advance: bool, use_graph: bool = True, scratch_slot: int = None):
+    def __init__(self, model, batch: int, advance: bool, use_graph: bool = True, scratch_slot: int = None,
+                 sample: bool = False):
         dev = model.device
         self.scratch_slot = scratch_slot
         self.model = model
         self.batch = batch
         self.advance = advance
+        self.sample = sample
         self.ids = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.slots = torch.arange(batch, dtype=torch.int32, device=dev)
         self.positions = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.next_ids = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.next_lp = torch.zeros(batch, dtype=torch.float32, device=dev)
+        # sampler inputs (temperature, top_k, top_p, seed, step); zeros = greedy
+        self.sp = [torch.zeros(batch, dtype=dt, device=dev)
+                   for dt in (torch.float32, torch.int32, torch.float32, torch.int64, torch.int64)]
+        self.sp[2].fill_(1.0)
         self.graph = None
         self.use_graph = use_graph and model.device.type == "cuda"
 
     def _body(self):
         m = self.model
         x = m.step(self.ids, self.slots, self.positions)
-        nxt = ops.argmax(m.logits(x))
+        if self.sample:
+            nxt, lp = sampling.sample(m.logits(x), *self.sp)
+            self.next_lp.copy_(lp)
+        else:
+            nxt = ops.argmax(m.logits(x))
         self.next_ids.copy_(nxt)
         if self.advance:
             self.ids.copy_(nxt)
@@ -116,16 +138,19 @@ class LLM:
         self.h_pos = torch.zeros(nh, dtype=torch.int32, pin_memory=pin)
         self.h_slots = torch.zeros(nh, dtype=torch.int32, pin_memory=pin)
         self.h_out = torch.zeros(nh, dtype=torch.int32, pin_memory=pin)
+        self.h_lp = torch.zeros(nh, dtype=torch.float32, pin_memory=pin)
+        self.h_sp = [torch.zeros(nh, dtype=dt, pin_memory=pin)
+                     for dt in (torch.float32, torch.int32, torch.float32, torch.int64, torch.int64)]
         self.eos = getattr(cfg, "eos_token_id", -1)
         self.stats = {"steps": 0, "tokens": 0, "prefill_tokens": 0}
 
     # ---------------------------------------------------------------------------------- admission
-    def add(self, prompt, max_new_tokens: int = 64, prefill_chunk: int = 2048) -> Sequence:
+    def add(self, prompt, max_new_tokens: int = 64, prefill_chunk: int = 2048, sp: SamplingParams = None) -> Sequence:
         if not self.free_slots:
             raise RuntimeError("no free sequence slot")
         slot = self.free_slots.pop()
         self.model.reset_slot(slot)
-        seq = Sequence(slot, list(map(int, prompt)), max_new_tokens)
+        seq = Sequence(slot, list(map(int, prompt)), max_new_tokens, sp=sp or SamplingParams())
         need = len(seq.prompt) + max_new_tokens
         if need > self.ec.max_model_len:
             self.free_slots.append(slot)
@@ -144,9 +169,9 @@ class LLM:
             x = self.model.step(ids[a:b].to(dev), torch.tensor([seq.slot], dtype=torch.int32, device=dev),
                                 torch.tensor([a], dtype=torch.int32, device=dev), n_tok=b - a)
             last = x[-1:]
-        nxt = int(ops.argmax(self.model.logits(last))[0])
         seq.pos = len(seq.prompt)
-        seq.out.append(nxt)
+        self._append_sample(seq, last)
+        self._finished(seq)
         seq.t_first = time.perf_counter()
         self.stats["prefill_tokens"] += len(seq.prompt)
 
@@ -155,6 +180,11 @@ class LLM:
         The previously sampled token that was never fed is dropped in favour of the pushed tokens."""
         if max_new_tokens is not None:
             seq.max_new = len(seq.out) + max_new_tokens
+        if not tokens:
+            raise ValueError("extend needs at least one token (push back the pending sampled token to continue)")
+        if seq.pos + len(tokens) > self.ec.max_model_len - 1:
+            raise ContextFull(f"{seq.pos} held + {len(tokens)} pushed > max_model_len {self.ec.max_model_len} - 1")
+        seq.ctx_full = False
         need = seq.pos + len(tokens) + (seq.max_new - len(seq.out)) + 1
         self.model.assign_blocks(seq.slot, need, self.alloc)
         dev = self.device
@@ -163,9 +193,18 @@ class LLM:
                             torch.tensor([seq.pos], dtype=torch.int32, device=dev), n_tok=len(tokens))
         seq.prompt += list(tokens)
         seq.pos += len(tokens)
-        seq.out.append(int(ops.argmax(self.model.logits(x[-1:]))[0]))
         seq.done = False
+        seq.finish = ""
+        self._append_sample(seq, x[-1:])
+        self._finished(seq)
         self.running[seq.slot] = seq
+
+    def _append_sample(self, seq: Sequence, x_last):
+        """Sample the next token of `seq` from the hidden state of its last fed token."""
+        ts = sampling.params_tensors([seq.sp], [len(seq.out)], self.device)
+        ids, lp = sampling.sample(self.model.logits(x_last).float(), *[t.to(self.device) for t in ts])
+        seq.out.append(int(ids[0]))
+        seq.lps.append(float(lp[0]))
 
     def release(self, seq: Sequence):
         self.running.pop(seq.slot, None)
@@ -178,7 +217,7 @@ class LLM:
         g = self.graphs.get(bucket)
         if g is None:
             g = DecodeGraph(self.model, bucket, advance=False, use_graph=self.ec.cuda_graphs,
-                            scratch_slot=self.scratch)
+                            scratch_slot=self.scratch, sample=True)
             g.capture()
             self.graphs[bucket] = g
         return g
@@ -192,17 +231,24 @@ class LLM:
         n = len(seqs)
         g = self._graph_for(max(n, 1))
         B = g.batch
+        hs = self.h_sp
         for i in range(B):
             if i < n:
                 s = seqs[i]
                 self.h_ids[i], self.h_pos[i], self.h_slots[i] = s.out[-1], s.pos, s.slot
+                hs[0][i], hs[1][i], hs[2][i], hs[3][i], hs[4][i] = (s.sp.temperature, s.sp.top_k, s.sp.top_p,
+                                                                    s.sp.seed, len(s.out))
             else:  # padding row: scratch slot, position 0, output ignored
                 self.h_ids[i], self.h_pos[i], self.h_slots[i] = 0, 0, self.scratch
+                hs[0][i], hs[1][i], hs[2][i] = 0.0, 0, 1.0
         g.ids.copy_(self.h_ids[:B], non_blocking=True)
         g.positions.copy_(self.h_pos[:B], non_blocking=True)
         g.slots.copy_(self.h_slots[:B], non_blocking=True)
+        for dst, src in zip(g.sp, hs):
+            dst.copy_(src[:B], non_blocking=True)
         g.run()
         self.h_out[:B].copy_(g.next_ids, non_blocking=True)
+        self.h_lp[:B].copy_(g.next_lp, non_blocking=True)
         if self.device.type == "cuda":
             torch.cuda.current_stream().synchronize()
         now = time.perf_counter()
@@ -211,22 +257,30 @@ class LLM:
             t = int(self.h_out[i])
             s.pos += 1
             s.t_last = now
-            if len(s.out) >= s.max_new or s.out[-1] == self.eos:
-                s.done = True
-                continue
             s.out.append(t)
+            s.lps.append(float(self.h_lp[i]))
             res[s.slot] = t
+            self._finished(s)
         self.stats["steps"] += 1
         self.stats["tokens"] += len(res)
         return res
 
-    def generate(self, prompts, max_new_tokens: int = 64) -> list:
-        seqs = [self.add(p, max_new_tokens) for p in prompts]
+    def _finished(self, s: Sequence) -> bool:
+        """Mark `s` done if its newest token ends it (eos / stop id) or it reached its token budget. The newest
+        token is then left unfed (``pos`` counts fed tokens): a session continues by pushing it back first."""
+        last = s.out[-1]
+        if last == self.eos or last in s.sp.stop_token_ids:
+            s.done, s.finish = True, "stop"
+        elif len(s.out) >= s.max_new:
+            s.done, s.finish = True, "length"
+        elif s.pos + 1 >= self.ec.max_model_len - 1:
+            s.done, s.finish, s.ctx_full = True, "length", True
+        return s.done
+
+    def generate(self, prompts, max_new_tokens: int = 64, sp: SamplingParams = None) -> list:
+        seqs = [self.add(p, max_new_tokens, sp=sp) for p in prompts]
         while any(not s.done for s in seqs):
             self.step()
-            for s in seqs:
-                if len(s.out) >= s.max_new:
-                    s.done = True
         outs = [s.out[: s.max_new] for s in seqs]
         for s in seqs:
             self.release(s)

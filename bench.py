@@ -238,7 +238,7 @@ def main():
             "p50_tpot_ms": round(p50, 3),
             "clocks": clk,
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 3),
-                    "h2d_bytes_per_step": 3 * 4 * args.batch, "d2h_bytes_per_step": 4 * args.batch},
+                    "h2d_bytes_per_step": (3 * 4 + 28) * args.batch, "d2h_bytes_per_step": 8 * args.batch},
             "gpu_launches": launches * K,
             "gpu_launches_per_step": launches,
             "weights_gb": {k: round(v / 1e9, 2) for k, v in nbytes.items()},
