@@ -1,0 +1,143 @@
+"""Agent harness on CPU: grid helpers and invariants, the sandbox limits, voting, the solver loop with a scripted
+model, atomic submissions, and the session client against a live CPU server."""
+import asyncio
+import json
+import os
+
+import numpy as np
+import pytest
+
+from arcagi2_flashnext_dots3_b200.agent import arckit as ak
+from arcagi2_flashnext_dots3_b200.agent.sandbox import feedback, run_code_sync
+from arcagi2_flashnext_dots3_b200.agent.solver import Solver, ensure_submission, write_submission
+from arcagi2_flashnext_dots3_b200.agent.vote import rank
+
+TASK = {"train": [{"input": [[1, 0], [0, 0]], "output": [[0, 1], [0, 0]]},
+                  {"input": [[0, 0, 2], [0, 3, 0]], "output": [[2, 0, 0], [0, 3, 0]]}],
+        "test": [{"input": [[5, 0, 0], [0, 0, 7]]}]}
+GOOD = "def transform(g):\n    return [row[::-1] for row in g]\n"
+
+
+def test_arckit_basics():
+    g = ak.grid([[0, 0, 0], [0, 4, 4], [0, 4, 0]])
+    assert ak.bg(g) == 0 and ak.palette(g) == [0, 4]
+    assert ak.bbox(g != 0) == (1, 1, 3, 3)
+    assert ak.trim(g).tolist() == [[4, 4], [4, 0]]
+    objs = ak.objects(g)
+    assert len(objs) == 1 and objs[0].size == 3 and objs[0].colour == 4
+    assert "fliplr" in ak.symmetries([[1, 2, 1], [3, 3, 3]])
+    assert ak.period([[1, 2, 1, 2], [1, 2, 1, 2]]) == (1, 2)
+    assert ak.gravity([[1, 0], [0, 0]]).tolist() == [[0, 0], [1, 0]]
+    assert ak.find_sub([[1, 2, 3], [4, 5, 6]], [[5, 6]]) == [(1, 1)]
+    assert ak.downscale(ak.scale([[1, 2]], 3), 3).tolist() == [[1, 2]]
+    assert ak.enclosed([[1, 1, 1], [1, 0, 1], [1, 1, 1]], bgc=0)[1, 1]
+
+
+def test_invariants_and_flag():
+    inv = ak.invariants(TASK["train"])
+    assert "output shape == input shape" in inv
+    assert "output colours subset of input colours" in inv
+    bad = ak.flag(TASK["train"], [TASK["test"][0]["input"]], [[[9, 9, 9], [9, 9, 9]]])
+    assert "output colours subset of input colours" in bad
+
+
+def test_sandbox_runs_and_scores():
+    r = run_code_sync(GOOD, TASK)
+    assert r["has_transform"] and all(p["ok"] for p in r["train"])
+    assert r["tests"][0]["out"] == [[0, 0, 5], [7, 0, 0]]
+    r = run_code_sync("def transform(g):\n    return g\n", TASK)
+    assert not r["train"][0]["ok"]
+    assert "train 0: wrong cells" in feedback(r, TASK)
+
+
+@pytest.mark.parametrize("code,needle", [
+    ("while True:\n    pass\n", "timeout"),
+    ("import socket\nsocket.create_connection(('127.0.0.1', 9))\n", "not allowed"),
+    ("import subprocess\nsubprocess.run(['true'])\n", "not allowed"),
+    ("open('/tmp/fw_sandbox_escape', 'w').write('x')\n", "outside the sandbox"),
+    ("x = bytearray(3 << 30)\n", "MemoryError"),
+])
+def test_sandbox_limits(code, needle):
+    r = run_code_sync(code + GOOD, TASK, timeout=4.0, cpu_s=3)
+    assert needle in (r.get("error") or ""), r
+    assert not os.path.exists("/tmp/fw_sandbox_escape")
+
+
+def test_vote_ranking():
+    g1, g2, g3 = [[1]], [[2]], [[3]]
+    recs = [{"progs": [{"verified": True, "tests": [g1], "n_ok": 2, "n_train": 2}]},
+            {"progs": [{"verified": True, "tests": [g2], "n_ok": 2, "n_train": 2}]},
+            {"progs": [{"verified": True, "tests": [g2], "n_ok": 2, "n_train": 2}]},
+            {"progs": [{"verified": False, "tests": [g3], "n_ok": 1, "n_train": 2}], "answer": [g3]}]
+    r = rank(recs, 1)[0]
+    assert r["attempts"] == [g2, g1] and r["votes"] == [2, 1]
+    r = rank(recs[3:], 1)[0]
+    assert r["attempts"] == [g3] and r["from"] == ["fb"]
+
+
+def test_solver_with_scripted_model(tmp_path):
+    tasks = {"a": TASK, "b": TASK}
+
+    def factory(tid, idx):
+        turns = ["```python\ndef transform(g):\n    return g\n```", "fixed:\n```python\n" + GOOD + "```"]
+
+        async def complete(messages, max_tokens):
+            return turns[min(len([m for m in messages if m["role"] == "assistant"]), 1)]
+        return complete
+
+    s = Solver(tasks, factory, samples_per_task=3, concurrency=4, deadline_s=60, endgame_s=5, settle_votes=2)
+    ans = asyncio.run(s.run())
+    assert ans["a"][0]["attempt_1"] == [[0, 0, 5], [7, 0, 0]]
+    assert all(x.get("verified") for x in s.log)
+    assert 2 <= sum(1 for x in s.log if x["tid"] == "a") <= 3
+    p = str(tmp_path / "submission.json")
+    write_submission(p, {"a": ans["a"]})
+    sub = ensure_submission(p, tasks)
+    assert sub["b"][0]["attempt_1"] == TASK["test"][0]["input"]
+    assert json.load(open(p)) == sub
+
+
+def test_session_client_against_cpu_server():
+    import socket
+    import threading
+    import time
+
+    import torch
+    import uvicorn
+
+    from arcagi2_flashnext_dots3_b200.agent.client import SessionClient
+    from arcagi2_flashnext_dots3_b200.config import EngineConfig, fn_small_config
+    from arcagi2_flashnext_dots3_b200.engine.llm import LLM
+    from arcagi2_flashnext_dots3_b200.models import fn_weights
+    from arcagi2_flashnext_dots3_b200.server.app import create_app
+    from arcagi2_flashnext_dots3_b200.server.engine_loop import EngineLoop
+    from arcagi2_flashnext_dots3_b200.server.tokenizer import ByteTokenizer
+
+    cfg = fn_small_config(num_layers=1, ple_layers=())
+    W = fn_weights.to_engine(fn_weights.random_dense(cfg, seed=0, symmetric=False), cfg, "cpu")
+    eng = EngineLoop(LLM(cfg, W, "cpu", EngineConfig(max_seqs=2, max_model_len=512, block_size=16,
+                                                     graph_batch_sizes=(1, 2))), ByteTokenizer()).start()
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    server = uvicorn.Server(uvicorn.Config(create_app(eng), host="127.0.0.1", port=port, log_level="warning"))
+    th = threading.Thread(target=server.run, daemon=True)
+    th.start()
+    while not server.started:
+        time.sleep(0.05)
+
+    async def go():
+        c = SessionClient(f"http://127.0.0.1:{port}", ByteTokenizer(), "t1", 512, temperature=0.0, chunk=3)
+        msgs = [{"role": "user", "content": "hi"}]
+        a = await c(msgs, 7)
+        msgs += [{"role": "assistant", "content": a}, {"role": "user", "content": "more"}]
+        b = await c(msgs, 5)
+        await c.close()
+        return a, b, eng.stats
+    try:
+        a, b, st = asyncio.run(go())
+        assert st["sessions"] == 1 and st["pushes"] >= 3 and st["generated"] >= 12
+    finally:
+        server.should_exit = True
+        th.join(timeout=10)
+        eng.stop()
