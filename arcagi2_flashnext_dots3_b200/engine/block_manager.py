@@ -1,6 +1,6 @@
 """Paged-KV block allocator: a free list of fixed-size KV blocks and per-slot block lists.
 
-The native C++ allocator (csrc/host_blocks.cpp, module `_host`) is used when it is built; this pure-Python
+The native C++ allocator (csrc/host_runtime.cpp, module `_host`) is used when it is built; this pure-Python
 class has the same interface and is the fallback on machines without the host extension (the allocator is
 host-side bookkeeping only: it never touches device memory).
 """

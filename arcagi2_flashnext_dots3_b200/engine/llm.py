@@ -14,6 +14,7 @@ Replaces the reference's external vLLM engine (scheduler, KV manager, CUDA graph
 """
 from __future__ import annotations
 
+import os
 import time
 from dataclasses import dataclass, field
 
@@ -142,6 +143,10 @@ class LLM:
         self.h_sp = [torch.zeros(nh, dtype=dt, pin_memory=pin)
                      for dt in (torch.float32, torch.int32, torch.float32, torch.int64, torch.int64)]
         self.eos = getattr(cfg, "eos_token_id", -1)
+        self.steplog = None
+        if os.environ.get("FW_STEPLOG"):  # binary per-step records (utils/steplog.py)
+            from ..utils.steplog import StepLog
+            self.steplog = StepLog(os.environ["FW_STEPLOG"])
         self.stats = {"steps": 0, "tokens": 0, "prefill_tokens": 0}
 
     # ---------------------------------------------------------------------------------- admission
@@ -263,6 +268,8 @@ class LLM:
             self._finished(s)
         self.stats["steps"] += 1
         self.stats["tokens"] += len(res)
+        if self.steplog is not None:
+            self.steplog.append(t_us=int(now * 1e6), batch=n, tokens=len(res), kv_blocks_free=self.alloc.n_free())
         return res
 
     def _finished(self, s: Sequence) -> bool:
