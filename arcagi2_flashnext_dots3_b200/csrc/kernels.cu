@@ -9,6 +9,7 @@ void register_ep(pybind11::module& m);
 void register_train(pybind11::module& m);
 void register_d3(pybind11::module& m);
 void register_sample(pybind11::module& m);
+void register_ple(pybind11::module& m);
 
 void register_kernels(pybind11::module& m) {
   register_fn(m);
@@ -16,4 +17,5 @@ void register_kernels(pybind11::module& m) {
   register_train(m);
   register_d3(m);
   register_sample(m);
+  register_ple(m);
 }

@@ -35,8 +35,8 @@ class FNCaches:
     block_table: torch.Tensor  # [S, max_blocks] int32
     block_size: int
     n_blocks: int
-    ple_hist: torch.Tensor = None   # [S, (ple_conv-1)*ngram, hc*H] gvn history (PLE layers share one slot)
-    tok_hist: torch.Tensor = None   # [S, ngram-1] previous tokens (-1 = none) + [S] tokens since eos
+    ple_hist: list = None           # per PLE layer [S, (ple_conv-1)*ngram, hc*H] ring of normalized gated values
+    tok_hist: torch.Tensor = None   # [S, ngram]: ngram-1 previous tokens (newest first) + tokens since eos
 
 
 def kv_dtype_for(device, kv_dtype: str):
@@ -69,9 +69,10 @@ def allocate_caches(cfg, device, n_slots: int, max_len: int, block_size: int = 6
         block_table=torch.zeros(n_slots, max_blocks, dtype=torch.int32, device=dev),
         block_size=block_size, n_blocks=n_blocks)
     if cfg.ple_layers:
-        c.ple_hist = torch.zeros(n_slots, (cfg.ple_conv - 1) * cfg.ngram_size, cfg.hc_count * cfg.hidden_size,
-                                 dtype=torch.float32, device=dev)
-        c.tok_hist = torch.full((n_slots, cfg.ngram_size), -1, dtype=torch.int64, device=dev)
+        c.ple_hist = [torch.zeros(n_slots, (cfg.ple_conv - 1) * cfg.ngram_size, cfg.hc_count * cfg.hidden_size,
+                                  dtype=torch.float32, device=dev) for _ in cfg.ple_layers]
+        c.tok_hist = torch.full((n_slots, cfg.ngram_size), cfg.eos_token_id, dtype=torch.int64, device=dev)
+        c.tok_hist[:, -1] = 0
     return c
 
 
@@ -157,7 +158,8 @@ class FNModel:
             emb = fn_ple.embed_rows(self, ids, slots, positions, n_tok)
         for l, L in enumerate(W["layers"]):
             if "ple" in L:
-                fn_ple.apply(self, h, emb, L["ple"], slots, n_tok)
+                fn_ple.apply(self, h, emb, L["ple"], self.c.ple_hist[cfg.ple_layers.index(l)], slots, positions,
+                             n_tok)
             x, inj = self._hc(h, L["ahc"])
             if cfg.layer_kind(l) == "linear":
                 y = self._gdn(x, L["mix"], self.lin_idx[l], slots, n_tok)
@@ -187,5 +189,7 @@ class FNModel:
         for t in c.conv + c.ssm + c.kr_ring:
             t[slot].zero_()
         if c.ple_hist is not None:
-            c.ple_hist[slot].zero_()
-            c.tok_hist[slot].fill_(-1)
+            for t in c.ple_hist:
+                t[slot].zero_()
+            c.tok_hist[slot, :-1].fill_(self.cfg.eos_token_id)   # n-gram context before the first token: eos
+            c.tok_hist[slot, -1] = 0                              # tokens since the last eos

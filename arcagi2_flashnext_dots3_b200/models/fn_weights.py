@@ -180,7 +180,7 @@ def to_engine(W: dict, cfg, device) -> dict:
                     "sd": _ws(mo["sd"], cfg, device)}
         if "ple" in L:
             P = L["ple"]
-            M["ple"] = {"kp": _ws(P["kp"], cfg, device), "vp": _ws(P["vp"], cfg, device),
+            M["ple"] = {"kv": _ws(torch.cat([P["kp"], P["vp"]], 0), cfg, device),
                         **{k: P[k].float().to(device) for k in ("nk", "nq", "nc")},
                         "conv": P["conv"].reshape(P["conv"].shape[0], -1).float().to(device)}
         E["layers"].append(M)
@@ -283,7 +283,7 @@ def random_engine(cfg, device, seed: int = 0, symmetric: bool = False, expert_sh
     for l in range(cfg.num_layers):
         M = {"ahc": hc_params(), "mhc": hc_params()}
         if l in cfg.ple_layers:
-            M["ple"] = {"kp": dense(hc * H, nh * cfg.ple_dim), "vp": dense(H, nh * cfg.ple_dim),
+            M["ple"] = {"kv": dense(hc * H + H, nh * cfg.ple_dim),
                         "nk": rn(hc * H, std=0.1), "nq": rn(hc * H, std=0.1), "nc": rn(hc * H, std=0.1),
                         "conv": rn(hc * H, cfg.ple_conv, std=0.3)}
         if cfg.layer_kind(l) == "linear":

@@ -77,7 +77,7 @@ def count_launches(model, step_fn):
     of this repository's kernels per step."""
     from arcagi2_flashnext_dots3_b200.ops import native
     C = native.C()
-    per_call = {"gdn_step": 2, "qsa_prep": 2, "qsa_select": 2, "attn_decode": 2, "ep_gather": 2}
+    per_call = {"gdn_step": 2, "qsa_prep": 2, "qsa_select": 2, "attn_decode": 2, "ep_gather": 2, "ple_mix": 3}
     names = [n for n in dir(C) if not n.startswith("_") and callable(getattr(C, n)) and n != "sm_count"]
     counts = {}
     orig = {}
@@ -132,7 +132,7 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
-    kw = {"ple_layers": ()}
+    kw = {}
     if args.layers:
         kw["num_layers"] = args.layers
     cfg = fn_config(**kw)
@@ -232,7 +232,8 @@ def main():
                                        else f"dp{world}"),
                        "kv_cache": "fp8 paged, block 64",
                        "l2": "inputs larger than L2 (weights streamed per step >> 126 MB)",
-                       "ple": "off (n-gram embedding layer not in this measurement)",
+                       "ple": f"layers {list(cfg.ple_layers)}, {cfg.ple_rows // 10**6}M x {cfg.ple_dim} fp8 n-gram table",
+                       "mtp": "off (no speculative decoding in this measurement)",
                        "compute": "fp16 tensor-core MMA, fp32 accumulate; activations fp16/fp32",
                        "valid": not args.layers},
             "p50_tpot_ms": round(p50, 3),

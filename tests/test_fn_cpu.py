@@ -73,3 +73,27 @@ def test_config1_greedy_decode_batch2():
         want_logits = ref.forward(W, cfg, seq)
         want_tokens = want_logits[255:].argmax(-1).tolist()
         assert want_tokens == outs[s], (s, [i for i, (a, b) in enumerate(zip(want_tokens, outs[s])) if a != b][:5])
+
+
+def test_ple_engine_matches_oracle():
+    """PLE layers (n-gram ids with eos restarts, FP8 table, gated dilated conv over the ring) in chunked prefill and
+    decode against the full-sequence oracle."""
+    from arcagi2_flashnext_dots3_b200.config import fn_small_config
+    cfg = fn_small_config(num_layers=2, ple_layers=(0, 1), indexer_budget=1 << 20)
+    W = fn_weights.random_dense(cfg, seed=6, symmetric=False)
+    E = fn_weights.to_engine(W, cfg, "cpu")
+    c = allocate_caches(cfg, "cpu", 2, 64, block_size=16)
+    m = FNModel(cfg, E, c, "cpu")
+    alloc = PyBlockAllocator(c.n_blocks, 2)
+    ids = torch.randint(3, cfg.vocab_size, (23,), generator=torch.Generator().manual_seed(8))
+    ids[9] = cfg.eos_token_id  # n-grams restart after an eos
+    m.reset_slot(1)
+    m.assign_blocks(1, 30, alloc)
+    s = torch.tensor([1], dtype=torch.int32)
+    xs = [m.step(ids[:6], s, torch.tensor([0], dtype=torch.int32), 6),
+          m.step(ids[6:14], s, torch.tensor([6], dtype=torch.int32), 8)]
+    for t in range(14, 23):
+        xs.append(m.step(ids[t:t + 1], s, torch.tensor([t], dtype=torch.int32), 1))
+    lg = m.logits(torch.cat(xs))
+    want = ref.forward(W, cfg, ids)
+    assert (lg - want).abs().max() <= 2e-3 * want.abs().max()

@@ -181,9 +181,9 @@ def test_attention_path(n_tok, L0):
     native.check_error()
 
 
-@pytest.mark.parametrize("kv", ["bf16", "fp8"])
-def test_small_model_gpu_vs_cpu(kv):
-    cfg = fn_small_config(ple_layers=())
+@pytest.mark.parametrize("kv,ple", [("bf16", ()), ("fp8", ()), ("fp8", (0, 2))])
+def test_small_model_gpu_vs_cpu(kv, ple):
+    cfg = fn_small_config(ple_layers=ple)
     W = fn_weights.random_dense(cfg, seed=11, symmetric=False)
     g = torch.Generator().manual_seed(12)
     ids = torch.randint(0, cfg.vocab_size, (90,), generator=g)
@@ -193,6 +193,7 @@ def test_small_model_gpu_vs_cpu(kv):
         c = allocate_caches(cfg, dev, 2, 256, block_size=16, kv_dtype=kv)
         m = FNModel(cfg, E, c, dev)
         alloc = PyBlockAllocator(c.n_blocks, 2)
+        m.reset_slot(0)
         m.assign_blocks(0, 128, alloc)
         models[dev] = m
     outs = {}
