@@ -199,12 +199,15 @@ void hc_residual(torch::Tensor h, torch::Tensor y, torch::Tensor inj) {
 // ======================================================================================= Gated DeltaNet
 // Causal depthwise conv over [conv_state | new tokens] + SiLU for every channel; updates conv_state in place.
 // Rows of proj: seq b token j at b*n_tok + j. One thread per (seq, channel).
+// n_commit (optional, per sequence): only the state after the first n_commit[b] tokens is written back (speculative
+// verification computes every token's output but commits the accepted prefix in a later pass).
 __global__ void gdn_conv_kernel(const float* proj, int ldp, const float* conv_w, float* conv_state, const int* slots,
-                                float* out, int C, int kc, int n_tok, int B) {
+                                float* out, int C, int kc, int n_tok, int B, const int* n_commit) {
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (int64_t)B * C) return;
   const int b = idx / C, c = idx % C;
   const int s = slots[b];
+  const int m = n_commit ? n_commit[b] : n_tok;
   float* st = conv_state + ((int64_t)s * C + c) * (kc - 1);
   float hist[8];  // kc - 1 <= 7
   for (int j = 0; j < kc - 1; ++j) hist[j] = st[j];
@@ -217,8 +220,9 @@ __global__ void gdn_conv_kernel(const float* proj, int ldp, const float* conv_w,
     for (int j = 0; j < kc - 2; ++j) hist[j] = hist[j + 1];
     hist[kc - 2] = x;
     out[((int64_t)b * n_tok + t) * C + c] = silu(acc);
+    if (t + 1 == m)
+      for (int j = 0; j < kc - 1; ++j) st[j] = hist[j];
   }
-  for (int j = 0; j < kc - 1; ++j) st[j] = hist[j];
 }
 
 // Gated delta rule for one (sequence, value head) over n_tok tokens; DK = DV = 128, 256 threads:
@@ -227,7 +231,7 @@ template <typename ST>
 __global__ void __launch_bounds__(256) gdn_recur_kernel(const float* qkv, const float* proj, int ldp, ST* ssm,
                                                         const int* slots, const float* A_log, const float* dt_bias,
                                                         const float* norm_w, __half* out, int nk, int nv, int n_tok,
-                                                        float eps, int gate_sigmoid) {
+                                                        float eps, int gate_sigmoid, const int* n_commit) {
   constexpr int DK = 128, DV = 128;
   __shared__ float q_s[DK], k_s[DK], part[2][DV], red[32];
   const int b = blockIdx.x, hv = blockIdx.y;
@@ -241,6 +245,7 @@ __global__ void __launch_bounds__(256) gdn_recur_kernel(const float* qkv, const 
   for (int i = 0; i < 64; ++i) Sr[i] = ldf(&S[(int64_t)(64 * half + i) * DV + j]);
   const float A = -__expf(A_log[hv]);
   const float dtb = dt_bias[hv];
+  const int m = n_commit ? n_commit[b] : n_tok;
   const float scale = rsqrtf((float)DK);
   for (int t = 0; t < n_tok; ++t) {
     const int64_t row = (int64_t)b * n_tok + t;
@@ -289,16 +294,24 @@ __global__ void __launch_bounds__(256) gdn_recur_kernel(const float* qkv, const 
       const float gz = gate_sigmoid ? sigm(z) : silu(z);
       out[row * (nv * DV) + hv * DV + j] = __float2half_rn(on * gz);
     }
+    if (t + 1 == m) {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) stf(&S[(int64_t)(64 * half + i) * DV + j], Sr[i]);
+    }
     __syncthreads();
   }
-#pragma unroll
-  for (int i = 0; i < 64; ++i) stf(&S[(int64_t)(64 * half + i) * DV + j], Sr[i]);
 }
 
 void gdn_step(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor conv_state, torch::Tensor ssm,
               torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor norm_w, torch::Tensor slots, torch::Tensor out,
-              int64_t nk, int64_t nv, int64_t dk, int64_t dv, int64_t n_tok, double eps, int64_t gate_sigmoid) {
+              int64_t nk, int64_t nv, int64_t dk, int64_t dv, int64_t n_tok, double eps, int64_t gate_sigmoid,
+              c10::optional<torch::Tensor> n_commit) {
   CK(dk == 128 && dv == 128);
+  const int* ncm = nullptr;
+  if (n_commit) {
+    CK(n_commit->scalar_type() == torch::kInt32 && n_commit->numel() * n_tok == proj.size(0));
+    ncm = n_commit->data_ptr<int32_t>();
+  }
   CK(proj.scalar_type() == torch::kFloat && proj.is_contiguous());
   CK(slots.scalar_type() == torch::kInt32);
   const int rows = proj.size(0);
@@ -312,18 +325,18 @@ void gdn_step(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor conv_state
   gdn_conv_kernel<<<(nthr + 255) / 256, 256, 0, STREAM>>>(proj.data_ptr<float>(), proj.size(1),
                                                           conv_w.data_ptr<float>(), conv_state.data_ptr<float>(),
                                                           slots.data_ptr<int32_t>(), qkv.data_ptr<float>(), C, kc,
-                                                          n_tok, B);
+                                                          n_tok, B, ncm);
   dim3 grid(B, nv);
   if (ssm.scalar_type() == torch::kBFloat16)
     gdn_recur_kernel<__nv_bfloat16><<<grid, 256, 0, STREAM>>>(
         qkv.data_ptr<float>(), proj.data_ptr<float>(), proj.size(1), (__nv_bfloat16*)ssm.data_ptr(),
         slots.data_ptr<int32_t>(), A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), norm_w.data_ptr<float>(),
-        (__half*)out.data_ptr(), nk, nv, n_tok, (float)eps, gate_sigmoid);
+        (__half*)out.data_ptr(), nk, nv, n_tok, (float)eps, gate_sigmoid, ncm);
   else
     gdn_recur_kernel<float><<<grid, 256, 0, STREAM>>>(
         qkv.data_ptr<float>(), proj.data_ptr<float>(), proj.size(1), ssm.data_ptr<float>(), slots.data_ptr<int32_t>(),
         A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), norm_w.data_ptr<float>(), (__half*)out.data_ptr(), nk,
-        nv, n_tok, (float)eps, gate_sigmoid);
+        nv, n_tok, (float)eps, gate_sigmoid, ncm);
 }
 
 // ============================================================================================ attention
@@ -406,19 +419,21 @@ __global__ void qsa_prep_kernel(const float* proj, int ldp, const float* qn, con
 
 // One block per sequence: compressed indexer keys of every block that completes within this step, from the ring
 // of the previous raw keys plus this step's rows; then the ring is refreshed. Sequential per sequence (no race).
+// The ring holds RL >= r raw keys indexed by position mod RL; the extra RL - r entries keep the keys of accepted
+// positions intact while speculative steps write (and later rewrite) up to RL - r rejected positions ahead.
 template <typename CT>
 __global__ void qsa_compress_kernel(const float* proj, int ldp, int kr_off, float* ring, CT* comp, int max_comp,
                                     const float* ikn, const float* rope, int rope_len, int rdq, const int* slots,
-                                    const int* positions, int r, int iD, int n_tok, float eps) {
+                                    const int* positions, int r, int RL, int iD, int n_tok, float eps) {
   extern __shared__ float sm[];
-  float* old = sm;             // [r][iD]
-  float* xs = sm + r * iD;     // [iD]
+  float* old = sm;             // [RL][iD]
+  float* xs = sm + RL * iD;    // [iD]
   __shared__ float red[32];
   const int b = blockIdx.x;
   const int s = slots[b];
   const int p0 = positions[b];
-  float* rg = ring + (int64_t)s * r * iD;
-  for (int i = threadIdx.x; i < r * iD; i += blockDim.x) old[i] = rg[i];
+  float* rg = ring + (int64_t)s * RL * iD;
+  for (int i = threadIdx.x; i < RL * iD; i += blockDim.x) old[i] = rg[i];
   __syncthreads();
   for (int t = 0; t < n_tok; ++t) {
     const int p = p0 + t;
@@ -428,7 +443,7 @@ __global__ void qsa_compress_kernel(const float* proj, int ldp, int kr_off, floa
     for (int d = threadIdx.x; d < iD; d += blockDim.x) {
       float acc = 0.f;
       for (int q = st; q <= p; ++q) {
-        const float v = q >= p0 ? proj[((int64_t)b * n_tok + (q - p0)) * ldp + kr_off + d] : old[(q % r) * iD + d];
+        const float v = q >= p0 ? proj[((int64_t)b * n_tok + (q - p0)) * ldp + kr_off + d] : old[(q % RL) * iD + d];
         acc += v;
       }
       xs[d] = acc / r;
@@ -440,12 +455,12 @@ __global__ void qsa_compress_kernel(const float* proj, int ldp, int kr_off, floa
       for (int d = threadIdx.x; d < iD; d += blockDim.x) stf(&comp[((int64_t)s * max_comp + cb) * iD + d], xs[d]);
     __syncthreads();
   }
-  // refresh the ring with the last min(r, n_tok) raw keys of this step
-  const int first = max(0, n_tok - r);
+  // refresh the ring with the last min(RL, n_tok) raw keys of this step
+  const int first = max(0, n_tok - RL);
   for (int t = first; t < n_tok; ++t) {
     const int p = p0 + t;
     for (int d = threadIdx.x; d < iD; d += blockDim.x)
-      rg[(p % r) * iD + d] = proj[((int64_t)b * n_tok + t) * ldp + kr_off + d];
+      rg[(p % RL) * iD + d] = proj[((int64_t)b * n_tok + t) * ldp + kr_off + d];
   }
 }
 
@@ -475,17 +490,19 @@ void qsa_prep(torch::Tensor proj, torch::Tensor qn, torch::Tensor kn, torch::Ten
 #undef PREP
   const int B = rows / n_tok;
   const int kr_off = Hq * 2 * D + 2 * KV * D + iH * iD;
-  const size_t smc = (ratio * iD + iD) * sizeof(float);
+  const int RL = kr_ring.size(1);
+  CK(RL >= ratio);
+  const size_t smc = (RL * iD + iD) * sizeof(float);
   if (comp_cache.scalar_type() == torch::kBFloat16)
     qsa_compress_kernel<__nv_bfloat16><<<B, 128, smc, STREAM>>>(
         proj.data_ptr<float>(), proj.size(1), kr_off, kr_ring.data_ptr<float>(), (__nv_bfloat16*)comp_cache.data_ptr(),
         comp_cache.size(1), ikn.data_ptr<float>(), rope.data_ptr<float>(), rope_len, rd, slots.data_ptr<int32_t>(),
-        positions.data_ptr<int32_t>(), ratio, iD, n_tok, (float)eps);
+        positions.data_ptr<int32_t>(), ratio, RL, iD, n_tok, (float)eps);
   else
     qsa_compress_kernel<float><<<B, 128, smc, STREAM>>>(
         proj.data_ptr<float>(), proj.size(1), kr_off, kr_ring.data_ptr<float>(), comp_cache.data_ptr<float>(),
         comp_cache.size(1), ikn.data_ptr<float>(), rope.data_ptr<float>(), rope_len, rd, slots.data_ptr<int32_t>(),
-        positions.data_ptr<int32_t>(), ratio, iD, n_tok, (float)eps);
+        positions.data_ptr<int32_t>(), ratio, RL, iD, n_tok, (float)eps);
 }
 
 // Indexer scores s[row, blk] = sum_h relu(iq[row,h] . comp[blk]) / sqrt(iD) for complete blocks, -inf beyond.

@@ -8,8 +8,8 @@
 //   ple_ids     : one thread per sequence walks its tokens in order (token history + tokens-since-eos per slot)
 //   ple_gather  : FP8 table rows -> fp16 embedding rows (the input of the fused key|value GEMM)
 //   ple_mix1    : per token: gate, gv and gvn (written to scratch)
-//   ple_mix2    : per token: dilated conv over gvn history (ring of the last (kc-1)*d positions per slot or
-//                 earlier tokens of the same chunk), h += gv + silu(conv)
+//   ple_mix2    : per token: dilated conv over gvn history (earlier tokens of the same chunk, or the per-slot ring
+//                 of >= (kc-1)*d rows indexed by position mod ring length), h += gv + silu(conv)
 //   ple_ring    : store the chunk's newest gvn rows into the ring (after every reader of this step)
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -119,10 +119,10 @@ __global__ void __launch_bounds__(256) ple_mix1_kernel(const float* P, const flo
 }
 
 __global__ void ple_mix2_kernel(float* h, const float* gv, const float* gvn, const float* ring, const float* conv,
-                                int C, int kc, int d, const int32_t* slots, const int32_t* positions, int n_tok) {
+                                int C, int kc, int d, int R, const int32_t* slots, const int32_t* positions,
+                                int n_tok) {
   const int t = blockIdx.x, b = t / n_tok, j = t % n_tok;
   const int p = positions[b] + j;
-  const int R = (kc - 1) * d;
   const float* rg = ring + (int64_t)slots[b] * R * C;
   for (int c = blockIdx.y * blockDim.x + threadIdx.x; c < C; c += gridDim.y * blockDim.x) {
     float acc = 0.f;
@@ -170,8 +170,8 @@ void ple_gather(torch::Tensor table, torch::Tensor rows, double scale, torch::Te
 void ple_mix(torch::Tensor h, torch::Tensor P, torch::Tensor nk, torch::Tensor nq, torch::Tensor nc, torch::Tensor conv,
              torch::Tensor ring, torch::Tensor slots, torch::Tensor positions, int64_t n_tok, int64_t hc, int64_t d,
              double eps) {
-  const int T = h.size(0), C = h.size(1), H = C / hc, kc = conv.size(1), R = (kc - 1) * d;
-  CK(hc <= 16 && P.size(1) == (hc + 1) * H && ring.size(1) == R && ring.size(2) == C);
+  const int T = h.size(0), C = h.size(1), H = C / hc, kc = conv.size(1), R = ring.size(1);
+  CK(hc <= 16 && P.size(1) == (hc + 1) * H && R >= (kc - 1) * d && ring.size(2) == C);
   CK(h.is_contiguous() && P.is_contiguous() && conv.is_contiguous() && ring.is_contiguous());
   if (!T) return;
   auto gv = torch::empty({T, C}, h.options());
@@ -181,7 +181,7 @@ void ple_mix(torch::Tensor h, torch::Tensor P, torch::Tensor nk, torch::Tensor n
                                          gv.data_ptr<float>(), gvn.data_ptr<float>());
   ple_mix2_kernel<<<dim3(T, (C + 1023) / 1024), 256, 0, STREAM>>>(
       h.data_ptr<float>(), gv.data_ptr<float>(), gvn.data_ptr<float>(), ring.data_ptr<float>(), conv.data_ptr<float>(),
-      C, kc, d, slots.data_ptr<int32_t>(), positions.data_ptr<int32_t>(), n_tok);
+      C, kc, d, R, slots.data_ptr<int32_t>(), positions.data_ptr<int32_t>(), n_tok);
   ple_ring_kernel<<<T, 256, 0, STREAM>>>(ring.data_ptr<float>(), gvn.data_ptr<float>(), C, R, slots.data_ptr<int32_t>(),
                                          positions.data_ptr<int32_t>(), n_tok);
 }

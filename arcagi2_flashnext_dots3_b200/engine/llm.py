@@ -169,11 +169,16 @@ class LLM:
         dev = self.device
         ids = torch.tensor(seq.prompt, dtype=torch.int32)
         last = None
+        keep = getattr(self, "_keep_prefill_rows", False)   # speculative drafters read every prompt row
+        rows = []
         for a in range(0, len(seq.prompt), chunk):
             b = min(len(seq.prompt), a + chunk)
             x = self.model.step(ids[a:b].to(dev), torch.tensor([seq.slot], dtype=torch.int32, device=dev),
                                 torch.tensor([a], dtype=torch.int32, device=dev), n_tok=b - a)
             last = x[-1:]
+            if keep:
+                rows.append(x)
+        self._prefill_rows = torch.cat(rows) if keep else None
         seq.pos = len(seq.prompt)
         self._append_sample(seq, last)
         self._finished(seq)
@@ -237,15 +242,16 @@ class LLM:
         g = self._graph_for(max(n, 1))
         B = g.batch
         hs = self.h_sp
-        for i in range(B):
-            if i < n:
-                s = seqs[i]
-                self.h_ids[i], self.h_pos[i], self.h_slots[i] = s.out[-1], s.pos, s.slot
-                hs[0][i], hs[1][i], hs[2][i], hs[3][i], hs[4][i] = (s.sp.temperature, s.sp.top_k, s.sp.top_p,
-                                                                    s.sp.seed, len(s.out))
-            else:  # padding row: scratch slot, position 0, output ignored
-                self.h_ids[i], self.h_pos[i], self.h_slots[i] = 0, 0, self.scratch
-                hs[0][i], hs[1][i], hs[2][i] = 0.0, 0, 1.0
+        pad = B - n
+        # vectorized fills of the pinned staging buffers (numpy views), one async copy per input vector
+        self.h_ids.numpy()[:B] = [s.out[-1] for s in seqs] + [0] * pad
+        self.h_pos.numpy()[:B] = [s.pos for s in seqs] + [0] * pad
+        self.h_slots.numpy()[:B] = [s.slot for s in seqs] + [self.scratch] * pad
+        hs[0].numpy()[:B] = [s.sp.temperature for s in seqs] + [0.0] * pad
+        hs[1].numpy()[:B] = [s.sp.top_k for s in seqs] + [0] * pad
+        hs[2].numpy()[:B] = [s.sp.top_p for s in seqs] + [1.0] * pad
+        hs[3].numpy()[:B] = [s.sp.seed for s in seqs] + [0] * pad
+        hs[4].numpy()[:B] = [len(s.out) for s in seqs] + [0] * pad
         g.ids.copy_(self.h_ids[:B], non_blocking=True)
         g.positions.copy_(self.h_pos[:B], non_blocking=True)
         g.slots.copy_(self.h_slots[:B], non_blocking=True)
@@ -258,12 +264,13 @@ class LLM:
             torch.cuda.current_stream().synchronize()
         now = time.perf_counter()
         res = {}
-        for i, s in enumerate(seqs):
-            t = int(self.h_out[i])
+        toks = self.h_out[:n].tolist()
+        lps = self.h_lp[:n].tolist()
+        for s, t, lp in zip(seqs, toks, lps):
             s.pos += 1
             s.t_last = now
             s.out.append(t)
-            s.lps.append(float(self.h_lp[i]))
+            s.lps.append(lp)
             res[s.slot] = t
             self._finished(s)
         self.stats["steps"] += 1

@@ -1,0 +1,191 @@
+"""Speculative decoding: drafters propose k tokens per sequence, one main-model step verifies all k + 1 positions.
+
+Step (greedy sequences; the reference's MTP-3 verify loop, SURVEY call stack 3.2, with the recurrent-state
+rollback of its RecoverSSM / lazy-fold patches, fnext/kv/0001-...recoverssm.patch and fnext/base/gdn_lazy.py):
+
+1. tokens [pending, d_1 .. d_k] of every sequence run through the main model in one step (``verify=True``): the
+   attention caches are written at their positions, recurrent states are not committed;
+2. targets y_j = argmax of the logits at each position; accepted a = length of the prefix with d_j == y_j;
+3. ``commit`` advances the recurrent states by a + 1 tokens and replays the PLE token history;
+4. the sequence gains d_1 .. d_a and y_{a+1} (pending); output equals plain greedy decoding exactly.
+
+Drafters:
+* :class:`MTPDrafter` — the model's MTP head (:mod:`..models.fn_mtp`): run over the verified rows (filling its KV
+  cache), then chained k - 1 single-token steps;
+* :class:`NgramDrafter` — prompt lookup: the continuation of the most recent earlier occurrence of the last n
+  tokens (n = max_n .. 1) in the sequence's own history (no model, host only);
+* :class:`OracleDrafter` — replays known continuations (tests of the verify/commit path at full acceptance).
+"""
+from __future__ import annotations
+
+import torch
+
+from ..ops import fn_ops as ops
+from .block_manager import BlockAllocator
+
+
+class NgramDrafter:
+    def __init__(self, max_n: int = 3):
+        self.max_n = max_n
+
+    def propose(self, llm, seqs, k):
+        out = []
+        for s in seqs:
+            ctx = s.prompt + s.out
+            d = []
+            for n in range(min(self.max_n, len(ctx) - 1), 0, -1):
+                key = ctx[-n:]
+                for i in range(len(ctx) - n - 1, -1, -1):
+                    if ctx[i:i + n] == key:
+                        d = ctx[i + n:i + n + k]
+                        break
+                if d:
+                    break
+            out.append((d + [ctx[-1]] * k)[:k])
+        return out
+
+    def observe(self, llm, seqs, x, ids, accepted, k):
+        pass
+
+
+class OracleDrafter:
+    def __init__(self, continuations: dict):
+        self.cont = continuations  # tuple(prompt) -> full expected output list
+
+    def propose(self, llm, seqs, k):
+        out = []
+        for s in seqs:
+            full = self.cont[tuple(s.prompt)]
+            n = len(s.out)
+            out.append((full[n:n + k] + [0] * k)[:k])
+        return out
+
+    def observe(self, llm, seqs, x, ids, accepted, k):
+        pass
+
+
+class MTPDrafter:
+    """Keeps, per slot, the MTP hidden state and next drafts produced after the last verify."""
+
+    def __init__(self, head):
+        self.head = head
+        self.alloc = BlockAllocator(head.caches.n_blocks, head.caches.block_table.shape[0])
+        self.next = {}
+
+    def prefill(self, llm, seq, x_rows: torch.Tensor, k: int):
+        """MTP over the prompt: position q reads (x_q, t_{q+1}); the last row uses the first sampled token."""
+        dev = llm.device
+        toks = seq.prompt[1:] + [seq.out[0]]
+        self.head.reset_slot(seq.slot)
+        self.alloc.release(seq.slot)
+        self.head.assign_blocks(seq.slot, len(seq.prompt) + seq.max_new + k + 8, self.alloc)
+        sl = torch.tensor([seq.slot], dtype=torch.int32, device=dev)
+        xm = self.head.step(x_rows, torch.tensor(toks, dtype=torch.int32, device=dev), sl,
+                            torch.tensor([0], dtype=torch.int32, device=dev), len(toks))
+        self._chain(llm, [seq], xm[-1:], torch.tensor([len(toks) - 1], device=dev), k)
+
+    def _chain(self, llm, seqs, xm, q_last, k):
+        """From MTP hidden rows xm [B, H] at positions q_last: draft 1 = argmax, then k - 1 chained steps."""
+        dev = llm.device
+        sl = torch.tensor([s.slot for s in seqs], dtype=torch.int32, device=dev)
+        d = ops.argmax(self.head.logits(xm)).to(torch.int32)
+        drafts = [d]
+        for i in range(1, k):
+            xm = self.head.step(xm, d, sl, (q_last + i).to(torch.int32), 1)
+            d = ops.argmax(self.head.logits(xm)).to(torch.int32)
+            drafts.append(d)
+        dd = torch.stack(drafts, 1).tolist()
+        for s, row in zip(seqs, dd):
+            self.next[s.slot] = row
+
+    def propose(self, llm, seqs, k):
+        return [self.next.get(s.slot, [s.out[-1]] * k)[:k] for s in seqs]
+
+    def observe(self, llm, seqs, x, ids, accepted, k):
+        """x [B*(k+1), H] verify hidden rows; ids [B, k+1] verify tokens; accepted [B] (host list)."""
+        dev = llm.device
+        B, k1 = len(seqs), k + 1
+        toks = []
+        for b, s in enumerate(seqs):
+            a = accepted[b]
+            row = ids[b][1:a + 1] + [s.out[-1]]          # next tokens of rows 0..a
+            toks.append((row + [s.out[-1]] * k1)[:k1])
+        sl = torch.tensor([s.slot for s in seqs], dtype=torch.int32, device=dev)
+        pos0 = torch.tensor([s.pos - accepted[b] - 1 for b, s in enumerate(seqs)], dtype=torch.int32, device=dev)
+        for s in seqs:
+            self.head.assign_blocks(s.slot, s.pos + 2 * k1 + 8, self.alloc)
+        xm = self.head.step(x, torch.tensor(toks, dtype=torch.int32, device=dev).view(-1), sl, pos0, k1)
+        idx = torch.tensor([b * k1 + accepted[b] for b in range(B)], device=dev)
+        self._chain(llm, seqs, xm[idx], pos0.long() + torch.tensor(accepted, device=dev), k)
+
+
+class SpecDecoder:
+    def __init__(self, llm, drafter, k: int = 3):
+        self.llm, self.drafter, self.k = llm, drafter, k
+        self.stats = {"steps": 0, "drafted": 0, "accepted": 0, "emitted": 0}
+
+    def add(self, prompt, max_new_tokens: int = 64):
+        llm = self.llm
+        if isinstance(self.drafter, MTPDrafter):
+            llm._keep_prefill_rows = True
+        seq = llm.add(prompt, max_new_tokens)
+        if isinstance(self.drafter, MTPDrafter):
+            self.drafter.prefill(llm, seq, llm._prefill_rows, self.k)
+            llm._keep_prefill_rows = False
+        return seq
+
+    def step(self) -> dict:
+        llm, k = self.llm, self.k
+        k1 = k + 1
+        seqs = [s for s in llm.running.values() if not s.done]
+        if not seqs:
+            return {}
+        if any(s.sp.temperature > 0 for s in seqs):
+            raise ValueError("speculative decoding verifies greedy sequences only")
+        dev = llm.device
+        drafts = self.drafter.propose(llm, seqs, k)
+        ids = [[s.out[-1]] + list(d) for s, d in zip(seqs, drafts)]
+        for s in seqs:
+            llm.model.assign_blocks(s.slot, s.pos + k1 + 1, llm.alloc)
+        sl = torch.tensor([s.slot for s in seqs], dtype=torch.int32, device=dev)
+        pos = torch.tensor([s.pos for s in seqs], dtype=torch.int32, device=dev)
+        x = llm.model.step(torch.tensor(ids, dtype=torch.int32, device=dev).view(-1), sl, pos, k1, verify=True)
+        y = ops.argmax(llm.model.logits(x)).view(len(seqs), k1).tolist()
+        accepted = []
+        for d, yy in zip(drafts, y):
+            a = 0
+            while a < k and d[a] == yy[a]:
+                a += 1
+            accepted.append(a)
+        llm.model.commit(torch.tensor([a + 1 for a in accepted], dtype=torch.int32, device=dev))
+        res = {}
+        for s, d, yy, a in zip(seqs, drafts, y, accepted):
+            s.pos += a + 1
+            new = list(d[:a]) + [yy[a]]
+            for t in new:
+                s.out.append(t)
+                s.lps.append(0.0)
+                res.setdefault(s.slot, []).append(t)
+                if llm._finished(s):
+                    break
+            self.stats["emitted"] += len(res[s.slot])
+        self.stats["steps"] += 1
+        self.stats["drafted"] += k * len(seqs)
+        self.stats["accepted"] += sum(accepted)
+        self.drafter.observe(llm, seqs, x, ids, accepted, k)
+        return res
+
+    def generate(self, prompts, max_new_tokens: int = 64) -> list:
+        seqs = [self.add(p, max_new_tokens) for p in prompts]
+        while any(not s.done for s in seqs):
+            self.step()
+        outs = [s.out[: s.max_new] for s in seqs]
+        for s in seqs:
+            self.llm.release(s)
+        return outs
+
+    @property
+    def acceptance(self) -> float:
+        """Mean tokens emitted per sequence-step (1 + accepted drafts)."""
+        n = self.stats["drafted"] / max(1, self.k)
+        return self.stats["emitted"] / max(1, n)

@@ -24,11 +24,16 @@ from ..ops import wgemm
 from .fn_weights import rank_pad
 
 
+# Extra entries of the position-indexed rings (indexer raw keys, PLE values): speculative verification writes up to
+# this many rejected positions ahead without overwriting entries that accepted positions still need.
+SPEC_SLACK = 8
+
+
 @dataclass
 class FNCaches:
     k: list            # per attention layer [n_blocks, block_size, KV, D]
     v: list
-    kr_ring: list      # per attention layer [S, ratio, iD]
+    kr_ring: list      # per attention layer [S, ratio + SPEC_SLACK, iD] raw indexer keys by position mod length
     comp: list         # per attention layer [S, max_comp_blocks, iD]
     conv: list         # per linear layer [S, C, kc-1]
     ssm: list          # per linear layer [S, nv, dk, dv]
@@ -60,7 +65,7 @@ def allocate_caches(cfg, device, n_slots: int, max_len: int, block_size: int = 6
     c = FNCaches(
         k=[torch.zeros(n_blocks, block_size, cfg.n_kv_heads, cfg.head_dim, dtype=kvd, device=dev) for _ in range(n_attn)],
         v=[torch.zeros(n_blocks, block_size, cfg.n_kv_heads, cfg.head_dim, dtype=kvd, device=dev) for _ in range(n_attn)],
-        kr_ring=[torch.zeros(n_slots, cfg.indexer_ratio, cfg.indexer_dim, dtype=torch.float32, device=dev)
+        kr_ring=[torch.zeros(n_slots, cfg.indexer_ratio + SPEC_SLACK, cfg.indexer_dim, dtype=torch.float32, device=dev)
                  for _ in range(n_attn)],
         comp=[torch.zeros(n_slots, max_len // cfg.indexer_ratio + 1, cfg.indexer_dim, dtype=idx_dt, device=dev)
               for _ in range(n_attn)],
@@ -69,7 +74,7 @@ def allocate_caches(cfg, device, n_slots: int, max_len: int, block_size: int = 6
         block_table=torch.zeros(n_slots, max_blocks, dtype=torch.int32, device=dev),
         block_size=block_size, n_blocks=n_blocks)
     if cfg.ple_layers:
-        c.ple_hist = [torch.zeros(n_slots, (cfg.ple_conv - 1) * cfg.ngram_size, cfg.hc_count * cfg.hidden_size,
+        c.ple_hist = [torch.zeros(n_slots, (cfg.ple_conv - 1) * cfg.ngram_size + SPEC_SLACK, cfg.hc_count * cfg.hidden_size,
                                   dtype=torch.float32, device=dev) for _ in cfg.ple_layers]
         c.tok_hist = torch.full((n_slots, cfg.ngram_size), cfg.eos_token_id, dtype=torch.int64, device=dev)
         c.tok_hist[:, -1] = 0
@@ -114,9 +119,40 @@ class FNModel:
 
     def _gdn(self, x, p, li, slots, n_tok):
         proj = self._mm(x, p["proj"])
+        v = getattr(self, "_verify", None)
+        ncm = None
+        if v is not None:
+            v["proj"][li] = (proj, p)
+            ncm = v["zeros"]
         o = ops.gdn_step(proj, p["conv"], self.c.conv[li], self.c.ssm[li], p["A_log"], p["dt_bias"], p["norm"],
-                         slots, self.cfg, n_tok)
+                         slots, self.cfg, n_tok, n_commit=ncm)
         return self._mm(o, p["out"])
+
+    def commit(self, n_commit: torch.Tensor):
+        """After a verify step: advance every recurrent state by the first n_commit[b] tokens of sequence b
+        (int32 [B] on the model's device) and restore + replay the PLE token history."""
+        v = self._verify
+        if v is None:
+            raise RuntimeError("commit() without a preceding verify step")
+        for li, (proj, p) in v["proj"].items():
+            ops.gdn_step(proj, p["conv"], self.c.conv[li], self.c.ssm[li], p["A_log"], p["dt_bias"], p["norm"],
+                         v["slots"], self.cfg, v["n_tok"], n_commit=n_commit)
+        if "tok_hist" in v:
+            self._replay_tok_hist(v, n_commit)
+        self._verify = None
+
+    def _replay_tok_hist(self, v, n_commit):
+        cfg = self.cfg
+        hist = v["tok_hist"].clone()                               # [B, n]: n-1 tokens newest first + since
+        toks = v["ids"].long().view(-1, v["n_tok"])
+        n = hist.shape[1]
+        for j in range(v["n_tok"]):
+            take = (n_commit.long() > j)[:, None]
+            t = toks[:, j:j + 1]
+            shifted = torch.cat([t, hist[:, :n - 2], torch.where(t == cfg.eos_token_id, torch.zeros_like(t),
+                                                                 hist[:, -1:] + 1)], 1)
+            hist = torch.where(take, shifted, hist)
+        self.c.tok_hist[v["slots"].long()] = hist
 
     def _attn(self, x, p, ai, slots, positions, n_tok):
         cfg, c = self.cfg, self.c
@@ -150,9 +186,23 @@ class FNModel:
         ops.moe_combine(h, ypair, pair_pos, w, ysh, logits[:, E], inj)
 
     # ------------------------------------------------------------------------------------------- step
-    def step(self, ids: torch.Tensor, slots: torch.Tensor, positions: torch.Tensor, n_tok: int = 1):
+    def step(self, ids: torch.Tensor, slots: torch.Tensor, positions: torch.Tensor, n_tok: int = 1,
+             verify: bool = False):
+        """``verify``: speculative verification of n_tok tokens per sequence. Recurrent (GDN) states are not
+        written back; the layer inputs are kept so :meth:`commit` can apply exactly the accepted prefix, and the
+        PLE token history is snapshotted for the same reason. Attention caches are position-indexed and need no
+        rollback (rejected positions are rewritten when real tokens reach them)."""
+        h = ops.embed_hc(ids, self.W["embed"], self.cfg.hc_count)
+        return self.step_from_h(h, ids, slots, positions, n_tok, verify)
+
+    def step_from_h(self, h, ids, slots, positions, n_tok: int = 1, verify: bool = False):
         cfg, W = self.cfg, self.W
-        h = ops.embed_hc(ids, W["embed"], cfg.hc_count)
+        self._verify = None
+        if verify:
+            self._verify = {"proj": {}, "slots": slots, "n_tok": n_tok, "ids": ids,
+                            "zeros": torch.zeros(slots.shape[0], dtype=torch.int32, device=slots.device)}
+            if self.c.tok_hist is not None:
+                self._verify["tok_hist"] = self.c.tok_hist[slots.long()].clone()
         if cfg.ple_layers:
             from . import fn_ple
             emb = fn_ple.embed_rows(self, ids, slots, positions, n_tok)

@@ -1,0 +1,70 @@
+"""Multi-token-prediction (MTP) draft head of the FN-shaped model.
+
+Structure (the reference serves the checkpoint's MTP layer, indexed as layer 48, as its draft model:
+flashnext/kaggle/README.md:30, fnext/mtp/fnmtp.py): at position q the head reads the main model's final hidden
+state x_q and the embedding of token t_{q+1}, normalizes both, projects [e; x] to the hidden size, runs one
+attention + MoE layer with its own KV cache (hyper-connection streams initialised from the projection), mixes the
+streams and applies the shared LM head; its output predicts t_{q+2}. Later drafts chain on the head's own hidden
+output. Weights: :func:`random_mtp` (no MTP checkpoint is available offline).
+"""
+from __future__ import annotations
+
+import dataclasses
+
+import torch
+
+from ..ops import fn_ops as ops
+from ..ops import wgemm
+from . import fn_weights
+from .fn import FNModel, allocate_caches
+
+
+def mtp_config(cfg):
+    return dataclasses.replace(cfg, num_layers=1, full_attn_interval=1, ple_layers=())
+
+
+def random_mtp(cfg, device, seed: int = 7) -> dict:
+    """Random MTP weights: fc [H, 2H], two RMSNorm weights, one attention+MoE layer and a stream mixer."""
+    mc = mtp_config(cfg)
+    if torch.device(device).type == "cpu" or cfg.hidden_size <= 1024:
+        W = fn_weights.to_engine(fn_weights.random_dense(mc, seed=seed, symmetric=False), mc, device)
+    else:
+        W = fn_weights.random_engine(mc, device, seed=seed)
+    g = torch.Generator().manual_seed(seed + 1)
+    H = cfg.hidden_size
+    fc = torch.randn(H, 2 * H, generator=g) * 0.02
+    return {"fc": fn_weights._ws(fc, mc, device), "pe": (torch.randn(H, generator=g) * 0.1).to(device),
+            "ph": (torch.randn(H, generator=g) * 0.1).to(device), "layer": W["layers"][0], "mixer": W["mixer"]}
+
+
+class MTPHead:
+    def __init__(self, cfg, main_W: dict, mtp_W: dict, device, n_slots: int, max_len: int, block_size: int = 64,
+                 kv_dtype: str = "fp8"):
+        self.cfg = cfg
+        self.mc = mtp_config(cfg)
+        self.W = mtp_W
+        self.main_W = main_W
+        self.caches = allocate_caches(self.mc, device, n_slots, max_len, block_size, kv_dtype=kv_dtype)
+        inner_W = {"embed": main_W["embed"], "lm_head": main_W["lm_head"], "mixer": mtp_W["mixer"],
+                   "layers": [mtp_W["layer"]]}
+        self.inner = FNModel(self.mc, inner_W, self.caches, device)
+        self.device = torch.device(device)
+
+    def step(self, x_prev: torch.Tensor, ids: torch.Tensor, slots, positions, n_tok: int = 1) -> torch.Tensor:
+        """x_prev [T, H] (main or previous MTP hidden), ids [T] next tokens -> MTP hidden [T, H] (act)."""
+        cfg, H = self.cfg, self.cfg.hidden_size
+        e = ops.embed_hc(ids, self.main_W["embed"], 1)
+        en = ops.hc_prenorm(e, self.W["pe"], 1, H, cfg.rms_eps)
+        xn = ops.hc_prenorm(x_prev.float().contiguous(), self.W["ph"], 1, H, cfg.rms_eps)
+        u = self.inner._mm(torch.cat([en, xn], 1).contiguous(), self.W["fc"])
+        h = u.repeat(1, cfg.hc_count).contiguous()
+        return self.inner.step_from_h(h, ids, slots, positions, n_tok)
+
+    def logits(self, x):
+        return self.inner.logits(x)
+
+    def assign_blocks(self, slot, n_tokens, allocator):
+        self.inner.assign_blocks(slot, n_tokens, allocator)
+
+    def reset_slot(self, slot):
+        self.inner.reset_slot(slot)

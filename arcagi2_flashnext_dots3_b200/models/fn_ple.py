@@ -86,7 +86,7 @@ def apply(model, h, emb, p, ring, slots, positions, n_tok):
     gv = (torch.sigmoid(gate) * val[:, None, :]).reshape(T, hc * H)
     gvn = _rms1p(gv, p["nc"], cfg.rms_eps, H)
     kc = p["conv"].shape[1]
-    R = (kc - 1) * d
+    R = ring.shape[1]
     pos = positions.long()
     for t in range(T):
         b, j = divmod(t, n_tok)

@@ -81,16 +81,17 @@ def hc_residual(h: torch.Tensor, y: torch.Tensor, inj: torch.Tensor) -> None:
 # --------------------------------------------------------------------------------------- Gated DeltaNet
 def gdn_step(proj: torch.Tensor, conv_w: torch.Tensor, conv_state: torch.Tensor, ssm: torch.Tensor,
              A_log: torch.Tensor, dt_bias: torch.Tensor, norm_w: torch.Tensor, slots: torch.Tensor, cfg,
-             n_tok: int = 1) -> torch.Tensor:
+             n_tok: int = 1, n_commit: torch.Tensor = None) -> torch.Tensor:
     """Gated DeltaNet over `n_tok` consecutive tokens of each sequence (rows of proj are grouped per sequence:
     row = seq * n_tok + j). proj [rows, C + nv*dv + 2*nv] fp32 holds [qkv | z | b | a]. Updates conv_state
     [S, C, kc-1] and ssm [S, nv, dk, dv] (fp32 or bf16) of `slots` in place and returns the gated-normed output
-    [rows, nv*dv] (act). Math: student_fn.py:251-293 (fla gated delta rule, qk l2norm, scale dk^-0.5)."""
+    [rows, nv*dv] (act). Math: student_fn.py:251-293 (fla gated delta rule, qk l2norm, scale dk^-0.5).
+    ``n_commit`` (int32 [B]): write back only the states after the first n_commit[b] tokens (speculative verify)."""
     if _cuda(proj):
         out = torch.empty(proj.shape[0], cfg.lin_v_heads * cfg.lin_v_dim, dtype=torch.float16, device=proj.device)
         native.C().gdn_step(proj, conv_w, conv_state, ssm, A_log, dt_bias, norm_w, slots, out, cfg.lin_k_heads,
                             cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim, n_tok, cfg.rms_eps,
-                            1 if cfg.gdn_gate == "sigmoid" else 0)
+                            1 if cfg.gdn_gate == "sigmoid" else 0, n_commit)
         return out
     nk, nv, dk, dv = cfg.lin_k_heads, cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim
     C = 2 * nk * dk + nv * dv
@@ -105,7 +106,9 @@ def gdn_step(proj: torch.Tensor, conv_w: torch.Tensor, conv_state: torch.Tensor,
         qkv, z, bb, aa = P.split([C, nv * dv, nv, nv], -1)
         hist = torch.cat([conv_state[s].float(), qkv.t()], 1)              # [C, kc-1+n]
         conv = torch.stack([(hist[:, j:j + kc] * conv_w.view(C, kc)).sum(-1) for j in range(n_tok)], 0)
-        conv_state[s] = hist[:, -(kc - 1):].to(conv_state.dtype)
+        m = n_tok if n_commit is None else int(n_commit[b])
+        if m > 0:
+            conv_state[s] = hist[:, m:m + kc - 1].to(conv_state.dtype)
         x = F.silu(conv)
         q, k, v = x.split([nk * dk, nk * dk, nv * dv], -1)
         q = q.view(n_tok, nk, dk).repeat_interleave(r, 1)
@@ -123,7 +126,8 @@ def gdn_step(proj: torch.Tensor, conv_w: torch.Tensor, conv_state: torch.Tensor,
             u = beta[j][:, None] * (v[j] - kv)
             S = S + k[j][:, :, None] * u[:, None, :]
             o[j] = torch.einsum("hkv,hk->hv", S, q[j])
-        ssm[s] = S.to(ssm.dtype)
+            if j + 1 == m:
+                ssm[s] = S.to(ssm.dtype)
         o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + cfg.rms_eps) * norm_w.float()
         zz = z.view(n_tok, nv, dv)
         o = o * (torch.sigmoid(zz) if cfg.gdn_gate == "sigmoid" else F.silu(zz))
@@ -191,11 +195,12 @@ def qsa_prep(proj, qn, kn, iqn, ikn, rope, k_cache, v_cache, block_table, slots,
         blk = int(block_table[s, p // bs])
         k_cache[blk, p % bs] = k[row].to(k_cache.dtype)
         v_cache[blk, p % bs] = v[row].to(v_cache.dtype)
-        kr_ring[s, p % r] = kr[row].to(kr_ring.dtype)
+        RL = kr_ring.shape[1]
+        kr_ring[s, p % RL] = kr[row].to(kr_ring.dtype)
         if (p + 1) % r == 0:
             cb = (p + 1) // r - 1
-            kb = _rms1p(kr_ring[s].float().mean(0), ikn, cfg.rms_eps)
             st = cb * r
+            kb = _rms1p(kr_ring[s, [q % RL for q in range(st, p + 1)]].float().mean(0), ikn, cfg.rms_eps)
             comp_cache[s, cb] = _rope(kb, (rope[0][st], rope[1][st])).to(comp_cache.dtype)
     return q, gate, iq
 
