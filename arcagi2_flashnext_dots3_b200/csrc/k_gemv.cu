@@ -1,0 +1,298 @@
+// Grouped low-bit GEMV for decode-sized expert groups (at most 8 tokens per item), W4/3/2 x A8.
+//
+// With a handful of tokens per expert the MoE projections are matrix-vector products bound by the weight stream;
+// a tensor-core tile of 16+ tokens is mostly padding there. This kernel keeps the weight stream at HBM speed on
+// CUDA cores by spending about one integer instruction per weight:
+//
+//   * activations are quantized once per row and 128-column group to int8 (scale = absmax / 127) by
+//     `gemv_quant`, which also stores the group sums of the codes;
+//   * each thread owns one weight row of a 128-row tile and streams that row's code words from HBM (word i of
+//     row r at (i * 128 + r) * 4: a warp reads 128 contiguous bytes);
+//   * codes are moved into byte lanes in natural column order with shift / mask / byte-permute and multiplied
+//     with the int8 activations by `dp4a` (4 products per instruction), exact in int32;
+//   * per (row, group): y += s_w * s_x * (sum q*x - z * sum x) in fp32.
+//
+// The activation quantization is the one numerics change against fp16 activations (per-group int8, the same
+// family as the reference's per-token-group FP8 activation quantization of its dense W8A8 GEMMs,
+// dotsnote/engine/arcstats_pkg/arcstats/w8a8_ws.py:13-44).
+//
+// Epilogues: fp32 store (optionally to per-row destination addresses, the expert-parallel combine) and
+// silu(gate) * up in the silu-pair row order (tile t = 64 gate rows then the 64 matching up rows) as fp16.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_fp16.h>
+#include "wgemm.h"
+
+namespace {
+
+#define STREAM at::cuda::getCurrentCUDAStream()
+constexpr int kMaxTok = 8;
+constexpr int kMaxK = 2560;   // activation row length staged in shared memory (int8)
+
+// ------------------------------------------------------------------------------------ activation quantization
+// One warp per (row, 128-column group): lane l owns columns 4l..4l+3.
+__global__ void gemv_quant_kernel(const __half* x, int rows, int K, int8_t* xq, float* xs, int* xsum) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int G = K / 128;
+  if (warp >= rows * G) return;
+  const int r = warp / G, g = warp % G;
+  const __half2* src = reinterpret_cast<const __half2*>(x + (int64_t)r * K + g * 128) + 2 * lane;
+  const float2 a = __half22float2(src[0]), b = __half22float2(src[1]);
+  float m = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y)));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float s = m / 127.f;
+  const float inv = m > 0.f ? 127.f / m : 0.f;
+  const int q0 = __float2int_rn(a.x * inv), q1 = __float2int_rn(a.y * inv);
+  const int q2 = __float2int_rn(b.x * inv), q3 = __float2int_rn(b.y * inv);
+  reinterpret_cast<uint32_t*>(xq + (int64_t)r * K + g * 128)[lane] =
+      (uint32_t)(q0 & 255) | ((uint32_t)(q1 & 255) << 8) | ((uint32_t)(q2 & 255) << 16) | ((uint32_t)(q3 & 255) << 24);
+  int sum = q0 + q1 + q2 + q3;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0) {
+    xs[(int64_t)r * G + g] = s;
+    xsum[(int64_t)r * G + g] = sum;
+  }
+}
+
+// ------------------------------------------------------------------------------------ code extraction
+// quad<FMT>(w, m): codes of block-row columns 4m..4m+3 as bytes in natural order (m = 0..31, compile-time).
+template <int FMT, int M>
+__device__ __forceinline__ uint32_t quad(const uint32_t* w) {
+  if constexpr (FMT == 4) {
+    // word i = columns 8i..8i+7: pairs 4i+k in bits 4k (even col) and 16+4k (odd col)
+    const uint32_t x = w[M / 2];
+    const uint32_t A = x & 0x0F0F0F0Fu;          // [c0, c4, c1, c5]
+    const uint32_t B = (x >> 4) & 0x0F0F0F0Fu;   // [c2, c6, c3, c7]
+    return (M & 1) ? __byte_perm(A, B, 0x7531) : __byte_perm(A, B, 0x6420);
+  } else {
+    // pairs in bits BITS*k (even col) and 16+BITS*k (odd col), PPW pairs per word
+    constexpr int BITS = FMT, PPW = FMT == 3 ? 5 : 8;
+    constexpr uint32_t MASK = ((1u << BITS) - 1u) * 0x00010001u;
+    constexpr int p0 = 2 * M, p1 = 2 * M + 1;
+    const uint32_t P0 = (w[p0 / PPW] >> (BITS * (p0 % PPW))) & MASK;   // [c_{2p0}, 0, c_{2p0+1}, 0]
+    const uint32_t P1 = (w[p1 / PPW] >> (BITS * (p1 % PPW))) & MASK;
+    return __byte_perm(P0, P1, 0x6420);
+  }
+}
+
+template <int FMT>
+struct NWords {
+  static constexpr int value = FMT == 4 ? 16 : FMT == 3 ? 13 : 8;
+};
+
+// dot[t] += sum over the 128 columns of group g of codes * x[t] for NT tokens (activations from shared memory,
+// 16 bytes = 4 quads per load, the same address for every thread: a broadcast).
+template <int FMT, int NT, int M4>
+__device__ __forceinline__ void dot_quads(const uint32_t* cw, const int4* xg, int row_stride4, int* dot) {
+  const uint32_t q0 = quad<FMT, 4 * M4>(cw), q1 = quad<FMT, 4 * M4 + 1>(cw);
+  const uint32_t q2 = quad<FMT, 4 * M4 + 2>(cw), q3 = quad<FMT, 4 * M4 + 3>(cw);
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    const int4 x = xg[t * row_stride4 + M4];
+    dot[t] = __dp4a((int)q0, x.x, dot[t]);
+    dot[t] = __dp4a((int)q1, x.y, dot[t]);
+    dot[t] = __dp4a((int)q2, x.z, dot[t]);
+    dot[t] = __dp4a((int)q3, x.w, dot[t]);
+  }
+  if constexpr (M4 + 1 < 8) dot_quads<FMT, NT, M4 + 1>(cw, xg, row_stride4, dot);
+}
+
+// ------------------------------------------------------------------------------------ grouped GEMV
+struct GemvArgs {
+  const uint8_t* wbase;
+  const int64_t* exp_off;
+  const int8_t* exp_fmt;
+  int row_tiles, kg;
+  const int4* items;
+  const int* n_items;
+  int max_items;
+  const int8_t* xq;      // [rows, K] int8 activations
+  const float* xs;       // [rows, K/128] scales
+  const int* xsum;       // [rows, K/128] code sums
+  void* out;
+  int out_ld, out_cols;
+  int epi;
+  const int64_t* row_dst;
+};
+
+template <int FMT, int NT>
+__device__ __forceinline__ void run_item(const GemvArgs& a, int e, int t0, int n, int tile, const int* xsm,
+                                         const float* xs_sm, const int* xsum_sm, float* gsh) {
+  const int r = threadIdx.x;
+  const uint32_t bb = fw::wgemm_block_bytes(FMT);
+  constexpr int NW = NWords<FMT>::value;
+  const uint8_t* base = a.wbase + a.exp_off[e] + (int64_t)tile * a.kg * bb;
+  const int G = a.kg, Kw4 = a.kg * 8;  // int4 (16-byte) units of one activation row
+  const int4* x4 = reinterpret_cast<const int4*>(xsm);
+  float acc[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+  // software pipeline: the words, scale and zero of group g + 1 are in flight while group g is multiplied
+  uint32_t w[NW];
+  const uint32_t* wp = reinterpret_cast<const uint32_t*>(base);
+#pragma unroll
+  for (int i = 0; i < NW; ++i) w[i] = __ldg(wp + i * 128 + r);
+  unsigned short sb = __ldg(reinterpret_cast<const unsigned short*>(base + NW * 512) + r);
+  int z = __ldg(base + NW * 512 + 256 + r);
+  for (int g = 0; g < G; ++g) {
+    uint32_t cw[NW];
+#pragma unroll
+    for (int i = 0; i < NW; ++i) cw[i] = w[i];
+    const float s = __half2float(__ushort_as_half(sb));
+    const int zc = z;
+    if (g + 1 < G) {
+      const uint8_t* nb = base + (int64_t)(g + 1) * bb;
+      const uint32_t* nwp = reinterpret_cast<const uint32_t*>(nb);
+#pragma unroll
+      for (int i = 0; i < NW; ++i) w[i] = __ldg(nwp + i * 128 + r);
+      sb = __ldg(reinterpret_cast<const unsigned short*>(nb + NW * 512) + r);
+      z = __ldg(nb + NW * 512 + 256 + r);
+    }
+    int dot[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) dot[t] = 0;
+    dot_quads<FMT, NT, 0>(cw, x4 + g * 8, Kw4, dot);
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+      acc[t] = fmaf(s * xs_sm[t * G + g], (float)(dot[t] - zc * xsum_sm[t * G + g]), acc[t]);
+  }
+  const int row = tile * 128 + r;
+  if (a.epi == 0) {
+    if (row < a.out_cols) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        if (t < n) {
+          float* dst = a.row_dst ? reinterpret_cast<float*>(a.row_dst[t0 + t])
+                                 : reinterpret_cast<float*>(a.out) + (int64_t)(t0 + t) * a.out_ld;
+          dst[row] = acc[t];
+        }
+      }
+    }
+  } else {
+    __syncthreads();
+    if (r >= 64) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t) gsh[t * 64 + (r - 64)] = acc[t];
+    }
+    __syncthreads();
+    if (r < 64) {
+      const int f = tile * 64 + r;
+      if (f < a.out_cols) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          if (t < n) {
+            const float gt = acc[t], up = gsh[t * 64 + r];
+            reinterpret_cast<__half*>(a.out)[(int64_t)(t0 + t) * a.out_ld + f] =
+                __float2half_rn(gt / (1.f + __expf(-gt)) * up);
+          }
+        }
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(128, 5) gemv_grouped_kernel(GemvArgs a) {
+  extern __shared__ int xsm[];   // [kMaxTok][K/4] int8x4 activations of the current item
+  __shared__ float gsh[kMaxTok * 64];
+  __shared__ float xs_sm[kMaxTok * (kMaxK / 128)];
+  __shared__ int xsum_sm[kMaxTok * (kMaxK / 128)];
+  const int n_items = min(*a.n_items, a.max_items);
+  const int total = n_items * a.row_tiles;
+  const int Kw = a.kg * 32;
+  int staged = -1;
+  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    const int item = w / a.row_tiles, tile = w % a.row_tiles;
+    const int4 it = a.items[item];
+    const int e = it.x, t0 = it.y, n = min(it.z, kMaxTok);
+    if (n <= 0) continue;
+    if (staged != item) {
+      __syncthreads();
+      const int4* src = reinterpret_cast<const int4*>(a.xq + (int64_t)t0 * Kw * 4);
+      int4* dst = reinterpret_cast<int4*>(xsm);
+      for (int i = threadIdx.x; i < n * Kw / 4; i += blockDim.x) dst[i] = src[i];
+      for (int i = threadIdx.x; i < n * a.kg; i += blockDim.x) {
+        xs_sm[i] = a.xs[(int64_t)t0 * a.kg + i];
+        xsum_sm[i] = a.xsum[(int64_t)t0 * a.kg + i];
+      }
+      __syncthreads();
+      staged = item;
+    }
+    const int fmt = a.exp_fmt[e];
+#define FW_GEMV_NT(F)                                                                           \
+  if (n <= 1) run_item<F, 1>(a, e, t0, n, tile, xsm, xs_sm, xsum_sm, gsh);                      \
+  else if (n <= 2) run_item<F, 2>(a, e, t0, n, tile, xsm, xs_sm, xsum_sm, gsh);                 \
+  else if (n <= 4) run_item<F, 4>(a, e, t0, n, tile, xsm, xs_sm, xsum_sm, gsh);                 \
+  else run_item<F, 8>(a, e, t0, n, tile, xsm, xs_sm, xsum_sm, gsh);
+    if (fmt == 4) {
+      FW_GEMV_NT(4)
+    } else if (fmt == 3) {
+      FW_GEMV_NT(3)
+    } else if (fmt == 2) {
+      FW_GEMV_NT(2)
+    }
+#undef FW_GEMV_NT
+  }
+}
+
+void gemv_quant(torch::Tensor x, torch::Tensor xq, torch::Tensor xs, torch::Tensor xsum) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kHalf && x.is_contiguous() && x.size(1) % 128 == 0, "x fp16");
+  const int rows = x.size(0), K = x.size(1);
+  TORCH_CHECK(xq.scalar_type() == torch::kInt8 && xq.numel() >= (int64_t)rows * K, "xq int8");
+  TORCH_CHECK(xs.numel() >= (int64_t)rows * (K / 128) && xsum.numel() >= (int64_t)rows * (K / 128), "xs/xsum");
+  const int64_t warps = (int64_t)rows * (K / 128);
+  if (warps)
+    gemv_quant_kernel<<<(warps * 32 + 255) / 256, 256, 0, STREAM>>>(
+        reinterpret_cast<const __half*>(x.data_ptr()), rows, K, xq.data_ptr<int8_t>(), xs.data_ptr<float>(),
+        xsum.data_ptr<int>());
+}
+
+void gemv_grouped(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, int64_t row_tiles, int64_t kg,
+                  torch::Tensor items, torch::Tensor n_items, int64_t max_items, torch::Tensor xq, torch::Tensor xs,
+                  torch::Tensor xsum, torch::Tensor out, int64_t out_cols, int64_t epi,
+                  c10::optional<torch::Tensor> row_dst) {
+  TORCH_CHECK(xq.is_cuda() && xq.scalar_type() == torch::kInt8 && xq.size(1) == kg * 128, "xq int8 [rows, K]");
+  TORCH_CHECK(kg * 128 <= kMaxK, "K too large for the staged activations");
+  TORCH_CHECK(items.scalar_type() == torch::kInt32 && items.size(1) == 4, "items int32 [n, 4]");
+  TORCH_CHECK(epi == 0 ? out.scalar_type() == torch::kFloat : out.scalar_type() == torch::kHalf, "out dtype");
+  TORCH_CHECK(out.is_contiguous(), "out contiguous");
+  const c10::cuda::CUDAGuard guard(xq.device());
+  GemvArgs a{};
+  a.wbase = wbase.data_ptr<uint8_t>();
+  a.exp_off = exp_off.data_ptr<int64_t>();
+  a.exp_fmt = exp_fmt.data_ptr<int8_t>();
+  a.row_tiles = row_tiles;
+  a.kg = kg;
+  a.items = reinterpret_cast<const int4*>(items.data_ptr<int32_t>());
+  a.n_items = n_items.data_ptr<int32_t>();
+  a.max_items = max_items;
+  a.xq = xq.data_ptr<int8_t>();
+  a.xs = xs.data_ptr<float>();
+  a.xsum = xsum.data_ptr<int>();
+  a.out = out.data_ptr();
+  a.out_ld = out.size(1);
+  a.out_cols = out_cols;
+  a.epi = epi;
+  a.row_dst = row_dst ? row_dst->data_ptr<int64_t>() : nullptr;
+  int dev, sms;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const size_t smem = (size_t)kMaxTok * kg * 128;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(gemv_grouped_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxTok * kMaxK);
+    attr = true;
+  }
+  const int64_t work = max_items * row_tiles;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(work, (int64_t)sms * 12));
+  gemv_grouped_kernel<<<grid, 128, smem, STREAM>>>(a);
+}
+
+}  // namespace
+
+void register_gemv(pybind11::module& m) {
+  m.def("gemv_quant", &gemv_quant);
+  m.def("gemv_grouped", &gemv_grouped);
+}

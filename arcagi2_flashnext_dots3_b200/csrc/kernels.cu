@@ -10,6 +10,7 @@ void register_train(pybind11::module& m);
 void register_d3(pybind11::module& m);
 void register_sample(pybind11::module& m);
 void register_ple(pybind11::module& m);
+void register_gemv(pybind11::module& m);
 
 void register_kernels(pybind11::module& m) {
   register_fn(m);
@@ -18,4 +19,5 @@ void register_kernels(pybind11::module& m) {
   register_d3(m);
   register_sample(m);
   register_ple(m);
+  register_gemv(m);
 }

@@ -59,8 +59,15 @@ def bench_moe(args):
     t_gu = _time(lambda: wgemm.grouped(xs, gu, items, n_items, max_items, act, epi=wgemm.EPI_SILU_MUL,
                                        n_tile=n_tile), args.reps)
     t_d = _time(lambda: wgemm.grouped(act, d, items, n_items, max_items, yp, n_tile=n_tile), args.reps)
+    # CUDA-core grouped GEMV on a plan of <= 8 tokens per item
+    mi8 = (P + 7) // 8 + E
+    pp8, items8, n8 = ops.moe_plan(ids, E, 8, mi8)
+    xs8 = ops.moe_scatter(x, pp8)
+    t_gu8 = _time(lambda: wgemm.gemv_grouped(xs8, gu, items8, n8, mi8, act, epi=wgemm.EPI_SILU_MUL), args.reps)
+    t_d8 = _time(lambda: wgemm.gemv_grouped(act, d, items8, n8, mi8, yp), args.reps)
     native.check_error()
-    for name, t, b in (("moe_gate_up", t_gu, bytes_gu), ("moe_down", t_d, bytes_d)):
+    for name, t, b in (("moe_gate_up", t_gu, bytes_gu), ("moe_down", t_d, bytes_d),
+                       ("moe_gate_up_gemv", t_gu8, bytes_gu), ("moe_down_gemv", t_d8, bytes_d)):
         print(json.dumps({"case": name, "tokens": T, "experts": E, "touched": len(touched), "n_tile": n_tile,
                           "ms": round(t, 4), "MB": round(b / 1e6, 1), "GBps": round(b / t / 1e6, 1)}))
 

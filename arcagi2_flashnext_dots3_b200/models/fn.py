@@ -15,6 +15,7 @@ the last `ratio` raw indexer keys, GDN conv and recurrent states, PLE conv histo
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import torch
@@ -22,6 +23,8 @@ import torch
 from ..ops import fn_ops as ops
 from ..ops import wgemm
 from .fn_weights import rank_pad
+
+GEMV_MOE = os.environ.get("FW_MOE_GEMV", "1") != "0"   # decode MoE on the CUDA-core grouped GEMV
 
 
 # Extra entries of the position-indexed rings (indexer raw keys, PLE values): speculative verification writes up to
@@ -173,14 +176,19 @@ class FNModel:
         logits = self._mm(x, p["router"])
         ids, w = ops.moe_route(logits, E, cfg.top_k)
         P = T * cfg.top_k
-        n_tile = wgemm.pick_n_tile(max(1, (2 * P) // E)) if x.is_cuda else 16
+        gemv = x.is_cuda and GEMV_MOE and P <= 4 * E   # decode: a few tokens per expert -> CUDA-core GEMV
+        n_tile = wgemm.GEMV_MAX_TOK if gemv else (wgemm.pick_n_tile(max(1, (2 * P) // E)) if x.is_cuda else 16)
         max_items = (P + n_tile - 1) // n_tile + E
         pair_pos, items, n_items = ops.moe_plan(ids, E, n_tile, max_items)
         xs = ops.moe_scatter(x, pair_pos)
         act = torch.empty(P, cfg.moe_inter, dtype=self.act, device=x.device)
-        wgemm.grouped(xs, p["gu"], items, n_items, max_items, act, epi=wgemm.EPI_SILU_MUL, n_tile=n_tile)
         ypair = torch.empty(P, cfg.hidden_size, dtype=torch.float32, device=x.device)
-        wgemm.grouped(act, p["d"], items, n_items, max_items, ypair, n_tile=n_tile)
+        if gemv:
+            wgemm.gemv_grouped(xs, p["gu"], items, n_items, max_items, act, epi=wgemm.EPI_SILU_MUL)
+            wgemm.gemv_grouped(act, p["d"], items, n_items, max_items, ypair)
+        else:
+            wgemm.grouped(xs, p["gu"], items, n_items, max_items, act, epi=wgemm.EPI_SILU_MUL, n_tile=n_tile)
+            wgemm.grouped(act, p["d"], items, n_items, max_items, ypair, n_tile=n_tile)
         sact = self._mm(x, p["sgu"], epi=wgemm.EPI_SILU_MUL, out_dtype=self.act)
         ysh = self._mm(sact, p["sd"])
         ops.moe_combine(h, ypair, pair_pos, w, ysh, logits[:, E], inj)

@@ -158,6 +158,29 @@ def grouped(xs16: torch.Tensor, ws: WeightSet, items: torch.Tensor, n_items: tor
     return out
 
 
+GEMV_MAX_TOK = 8  # items of at most this many tokens can run on the CUDA-core grouped GEMV (csrc/k_gemv.cu)
+
+
+def gemv_grouped(xs16: torch.Tensor, ws: WeightSet, items: torch.Tensor, n_items: torch.Tensor, max_items: int,
+                 out: torch.Tensor, epi: int = EPI_STORE, row_dst: torch.Tensor = None) -> torch.Tensor:
+    """Same contract as :func:`grouped` for plans built with n_tile <= 8 (decode-sized expert groups): activations
+    are quantized to int8 per 128-column group, then every item (expert, first row, count <= 8) is computed by
+    integer dot products straight from the packed codes (csrc/k_gemv.cu)."""
+    cols = ws.rows // 2 if epi == EPI_SILU_MUL else ws.rows
+    if not xs16.is_cuda:
+        return grouped(xs16, ws, items, n_items, max_items, out, epi=epi, row_dst=row_dst)
+    if any(f > 4 for f in ws.fmts):
+        raise ValueError("the grouped GEMV handles 2/3/4-bit experts only")
+    R, K = xs16.shape
+    xq = torch.empty(R, K, dtype=torch.int8, device=xs16.device)
+    xsc = torch.empty(R, K // 128, dtype=torch.float32, device=xs16.device)
+    xsum = torch.empty(R, K // 128, dtype=torch.int32, device=xs16.device)
+    native.C().gemv_quant(xs16, xq, xsc, xsum)
+    native.C().gemv_grouped(ws.blob, ws.exp_off, ws.exp_fmt, ws.row_tiles, ws.kg, items, n_items, max_items, xq, xsc,
+                            xsum, out, cols, epi, row_dst)
+    return out
+
+
 def _ref_apply(y: torch.Tensor, epi: int) -> torch.Tensor:
     if epi == EPI_STORE:
         return y

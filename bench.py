@@ -234,7 +234,10 @@ def main():
                        "l2": "inputs larger than L2 (weights streamed per step >> 126 MB)",
                        "ple": f"layers {list(cfg.ple_layers)}, {cfg.ple_rows // 10**6}M x {cfg.ple_dim} fp8 n-gram table",
                        "mtp": "off (no speculative decoding in this measurement)",
-                       "compute": "fp16 tensor-core MMA, fp32 accumulate; activations fp16/fp32",
+                       "compute": ("dense projections: fp16 tcgen05 MMA, fp32 accumulate; decode MoE experts: "
+                                   "4/3-bit codes x int8 activations (per 128-column group) on dp4a, fp32 "
+                                   "accumulate" if os.environ.get("FW_MOE_GEMV", "1") != "0" else
+                                   "fp16 tcgen05 MMA, fp32 accumulate; activations fp16/fp32"),
                        "valid": not args.layers},
             "p50_tpot_ms": round(p50, 3),
             "clocks": clk,

@@ -126,3 +126,44 @@ def test_split_k_silu_epilogue():
     y = wgemm.matmul(x.cuda(), ws, epi=wgemm.EPI_SILU_MUL, out_dtype=torch.float32, k_splits=8)
     torch.cuda.synchronize()
     assert torch.allclose(y.cpu(), ref, atol=3e-3, rtol=3e-3)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("epi", [0, 1])
+def test_gemv_grouped_matches_reference(epi):
+    """CUDA-core grouped GEMV (<= 8 tokens per item) on mixed 4/3/2-bit experts against the torch reference
+    (same items, same blocks), store and silu*up epilogues, plus per-row destinations."""
+    from arcagi2_flashnext_dots3_b200.formats import lowbit_file
+    from arcagi2_flashnext_dots3_b200.formats import runtime as rt
+    from arcagi2_flashnext_dots3_b200.ops import fn_ops, wgemm
+    g = torch.Generator().manual_seed(3)
+    E, H, I = 6, 384, 256
+    lay = lowbit_file.random_layer(E, H, I, [4, 3, 2, 4, 3, 4], g, symmetric=False)
+    perm = rt.gate_up_perm(I)
+    if epi == 1:
+        blobs = [rt.pack_planar_blob(b.gu, b.gu_s, b.gu_z, b.bits, row_perm=perm) for b in lay.blobs]
+        ws = wgemm.build_weight_set(blobs, [b.bits for b in lay.blobs], 2 * I, H, silu_pairs=True, device="cuda")
+        K, cols = H, I
+    else:
+        blobs = [rt.pack_planar_blob(b.d, b.d_s, b.d_z, b.bits) for b in lay.blobs]
+        ws = wgemm.build_weight_set(blobs, [b.bits for b in lay.blobs], H, I, device="cuda")
+        K, cols = I, H
+    T, k = 13, 3
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32).cuda()
+    P = T * k
+    pair_pos, items, n_items = fn_ops.moe_plan(ids, E, 8, P // 8 + E + 1)
+    xs = (torch.randn(P, K, generator=g) * 0.5).half().cuda()
+    out_g = torch.zeros(P, cols, dtype=torch.float16 if epi else torch.float32, device="cuda")
+    ref = wgemm.grouped(xs.float().cpu(), ws.to("cpu"), items.cpu(), n_items.cpu(), items.shape[0],
+                        torch.zeros(P, cols), epi=epi)
+    wgemm.gemv_grouped(xs, ws, items, n_items, items.shape[0], out_g, epi=epi)
+    torch.cuda.synchronize()
+    err = (out_g.float().cpu() - ref).abs().max() / ref.abs().max()
+    assert err < 2e-2, err  # int8 activations per 128-column group
+    if epi == 0:  # per-row destinations: rows land in a permuted buffer
+        dst = torch.zeros(P, cols, dtype=torch.float32, device="cuda")
+        perm_rows = torch.randperm(P, generator=g).cuda()
+        addr = dst.data_ptr() + perm_rows.long() * cols * 4
+        wgemm.gemv_grouped(xs, ws, items, n_items, items.shape[0], out_g, row_dst=addr)
+        torch.cuda.synchronize()
+        assert torch.allclose(dst[perm_rows].cpu(), out_g.cpu())
