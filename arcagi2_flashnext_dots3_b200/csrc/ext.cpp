@@ -92,7 +92,10 @@ void wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, in
   static const int ab_env = getenv("FW_WGEMM_AB") ? atoi(getenv("FW_WGEMM_AB")) : 0;
   // Pipeline shape: `teams` dequant teams take stages round-robin. Both ring depths must be multiples of the
   // team count (see the kernel's note on parity waits); pick the most teams that leave >= 2 weight stages.
-  const size_t budget = 232448;
+  // CTAs per SM: two smaller pipelines per SM overlap their stage hand-off latencies (FW_WGEMM_CPS overrides)
+  static const int cps_env = getenv("FW_WGEMM_CPS") ? atoi(getenv("FW_WGEMM_CPS")) : 0;
+  const int cps = cps_env > 0 ? std::min(cps_env, 4) : 1;
+  const size_t budget = (232448 / cps) & ~(size_t)1023;
   int teams = 0, ab_stages = 0, w_stages = 0;
   for (int t = fw::kWgemmMaxTeams; t >= 1 && !teams; --t) {
     int P = ab_env > 0 ? ab_env : t;
@@ -117,7 +120,8 @@ void wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, in
   int ks = 1;
   if (dense_T >= 0) {
     const int64_t base = ((dense_T + n_tile - 1) / n_tile) * row_tiles;
-    if (base < sm_count()) ks = (int)std::min<int64_t>({kg, 16, (3 * sm_count() / 2 + base - 1) / base});
+    if (base < sm_count() * cps)
+      ks = (int)std::min<int64_t>({kg, 16, (3 * sm_count() * cps / 2 + base - 1) / base});
     if (k_splits > 0) ks = (int)std::min<int64_t>(k_splits, kg);
   }
   a.k_splits = ks;
@@ -134,7 +138,7 @@ void wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, in
   TORCH_CHECK(rc == 0, "cuTensorMapEncodeTiled failed: ", rc);
   const int64_t work = (dense_T >= 0 ? (dense_T + n_tile - 1) / n_tile : max_items) * row_tiles * ks;
   if (work <= 0) return;
-  const int grid = (int)std::min<int64_t>(sm_count(), work);
+  const int grid = (int)std::min<int64_t>((int64_t)sm_count() * cps, work);
   rc = fw::wgemm_launch(a, bmap, grid, at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(rc == 0, "wgemm launch failed: ", cudaGetErrorString((cudaError_t)rc));
 }

@@ -13,6 +13,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 #include <cfloat>
+#include <type_traits>
 #include <atomic>
 #include <cub/block/block_scan.cuh>
 #include "kernels.h"
@@ -82,6 +83,17 @@ __device__ __forceinline__ void load8f(const __nv_fp8_e4m3* p, float (&o)[8]) {
     }
   }
 }
+// 8 e4m3 values held in a uint2 -> 8 floats (pairs converted by the hardware e4m3x2 -> f16x2 conversion)
+__device__ __forceinline__ void fp8x8_to_f32(const uint2 raw, float (&o)[8]) {
+  const __nv_fp8x2_e4m3* p2 = reinterpret_cast<const __nv_fp8x2_e4m3*>(&raw);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = static_cast<float2>(p2[j]);
+    o[2 * j] = f.x;
+    o[2 * j + 1] = f.y;
+  }
+}
+
 __device__ __forceinline__ void load8f(const __nv_bfloat16* p, float (&o)[8]) {
   const uint4 u = *reinterpret_cast<const uint4*>(p);
   const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -125,6 +137,37 @@ void embed_hc(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t
 
 // ===================================================================================== hyper-connections
 // hn[t, s*H+i] = h * rsqrt(mean_s(h^2) + eps) * (1 + w[s*H+i]), one block per (token, stream).
+// One warp per (token, stream): the stream's H values stay in registers (float4 loads, H % 128 == 0, H <= 4096),
+// one pass over memory, no block barrier.
+template <int V4>
+__global__ void hc_prenorm_warp_kernel(const float* h, const float* w, __half* out, int H, int S, int rows, float eps) {
+  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (wid >= rows) return;
+  const int s = wid % S;
+  const float4* x = reinterpret_cast<const float4*>(h + (int64_t)wid * H);
+  const float4* ww = reinterpret_cast<const float4*>(w + (int64_t)s * H);
+  float4 v[V4];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < V4; ++j) {
+    const int i = lane + 32 * j;
+    v[j] = i < H / 4 ? x[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / H + eps);
+  __half2* o = reinterpret_cast<__half2*>(out + (int64_t)wid * H);
+#pragma unroll
+  for (int j = 0; j < V4; ++j) {
+    const int i = lane + 32 * j;
+    if (i < H / 4) {
+      const float4 a = ww[i];
+      o[2 * i] = __floats2half2_rn(v[j].x * r * (1.f + a.x), v[j].y * r * (1.f + a.y));
+      o[2 * i + 1] = __floats2half2_rn(v[j].z * r * (1.f + a.z), v[j].w * r * (1.f + a.w));
+    }
+  }
+}
+
 __global__ void hc_prenorm_kernel(const float* h, const float* w, __half* out, int H, float eps) {
   __shared__ float sh[32];
   const int t = blockIdx.x, s = blockIdx.y, S = gridDim.y;
@@ -142,6 +185,20 @@ void hc_prenorm(torch::Tensor h, torch::Tensor w, torch::Tensor out, int64_t H, 
   const int T = h.size(0);
   const int hc = h.size(1) / H;
   if (!T) return;
+  const int rows = T * hc;
+  if (H % 128 == 0 && H <= 4096) {
+    const int blocks = (rows * 32 + 255) / 256;
+    if (H <= 1024)
+      hc_prenorm_warp_kernel<8><<<blocks, 256, 0, STREAM>>>(h.data_ptr<float>(), w.data_ptr<float>(),
+                                                            (__half*)out.data_ptr(), H, hc, rows, (float)eps);
+    else if (H <= 2560)
+      hc_prenorm_warp_kernel<20><<<blocks, 256, 0, STREAM>>>(h.data_ptr<float>(), w.data_ptr<float>(),
+                                                             (__half*)out.data_ptr(), H, hc, rows, (float)eps);
+    else
+      hc_prenorm_warp_kernel<32><<<blocks, 256, 0, STREAM>>>(h.data_ptr<float>(), w.data_ptr<float>(),
+                                                             (__half*)out.data_ptr(), H, hc, rows, (float)eps);
+    return;
+  }
   hc_prenorm_kernel<<<dim3(T, hc), 256, 0, STREAM>>>(h.data_ptr<float>(), w.data_ptr<float>(),
                                                      (__half*)out.data_ptr(), H, (float)eps);
 }
@@ -838,6 +895,185 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float* q, const K
   }
 }
 
+// Split-K sparse GQA decode attention, version 2 (D = 128 or 256). A warp streams its keys 4 at a time with the
+// lanes spread over the head dimension (lane l owns dims [l*NI, l*NI+NI): every key and value row is one
+// coalesced 128/256-byte read), the G <= 8 query heads in registers. The 8 heads x 4 keys partial dot products
+// are reduced with a butterfly transpose-reduce (31 shuffles leave lane j with the full score of head j/4, key
+// j%4); each 4-lane group keeps the online-softmax state of its head, and the probabilities are broadcast back
+// for the P.V update of every lane's dims. Same partial-output contract as attn_split_kernel.
+template <typename KT, int D>
+__global__ void __launch_bounds__(128) attn_split_v2_kernel(const float* q, const KT* kc, const KT* vc,
+                                                            const int* block_table, int max_blocks, int bs,
+                                                            const int* slots, const int* positions, const int* sel,
+                                                            const int* sparse, int nblk, int r, int KV, int G,
+                                                            int n_tok, int n_split, float* part_o, float* part_ml) {
+  constexpr int NI = D / 32;
+  constexpr bool kPipe = std::is_same<KT, __nv_fp8_e4m3>::value && NI == 8;  // raw 8-byte prefetch path
+  extern __shared__ float sm[];
+  float* mrg = sm;                                            // [4 warps][8 heads][D + 2]
+  int* krow = reinterpret_cast<int*>(mrg + 4 * 8 * (D + 2));  // cache row of every key of this split
+  const int row = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  const int b = row / n_tok;
+  const int p = positions[b] + row % n_tok;
+  const int s = slots[b];
+  const int Hq = KV * G;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool is_sparse = sparse[row] != 0;
+  const int tail0 = ((p + 1) / r) * r;
+  const int n_keys = is_sparse ? nblk * r + (p + 1 - tail0) : p + 1;
+  const int per = (n_keys + n_split - 1) / n_split;
+  const int k0 = split * per, k1 = min(n_keys, k0 + per);
+  // prologue: resolve every key of the split to its cache row once (index-select + block table lookups)
+  for (int mk = k0 + threadIdx.x; mk < k1; mk += blockDim.x) {
+    int tok = mk;
+    if (is_sparse) tok = mk < nblk * r ? sel[(int64_t)row * nblk + mk / r] * r + mk % r : tail0 + (mk - nblk * r);
+    const int blk = block_table[(int64_t)s * max_blocks + tok / bs];
+    krow[mk - k0] = blk * bs + tok % bs;
+  }
+  const float scale = rsqrtf((float)D);
+  float qr[8][NI], acc[8][NI];
+#pragma unroll
+  for (int h = 0; h < 8; ++h)
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      qr[h][i] = h < G ? q[((int64_t)row * Hq + kvh * G + h) * D + lane * NI + i] * scale : 0.f;
+      acc[h][i] = 0.f;
+    }
+  __syncthreads();
+  float m_g = -FLT_MAX, l_g = 0.f;      // softmax state of head lane/4, kept by its 4-lane group
+  auto offset = [&](int mk) -> int64_t {
+    const int kr = krow[min(mk, k1 - 1) - k0];
+    return ((int64_t)kr * KV + kvh) * D + lane * NI;
+  };
+  uint2 kraw[4], vraw[4];
+  if constexpr (kPipe) {
+    const int c0 = k0 + warp * 4;
+    if (c0 < k1) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t o = offset(c0 + u);
+        kraw[u] = *reinterpret_cast<const uint2*>(kc + o);
+        vraw[u] = *reinterpret_cast<const uint2*>(vc + o);
+      }
+    }
+  }
+  // each warp takes every 4th chunk of 4 keys
+  for (int c0 = k0 + warp * 4; c0 < k1; c0 += 16) {
+    bool ok[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) ok[u] = c0 + u < k1;
+    float kf[4][NI], vf[4][NI];
+    if constexpr (kPipe) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        fp8x8_to_f32(kraw[u], kf[u]);
+        fp8x8_to_f32(vraw[u], vf[u]);
+      }
+      const int cn = c0 + 16;
+      if (cn < k1) {  // the next chunk's rows are in flight during this chunk's math
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t o = offset(cn + u);
+          kraw[u] = *reinterpret_cast<const uint2*>(kc + o);
+          vraw[u] = *reinterpret_cast<const uint2*>(vc + o);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t o = offset(c0 + u);
+        if constexpr (NI == 8) {
+          load8f(kc + o, kf[u]);
+          load8f(vc + o, vf[u]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < NI; ++i) {
+            kf[u][i] = ldf(&kc[o + i]);
+            vf[u][i] = ldf(&vc[o + i]);
+          }
+        }
+      }
+    }
+    // partial dots: v[h*4 + u]
+    float v[32];
+#pragma unroll
+    for (int h = 0; h < 8; ++h)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float d = 0.f;
+#pragma unroll
+        for (int i = 0; i < NI; ++i) d = fmaf(qr[h][i], kf[u][i], d);
+        v[h * 4 + u] = d;
+      }
+    // butterfly transpose-reduce: after the round with offset o the lane keeps the half selected by (lane & o)
+#pragma unroll
+    for (int o = 16, n = 16; o >= 1; o >>= 1, n >>= 1) {
+      const bool upper = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < n; ++i) {
+        const float send = upper ? v[i] : v[i + n];
+        const float keep = upper ? v[i + n] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+    }
+    const int hg = lane >> 2, ug = lane & 3;
+    const bool valid = ok[ug] && hg < G;
+    const float sc = valid ? v[0] : -FLT_MAX;
+    float cm = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 1));
+    cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
+    const float mn = fmaxf(m_g, cm);
+    const float pr = valid ? __expf(sc - mn) : 0.f;
+    const float corr = m_g == -FLT_MAX ? 0.f : __expf(m_g - mn);
+    float ps = pr + __shfl_xor_sync(0xffffffffu, pr, 1);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+    l_g = l_g * corr + ps;
+    m_g = mn;
+#pragma unroll
+    for (int h = 0; h < 8; ++h) {
+      const float ch = __shfl_sync(0xffffffffu, corr, 4 * h);
+#pragma unroll
+      for (int i = 0; i < NI; ++i) acc[h][i] *= ch;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float pk = __shfl_sync(0xffffffffu, pr, 4 * h + u);
+#pragma unroll
+        for (int i = 0; i < NI; ++i) acc[h][i] = fmaf(pk, vf[u][i], acc[h][i]);
+      }
+    }
+  }
+  float* mw = mrg + warp * 8 * (D + 2);
+#pragma unroll
+  for (int h = 0; h < 8; ++h) {
+#pragma unroll
+    for (int i = 0; i < NI; ++i) mw[h * (D + 2) + lane * NI + i] = acc[h][i];
+  }
+  if ((lane & 3) == 0) {
+    mw[(lane >> 2) * (D + 2) + D] = m_g;
+    mw[(lane >> 2) * (D + 2) + D + 1] = l_g;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int h = idx / D, d = idx % D;
+    float M = -FLT_MAX;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, mrg[(w * 8 + h) * (D + 2) + D]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float* mh = mrg + (w * 8 + h) * (D + 2);
+      const float f = mh[D] > -FLT_MAX ? __expf(mh[D] - M) : 0.f;
+      L += mh[D + 1] * f;
+      O += mh[d] * f;
+    }
+    const int64_t base = ((int64_t)row * Hq + kvh * G + h) * n_split + split;
+    part_o[base * D + d] = O;
+    if (d == 0) {
+      part_ml[base * 2] = M;
+      part_ml[base * 2 + 1] = L;
+    }
+  }
+}
+
 // Merge the splits of each (row, head) and apply the sigmoid output gate; out fp16 [rows, Hq*D].
 __global__ void attn_combine_kernel(const float* part_o, const float* part_ml, const float* gate, __half* out, int Hq,
                                     int D, int n_split) {
@@ -877,6 +1113,12 @@ void attn_decode(torch::Tensor q, torch::Tensor gate, torch::Tensor k_cache, tor
   auto part_ml = torch::empty({rows, Hq, n_split, 2}, q.options());
   const size_t sm = (8 * D + 4 * 8 * (D + 2)) * sizeof(float);
   dim3 grid(rows, KV, n_split);
+  static const bool attn_v2 = !(getenv("FW_ATTN_V1") && atoi(getenv("FW_ATTN_V1")));
+  // most keys one split can see (sparse: nblk*r selected + < r tail; dense only while fewer blocks are complete):
+  // every key index is resolved to its cache row in shared memory; fall back to v1 if that would not fit
+  const int64_t max_keys = std::min<int64_t>((int64_t)block_table.size(1) * k_cache.size(1), (int64_t)(nblk + 1) * r);
+  const int64_t max_per = (max_keys + n_split - 1) / n_split + 1;
+  const bool v2_fits = 4 * 8 * (D + 2) * 4 + max_per * 4 <= 100 * 1024;
 #define ATT(KT, DD)                                                                                                 \
   {                                                                                                                 \
     auto kern = attn_split_kernel<KT, DD>;                                                                         \
@@ -887,10 +1129,21 @@ void attn_decode(torch::Tensor q, torch::Tensor gate, torch::Tensor k_cache, tor
                                     sparse.data_ptr<int32_t>(), nblk, r, KV, G, n_tok, n_split,                    \
                                     part_o.data_ptr<float>(), part_ml.data_ptr<float>());                          \
   }
+#define ATT2(KT, DD)                                                                                                \
+  {                                                                                                                 \
+    auto kern = attn_split_v2_kernel<KT, DD>;                                                                      \
+    const size_t sm2 = 4 * 8 * (DD + 2) * sizeof(float) + (size_t)max_per * sizeof(int);                          \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);                          \
+    kern<<<grid, 128, sm2, STREAM>>>(q.data_ptr<float>(), (const KT*)k_cache.data_ptr(), (const KT*)v_cache.data_ptr(), \
+                                     block_table.data_ptr<int32_t>(), block_table.size(1), k_cache.size(1),         \
+                                     slots.data_ptr<int32_t>(), positions.data_ptr<int32_t>(), sel.data_ptr<int32_t>(), \
+                                     sparse.data_ptr<int32_t>(), nblk, r, KV, G, n_tok, n_split,                   \
+                                     part_o.data_ptr<float>(), part_ml.data_ptr<float>());                         \
+  }
 #define ATT_D(KT)            \
   if (D == 64) ATT(KT, 64)   \
-  else if (D == 128) ATT(KT, 128) \
-  else ATT(KT, 256)
+  else if (D == 128) { if (attn_v2 && v2_fits) ATT2(KT, 128) else ATT(KT, 128) } \
+  else { if (attn_v2 && v2_fits) ATT2(KT, 256) else ATT(KT, 256) }
   if (k_cache.scalar_type() == torch::kFloat8_e4m3fn) {
     ATT_D(__nv_fp8_e4m3)
   } else if (k_cache.scalar_type() == torch::kBFloat16) {
@@ -899,6 +1152,7 @@ void attn_decode(torch::Tensor q, torch::Tensor gate, torch::Tensor k_cache, tor
     ATT_D(float)
   }
 #undef ATT_D
+#undef ATT2
 #undef ATT
   attn_combine_kernel<<<dim3(rows, Hq), 128, 0, STREAM>>>(part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
                                                           gate.data_ptr<float>(), (__half*)out.data_ptr(), Hq, D,

@@ -84,10 +84,16 @@ def bench_dense(args):
         x = torch.randn(T, K, device=dev).half()
         out = torch.empty(T, R, device=dev)
         t = _time(lambda: wgemm.matmul(x, ws, out=out), args.reps)
-        t1 = _time(lambda: wgemm.matmul(x, ws, out=out, k_splits=1), args.reps)
         b = ws.nbytes()
-        print(json.dumps({"case": name, "rows": R, "K": K, "tokens": T, "ms": round(t, 4), "ms_no_split": round(t1, 4),
-                          "MB": round(b / 1e6, 2), "GBps": round(b / t / 1e6, 1)}))
+        sweep = {}
+        if args.sweep:
+            for nt in (16, 32, 64):
+                for ks in (1, 2, 4, 8, 16):
+                    if ks <= K // 128:
+                        sweep[f"n{nt}_k{ks}"] = round(1000 * _time(
+                            lambda: wgemm.matmul(x, ws, out=out, n_tile=nt, k_splits=ks), args.reps), 1)
+        print(json.dumps({"case": name, "rows": R, "K": K, "tokens": T, "ms": round(t, 4),
+                          "MB": round(b / 1e6, 2), "GBps": round(b / t / 1e6, 1), "sweep_us": sweep}))
     native.check_error()
 
 
@@ -156,6 +162,7 @@ def main():
     ap.add_argument("--experts", type=int, default=320)
     ap.add_argument("--ctx", type=int, default=9000)
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--sweep", action="store_true", help="dense: time every n_tile x split-K combination")
     args = ap.parse_args()
     cases = {"moe": bench_moe, "dense": bench_dense, "attn": bench_attn, "gdn": bench_gdn}
     for name, fn in cases.items():

@@ -25,6 +25,7 @@ from ..ops import wgemm
 from .fn_weights import rank_pad
 
 GEMV_MOE = os.environ.get("FW_MOE_GEMV", "1") != "0"   # decode MoE on the CUDA-core grouped GEMV
+SIDE_STREAM = os.environ.get("FW_SIDE_STREAM", "1") != "0"  # shared expert concurrent with the routed experts
 
 
 # Extra entries of the position-indexed rings (indexer raw keys, PLE values): speculative verification writes up to
@@ -174,6 +175,12 @@ class FNModel:
         T = x.shape[0]
         E = cfg.n_experts
         logits = self._mm(x, p["router"])
+        side = self._side_stream(x)
+        if side is not None:  # the shared expert runs concurrently with the routed experts (graph-capturable)
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                sact = self._mm(x, p["sgu"], epi=wgemm.EPI_SILU_MUL, out_dtype=self.act)
+                ysh = self._mm(sact, p["sd"])
         ids, w = ops.moe_route(logits, E, cfg.top_k)
         P = T * cfg.top_k
         gemv = x.is_cuda and GEMV_MOE and P <= 4 * E   # decode: a few tokens per expert -> CUDA-core GEMV
@@ -189,9 +196,21 @@ class FNModel:
         else:
             wgemm.grouped(xs, p["gu"], items, n_items, max_items, act, epi=wgemm.EPI_SILU_MUL, n_tile=n_tile)
             wgemm.grouped(act, p["d"], items, n_items, max_items, ypair, n_tile=n_tile)
-        sact = self._mm(x, p["sgu"], epi=wgemm.EPI_SILU_MUL, out_dtype=self.act)
-        ysh = self._mm(sact, p["sd"])
+        if side is not None:
+            torch.cuda.current_stream().wait_stream(side)
+            ysh.record_stream(torch.cuda.current_stream())
+            sact.record_stream(torch.cuda.current_stream())
+        else:
+            sact = self._mm(x, p["sgu"], epi=wgemm.EPI_SILU_MUL, out_dtype=self.act)
+            ysh = self._mm(sact, p["sd"])
         ops.moe_combine(h, ypair, pair_pos, w, ysh, logits[:, E], inj)
+
+    def _side_stream(self, x):
+        if not (x.is_cuda and SIDE_STREAM):
+            return None
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(device=x.device)
+        return self._side
 
     # ------------------------------------------------------------------------------------------- step
     def step(self, ids: torch.Tensor, slots: torch.Tensor, positions: torch.Tensor, n_tok: int = 1,
