@@ -88,6 +88,8 @@ void wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, in
   a.timeout_ns = (unsigned long long)timeout_ns;
   static const int dbg = getenv("FW_WGEMM_DBG") ? atoi(getenv("FW_WGEMM_DBG")) : 0;
   a.dbg = dbg;
+  static const int sleep_env = getenv("FW_WGEMM_SLEEP_NS") ? atoi(getenv("FW_WGEMM_SLEEP_NS")) : -1;
+  a.sleep_ns = sleep_env >= 0 ? (uint32_t)sleep_env : 20000u;
 
   static const int ab_env = getenv("FW_WGEMM_AB") ? atoi(getenv("FW_WGEMM_AB")) : 0;
   // Pipeline shape: `teams` dequant teams take stages round-robin. Both ring depths must be multiples of the

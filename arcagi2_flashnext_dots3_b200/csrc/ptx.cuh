@@ -90,14 +90,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
 // the thread until the phase completes (or ~20 us pass), so its polling does not take issue slots from the
 // dequant and MMA warps.
 __device__ __forceinline__ bool mbar_wait_sleepy(uint32_t bar, uint32_t parity, int* err, int code,
-                                                 volatile int* abort_flag, uint64_t limit_ns) {
+                                                 volatile int* abort_flag, uint64_t limit_ns,
+                                                 uint32_t hint_ns = 20000u) {
   uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {
     uint32_t ok;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(20000u)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
         : "memory");
     if (ok) return true;
     if (*abort_flag) return false;

@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t* src = a.wbase + a.exp_off[wk.e] + (size_t)wk.tile * a.kg * bb;
         for (int g = wk.g0; g < wk.g1; ++g, ++k) {
           const int s = k % S;
-          if (!mbar_wait_sleepy(bar_w_empty + 8 * s, ((k / S) & 1) ^ 1, err, 1001, abort_flag, lim)) break;
+          if (!mbar_wait_sleepy(bar_w_empty + 8 * s, ((k / S) & 1) ^ 1, err, 1001, abort_flag, lim, a.sleep_ns)) break;
           if (a.dbg & 8) {
             mbar_arrive(bar_w_full + 8 * s);
           } else {
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Work wk = decode_work(a, w, KS);
         for (int g = wk.g0; g < wk.g1; ++g, ++j) {
           const int p = j % P;
-          if (!mbar_wait_sleepy(bar_ab_empty + 8 * p, ((j / P) & 1) ^ 1, err, 2001, abort_flag, lim)) break;
+          if (!mbar_wait_sleepy(bar_ab_empty + 8 * p, ((j / P) & 1) ^ 1, err, 2001, abort_flag, lim, a.sleep_ns)) break;
           if (a.dbg & 16) {
             mbar_arrive(bar_b_full + 8 * p);
             continue;
@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = blockIdx.x; w < total && !*abort_flag; w += gridDim.x, ++it) {
       const Work wk = decode_work(a, w, KS);
       const int buf = it & 1;
-      if (!mbar_wait_sleepy(bar_acc_full + 8 * buf, (it >> 1) & 1, err, 5001, abort_flag, lim)) break;
+      if (!mbar_wait_sleepy(bar_acc_full + 8 * buf, (it >> 1) & 1, err, 5001, abort_flag, lim, a.sleep_ns)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * N;
       bool emit = !(a.dbg & 32);

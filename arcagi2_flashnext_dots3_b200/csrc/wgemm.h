@@ -71,6 +71,7 @@ struct WGemmArgs {
   // dequant stores, bit 3 = no weight bulk copies (the weight stage barrier is armed with 0 bytes).
   // Results are garbage when set.
   int dbg;
+  uint32_t sleep_ns;        // suspend-time hint of the off-critical-path barrier waits
 };
 
 int make_tmap_2d_f16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,

@@ -79,6 +79,8 @@ def bench_dense(args):
     shapes = [("hc_down", 388, 10240), ("hc_up", 10240, 384), ("gdn_proj", 16480, 2560), ("gdn_out", 2560, 6144),
               ("attn_proj", 11904, 2560), ("attn_o", 2560, 4096), ("router", 321, 2560), ("lm_head", 151936, 2560)]
     for name, R, K in shapes:
+        if args.only and name not in args.only.split(","):
+            continue
         wt = torch.randn(R, K, device=dev) * 0.02
         ws = wgemm.dense_fp8(wt)
         x = torch.randn(T, K, device=dev).half()
@@ -163,6 +165,7 @@ def main():
     ap.add_argument("--ctx", type=int, default=9000)
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--sweep", action="store_true", help="dense: time every n_tile x split-K combination")
+    ap.add_argument("--only", default="", help="dense: comma-separated case names")
     args = ap.parse_args()
     cases = {"moe": bench_moe, "dense": bench_dense, "attn": bench_attn, "gdn": bench_gdn}
     for name, fn in cases.items():

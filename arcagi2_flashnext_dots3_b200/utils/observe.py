@@ -1,0 +1,146 @@
+"""Observability: region tracing (CUDA events or wall clock, Chrome-trace export), MoE routing statistics and
+a memory census.
+
+Counterparts of the reference's CUDA-event timing around its attention kernels
+(dotsnote/engine/arcstats_pkg/arcstats/offload_cuda2.py:143-170), route-statistics ring buffers
+(flashnext/kaggle/code_dataset/fnext/moe/fnmoe.py:29-124 `_RouteStats`), its expert placement by routed load
+(`FN_EP_PLACE`, fnmoe.py:18-27) and its memory census / phase logging (arcstats/__init__.py:607-977).
+"""
+from __future__ import annotations
+
+import json
+import time
+from collections import defaultdict
+from contextlib import contextmanager
+
+import torch
+
+
+class Tracer:
+    """``with tracer.region("name"):`` records the region's duration (device time between CUDA events on the
+    current stream, or wall time on CPU). Nothing is synchronized until :meth:`summary` / :meth:`chrome`."""
+
+    def __init__(self, enabled: bool = True):
+        self.enabled = enabled
+        self.events = []          # (name, start_event_or_t, end_event_or_t, cuda, wall_start)
+
+    @contextmanager
+    def region(self, name: str, device=None):
+        if not self.enabled:
+            yield
+            return
+        cuda = torch.cuda.is_available() and (device is None or torch.device(device).type == "cuda")
+        w0 = time.perf_counter()
+        if cuda:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            yield
+            b.record()
+            self.events.append((name, a, b, True, w0))
+        else:
+            yield
+            self.events.append((name, w0, time.perf_counter(), False, w0))
+
+    def _durations(self):
+        if any(e[3] for e in self.events):
+            torch.cuda.synchronize()
+        out = []
+        for name, a, b, cuda, w0 in self.events:
+            ms = a.elapsed_time(b) if cuda else (b - a) * 1000
+            out.append((name, w0, ms))
+        return out
+
+    def summary(self) -> dict:
+        agg = defaultdict(lambda: [0, 0.0])
+        for name, _, ms in self._durations():
+            agg[name][0] += 1
+            agg[name][1] += ms
+        return {k: {"count": n, "total_ms": round(t, 4), "avg_ms": round(t / n, 4)} for k, (n, t) in agg.items()}
+
+    def chrome(self, path: str):
+        """Chrome trace (chrome://tracing, Perfetto): one complete event per region, start = host time."""
+        d = self._durations()
+        t0 = min((w for _, w, _ in d), default=0.0)
+        ev = [{"name": n, "ph": "X", "ts": (w - t0) * 1e6, "dur": ms * 1000, "pid": 0, "tid": 0} for n, w, ms in d]
+        with open(path, "w") as fh:
+            json.dump({"traceEvents": ev}, fh)
+
+
+class RouteStats:
+    """Per-layer expert hit counts accumulated on the device (one bincount per MoE call), with a window of recent
+    steps for load-aware decisions."""
+
+    def __init__(self, n_layers: int, n_experts: int, device, window: int = 64):
+        self.counts = torch.zeros(n_layers, n_experts, dtype=torch.int64, device=device)
+        self.window = window
+        self.recent = []
+        self.steps = 0
+
+    def add(self, layer: int, ids: torch.Tensor):
+        self.counts[layer] += torch.bincount(ids.reshape(-1).long(), minlength=self.counts.shape[1])
+
+    def end_step(self):
+        self.steps += 1
+        self.recent.append(self.counts.clone())
+        if len(self.recent) > self.window:
+            self.recent.pop(0)
+
+    def load(self) -> torch.Tensor:
+        """Counts over the recent window (all steps if no step has ended)."""
+        if len(self.recent) >= 2:
+            return self.recent[-1] - self.recent[0]
+        return self.counts
+
+    def imbalance(self, world: int) -> float:
+        """max / mean routed rows per rank under the contiguous expert split."""
+        per = self.load().sum(0).view(world, -1).sum(1).double()
+        return float(per.max() / per.mean().clamp_min(1))
+
+    def to_json(self) -> dict:
+        return {"steps": self.steps, "counts": self.counts.cpu().tolist()}
+
+
+def place_experts(load: torch.Tensor, world: int) -> list:
+    """Expert -> rank assignment balancing total load (greedy longest-processing-time over experts sorted by
+    load; every rank gets exactly E / world experts). `load` [E]."""
+    E = load.numel()
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    cap = E // world
+    order = torch.argsort(load.double(), descending=True).tolist()
+    tot = [0.0] * world
+    n = [0] * world
+    owner = [0] * E
+    for e in order:
+        r = min((r for r in range(world) if n[r] < cap), key=lambda r: tot[r])
+        owner[e] = r
+        tot[r] += float(load[e])
+        n[r] += 1
+    return owner
+
+
+def memory_census(weights: dict = None, caches=None, device=None) -> dict:
+    """Bytes by category: weights (per top-level key), caches (per field), and the allocator's counters."""
+    def nbytes(x):
+        if isinstance(x, torch.Tensor):
+            return x.numel() * x.element_size()
+        if hasattr(x, "blob"):
+            return x.blob.numel()
+        if isinstance(x, dict):
+            return sum(nbytes(v) for v in x.values())
+        if isinstance(x, (list, tuple)):
+            return sum(nbytes(v) for v in x)
+        return 0
+    out = {}
+    if weights is not None:
+        out["weights"] = {k: nbytes(v) for k, v in weights.items()}
+    if caches is not None:
+        out["caches"] = {k: nbytes(v) for k, v in vars(caches).items() if nbytes(v)}
+    if torch.cuda.is_available():
+        dev = torch.device(device or "cuda")
+        s = torch.cuda.memory_stats(dev)
+        free, total = torch.cuda.mem_get_info(dev)
+        out["allocator"] = {"allocated": s.get("allocated_bytes.all.current", 0),
+                            "reserved": s.get("reserved_bytes.all.current", 0),
+                            "peak_allocated": s.get("allocated_bytes.all.peak", 0), "free": free, "total": total}
+    return out
