@@ -50,9 +50,9 @@ def dsa_mask(x, qc, p, cfg, cos, sin):
     w = (x @ p["iw"].t()) * iD ** -0.5 * iH ** -0.5
     s = torch.relu(torch.einsum("qhd,kd->qhk", q, k))
     lg = torch.einsum("qhk,qh->qk", s, w)
-    ar = torch.arange(T)
+    ar = torch.arange(T, device=x.device)
     lg = lg.masked_fill(ar[None, :] > ar[:, None], float("-inf"))
-    M = torch.zeros(T, T, dtype=torch.bool)
+    M = torch.zeros(T, T, dtype=torch.bool, device=x.device)
     # ties (ReLU makes exact zeros common) resolve to the lower position, the rule of the engine's radix select
     idx = torch.sort(lg, dim=-1, descending=True, stable=True).indices[:, : cfg.index_topk]
     M.scatter_(1, idx, True)
