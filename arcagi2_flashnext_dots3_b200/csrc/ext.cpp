@@ -37,7 +37,9 @@ void wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, in
            c10::optional<torch::Tensor> items, c10::optional<torch::Tensor> n_items, int64_t max_items,
            int64_t dense_T, torch::Tensor x, int64_t b_row0, torch::Tensor out, int64_t out_row0,
            int64_t out_cols, int64_t epi, bool accumulate, double alpha, int64_t n_tile, int64_t max_block_bytes,
-           torch::Tensor err, int64_t timeout_ns, int64_t k_splits, c10::optional<torch::Tensor> row_dst) {
+           torch::Tensor err, int64_t timeout_ns, int64_t k_splits, c10::optional<torch::Tensor> row_dst,
+           c10::optional<torch::Tensor> fan_ptrs, int64_t fan_me, int64_t fan_slot,
+           c10::optional<torch::Tensor> fan_epoch) {
   CHECK_CUDA(wbase); CHECK_CUDA(x); CHECK_CUDA(out); CHECK_CUDA(err);
   CHECK_CONTIG(x); CHECK_CONTIG(out);
   CHECK_ALIGN16(wbase); CHECK_ALIGN16(x);
@@ -86,6 +88,17 @@ void wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, in
     a.row_dst = row_dst->data_ptr<int64_t>();
   }
   a.timeout_ns = (unsigned long long)timeout_ns;
+  if (fan_ptrs) {
+    TORCH_CHECK(fan_epoch && out_dtype == fw::WGEMM_OUT_F32 && !accumulate && epi == fw::WGEMM_EPI_STORE && !row_dst,
+                "fan-out needs the fp32 store epilogue and an epoch tensor");
+    TORCH_CHECK(fan_ptrs->is_cuda() && fan_ptrs->scalar_type() == torch::kInt64 && out.numel() <= fan_slot &&
+                out.size(-1) == out_cols, "fan-out: device int64 pointers, output of at most one slot, dense rows");
+    a.fan_base = reinterpret_cast<const uint64_t*>(fan_ptrs->data_ptr<int64_t>());
+    a.fan_n = fan_ptrs->numel();
+    a.fan_me = fan_me;
+    a.fan_slot = fan_slot;
+    a.fan_epoch = fan_epoch->data_ptr<int64_t>();
+  }
   static const int dbg = getenv("FW_WGEMM_DBG") ? atoi(getenv("FW_WGEMM_DBG")) : 0;
   a.dbg = dbg;
   static const int sleep_env = getenv("FW_WGEMM_SLEEP_NS") ? atoi(getenv("FW_WGEMM_SLEEP_NS")) : -1;

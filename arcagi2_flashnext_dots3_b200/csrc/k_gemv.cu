@@ -28,7 +28,7 @@ namespace {
 
 #define STREAM at::cuda::getCurrentCUDAStream()
 constexpr int kMaxTok = 8;
-constexpr int kMaxK = 2560;   // activation row length staged in shared memory (int8)
+constexpr int kMaxK = 8192;   // longest activation row staged in shared memory (int8; dynamic size 8 x K)
 
 // ------------------------------------------------------------------------------------ activation quantization
 // One warp per (row, 128-column group): lane l owns columns 4l..4l+3.

@@ -11,6 +11,7 @@ void register_d3(pybind11::module& m);
 void register_sample(pybind11::module& m);
 void register_ple(pybind11::module& m);
 void register_gemv(pybind11::module& m);
+void register_tp(pybind11::module& m);
 
 void register_kernels(pybind11::module& m) {
   register_fn(m);
@@ -20,4 +21,5 @@ void register_kernels(pybind11::module& m) {
   register_sample(m);
   register_ple(m);
   register_gemv(m);
+  register_tp(m);
 }

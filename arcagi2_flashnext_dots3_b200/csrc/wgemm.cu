@@ -528,6 +528,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // per-row destination (may be a peer GPU's buffer): the expert-parallel combine's
                     // data movement happens here, one store per output element straight into its source
                     reinterpret_cast<float*>(a.row_dst[orow0 + n])[col] = f;
+                  } else if (a.fan_n > 0) {
+                    // tensor-parallel all-reduce: the partial goes straight into every rank's slot [me]
+                    const int64_t par = a.fan_epoch[0] & 1;
+                    const int64_t off = (par * a.fan_n + a.fan_me) * a.fan_slot + o;
+                    for (int pe = 0; pe < a.fan_n; ++pe) reinterpret_cast<float*>(a.fan_base[pe])[off] = f;
                   } else if (a.out_dtype == WGEMM_OUT_F32) {
                     float* op = reinterpret_cast<float*>(a.out) + o;
                     *op = a.accumulate ? *op + f : f;

@@ -52,6 +52,12 @@ struct WGemmArgs {
   int accumulate;           // fp32 store only: out += result
   float alpha;
   const int64_t* row_dst;   // optional: fp32 destination address of every output row (store epilogue only)
+  // optional fan-out (tensor-parallel all-reduce): every fp32 output element is also stored at
+  // fan_base[p] + (parity * fan_n + fan_me) * fan_slot + row * out_ld + col for p < fan_n, parity = epoch & 1
+  const uint64_t* fan_base;
+  int fan_n, fan_me;
+  int64_t fan_slot;
+  const int64_t* fan_epoch;
   // split-K (deterministic): k_splits CTAs share one (item, tile); each writes its fp32 partial
   // [N x 128] to workspace, bumps counters[item * row_tiles + tile]; the last one sums the partials in split
   // order, runs the epilogue and resets the counter to zero (so a captured graph can replay).

@@ -57,9 +57,12 @@ def allocate_caches(cfg, device, n_slots: int, max_len: int, block_size: int = 6
 class D3Model:
     allocate = staticmethod(allocate_caches)
 
-    def __init__(self, cfg, weights: dict, caches: D3Caches, device, ep=None):
+    def __init__(self, cfg, weights: dict, caches: D3Caches, device, ep=None, tp=None):
+        """``tp``: a :class:`..parallel.tp.TPGroup`; then `cfg` is the rank's view (:func:`..parallel.tp.tp_config`)
+        and `weights` the rank's shard (:func:`..parallel.tp.shard_d3_weights` + :func:`.d3_weights.to_engine`)."""
         self.cfg, self.W, self.c = cfg, weights, caches
         self.ep = ep
+        self.tp = tp
         self.device = torch.device(device)
         self.act = ops.act_dtype(self.device)
         self.rope = d3.rope_table(caches.max_len + 8, cfg.qk_rope_dim, cfg.rope_theta, self.device)
@@ -90,22 +93,69 @@ class D3Model:
         o_lat = d3.mla_attn(q_lat, q_pe, c.latent[l], c.block_table, slots, positions, n_tok, sel, window,
                             self.scale)
         o = self._bmm(o_lat, p["uv"].transpose(1, 2))           # [H, T, dv]
+        if self.tp is not None:  # row-parallel o-projection fused with the all-reduce; adds into h itself
+            self.tp.linear_allreduce_add(self, d3.mla_out(o, gate), p["o"], self._h)
+            return None
         return self._mm(d3.mla_out(o, gate), p["o"])
 
+    def _moe_tp(self, x, p, h):
+        """Tensor parallel: global routing, this rank's experts for all tokens, partial sum all-reduced into h.
+        The shared expert is added by rank 0 only."""
+        cfg, tp = self.cfg, self.tp
+        T, E = x.shape[0], cfg.n_experts
+        lo, hi = p["expert_range"]
+        E_loc = hi - lo
+        logits = self._mm(x, p["router"])
+        ids, w = d3.route(logits, E, p["bias"], cfg.top_k, cfg.route_scale)
+        local = (ids >= lo) & (ids < hi)
+        lid = torch.where(local, ids - lo, torch.full_like(ids, E_loc)).to(torch.int32)
+        wl = torch.where(local, w, torch.zeros_like(w))
+        P = T * cfg.top_k
+        gemv = x.is_cuda and P <= 4 * E
+        n_tile = wgemm.GEMV_MAX_TOK if gemv else (wgemm.pick_n_tile(max(1, (2 * P) // E)) if x.is_cuda else 16)
+        max_items = (P + n_tile - 1) // n_tile + E_loc + 1
+        pair_pos, items, n_items = ops.moe_plan(lid, E_loc + 1, n_tile, max_items)
+        idx = torch.arange(max_items, dtype=torch.int32, device=x.device)
+        n_loc = ((items[:, 0] < E_loc) & (idx < n_items)).sum().to(torch.int32).view(1)
+        xs = ops.moe_scatter(x, pair_pos)
+        act = torch.empty(P, cfg.moe_inter, dtype=self.act, device=x.device)
+        ypair = torch.empty(P + 1, cfg.hidden_size, dtype=torch.float32, device=x.device)
+        ypair[P].zero_()
+        if gemv:
+            wgemm.gemv_grouped(xs, p["gu"], items, n_loc, max_items, act, epi=wgemm.EPI_SILU_MUL)
+            wgemm.gemv_grouped(act, p["d"], items, n_loc, max_items, ypair)
+        else:
+            wgemm.grouped(xs, p["gu"], items, n_loc, max_items, act, epi=wgemm.EPI_SILU_MUL, n_tile=n_tile)
+            wgemm.grouped(act, p["d"], items, n_loc, max_items, ypair, n_tile=n_tile)
+        pp = torch.where(local, pair_pos, torch.full_like(pair_pos, P))
+        sact = self._mm(x, p["sgu"], epi=wgemm.EPI_SILU_MUL, out_dtype=self.act)
+        ysh = self._mm(sact, p["sd"])
+        sg = torch.full((T,), float("inf") if tp.rank == 0 else float("-inf"), device=x.device)
+        part = torch.zeros(T, cfg.hidden_size, dtype=torch.float32, device=x.device)
+        ops.moe_combine(part, ypair, pp, wl, ysh, sg, torch.ones(T, 1, dtype=torch.float32, device=x.device))
+        tp.allreduce_add(h, part)
+
     def _moe(self, x, p, h):
+        if self.tp is not None:
+            return self._moe_tp(x, p, h)
         cfg = self.cfg
         T, E = x.shape[0], cfg.n_experts
         logits = self._mm(x, p["router"])
         ids, w = d3.route(logits, E, p["bias"], cfg.top_k, cfg.route_scale)
         P = T * cfg.top_k
-        n_tile = wgemm.pick_n_tile(max(1, (2 * P) // E)) if x.is_cuda else 16
+        gemv = x.is_cuda and P <= 4 * E   # decode: a few tokens per expert -> CUDA-core grouped GEMV
+        n_tile = wgemm.GEMV_MAX_TOK if gemv else (wgemm.pick_n_tile(max(1, (2 * P) // E)) if x.is_cuda else 16)
         max_items = (P + n_tile - 1) // n_tile + E
         pair_pos, items, n_items = ops.moe_plan(ids, E, n_tile, max_items)
         xs = ops.moe_scatter(x, pair_pos)
         act = torch.empty(P, cfg.moe_inter, dtype=self.act, device=x.device)
-        wgemm.grouped(xs, p["gu"], items, n_items, max_items, act, epi=wgemm.EPI_SILU_MUL, n_tile=n_tile)
         ypair = torch.empty(P, cfg.hidden_size, dtype=torch.float32, device=x.device)
-        wgemm.grouped(act, p["d"], items, n_items, max_items, ypair, n_tile=n_tile)
+        if gemv:
+            wgemm.gemv_grouped(xs, p["gu"], items, n_items, max_items, act, epi=wgemm.EPI_SILU_MUL)
+            wgemm.gemv_grouped(act, p["d"], items, n_items, max_items, ypair)
+        else:
+            wgemm.grouped(xs, p["gu"], items, n_items, max_items, act, epi=wgemm.EPI_SILU_MUL, n_tile=n_tile)
+            wgemm.grouped(act, p["d"], items, n_items, max_items, ypair, n_tile=n_tile)
         sact = self._mm(x, p["sgu"], epi=wgemm.EPI_SILU_MUL, out_dtype=self.act)
         ysh = self._mm(sact, p["sd"])
         ones = torch.ones(T, 1, dtype=torch.float32, device=x.device)
@@ -114,6 +164,7 @@ class D3Model:
     def step(self, ids: torch.Tensor, slots: torch.Tensor, positions: torch.Tensor, n_tok: int = 1):
         cfg, W = self.cfg, self.W
         h = W["embed"][ids.long()].float()
+        self._h = h
         y = None
         for l, L in enumerate(W["layers"]):
             x = d3.add_rms(h, y, L["ln1"], cfg.rms_eps, self.act)

@@ -97,7 +97,8 @@ def to_engine(W: dict, cfg, device) -> dict:
                                                      device=dev),
                         "d": wgemm.build_weight_set(d, fmts, cfg.hidden_size, cfg.moe_inter, device=dev),
                         "sgu": _ws(_silu_perm_rows(mo["shared"]["gu"], cfg.shared_inter), cfg, dev, silu_pairs=True),
-                        "sd": _ws(mo["shared"]["d"], cfg, dev)}
+                        "sd": _ws(mo["shared"]["d"], cfg, dev),
+                        "expert_range": mo.get("expert_range", (0, cfg.n_experts))}
         else:
             M["mlp"] = {"gu": _ws(_silu_perm_rows(L["mlp"]["gu"], cfg.dense_inter), cfg, dev, silu_pairs=True),
                         "d": _ws(L["mlp"]["d"], cfg, dev)}

@@ -119,7 +119,8 @@ def dense_n_tile(T: int, ws: WeightSet) -> int:
 
 
 def matmul(x16: torch.Tensor, ws: WeightSet, out: torch.Tensor = None, epi: int = EPI_STORE,
-           out_dtype=torch.float32, accumulate=False, alpha=1.0, n_tile=None, k_splits: int = 0) -> torch.Tensor:
+           out_dtype=torch.float32, accumulate=False, alpha=1.0, n_tile=None, k_splits: int = 0,
+           fan=None) -> torch.Tensor:
     """Dense y = x @ W^T (or silu(gate)*up for a silu_pairs weight). x16: fp16 [T, K]."""
     T = x16.shape[0]
     cols = ws.rows // 2 if epi == EPI_SILU_MUL else ws.rows
@@ -134,9 +135,10 @@ def matmul(x16: torch.Tensor, ws: WeightSet, out: torch.Tensor = None, epi: int 
             out.copy_(y.to(out.dtype))
         return out
     n = n_tile or dense_n_tile(T, ws)
+    f_ptrs, f_me, f_slot, f_epoch = fan if fan is not None else (None, 0, 0, None)
     native.C().wgemm(ws.blob, ws.exp_off, ws.exp_fmt, ws.row_tiles, ws.kg, None, None, 0, T, x16, 0, out, 0,
                      cols, epi, accumulate, alpha, n, ws.max_block_bytes, native.err_word(x16.device),
-                     native.DEFAULT_TIMEOUT_NS, k_splits, None)
+                     native.DEFAULT_TIMEOUT_NS, k_splits, None, f_ptrs, f_me, f_slot, f_epoch)
     return out
 
 
@@ -154,7 +156,7 @@ def grouped(xs16: torch.Tensor, ws: WeightSet, items: torch.Tensor, n_items: tor
         return out
     native.C().wgemm(ws.blob, ws.exp_off, ws.exp_fmt, ws.row_tiles, ws.kg, items, n_items, max_items, -1, xs16, 0,
                      out, 0, cols, epi, False, 1.0, n_tile, ws.max_block_bytes, native.err_word(xs16.device),
-                     native.DEFAULT_TIMEOUT_NS, 1, row_dst)
+                     native.DEFAULT_TIMEOUT_NS, 1, row_dst, None, 0, 0, None)
     return out
 
 

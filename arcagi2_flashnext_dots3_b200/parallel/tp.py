@@ -1,0 +1,135 @@
+"""Tensor parallelism for the Dots3-shaped model: attention heads split over the ranks, row-parallel output
+projection fused with an NVLink all-reduce, experts split over the ranks with every rank computing the partial MoE
+sum of its experts for all tokens (no dispatch: tokens are replicated under TP), same all-reduce.
+
+The reference runs D3 with TP4 and replaces NCCL's all-reduce by a host-staged quantized one
+(dotsnote/engine/arcstats_pkg/arcstats/host_ar.py; routed in arcstats/__init__.py:383-410). Here
+``comm="fused"``: the o-projection GEMM stores its fp32 partial directly into every rank's symmetric buffer
+(wgemm fan-out epilogue), then csrc/k_tp.cu signals and reduces (bounded waits, deterministic rank order, the
+residual add fused into the reduce); the MoE partial is pushed the same way. ``comm="nccl"``: all_reduce.
+"""
+from __future__ import annotations
+
+import dataclasses
+
+import torch
+import torch.distributed as dist
+
+from ..ops import native
+
+
+def tp_config(cfg, world: int):
+    """The per-rank view of a D3 config: head counts divided by the TP world."""
+    if cfg.n_heads % world or cfg.swa_n_heads % world or cfg.n_experts % world:
+        raise ValueError(f"heads/experts of {cfg.name} do not split over {world} ranks")
+    return dataclasses.replace(cfg, n_heads=cfg.n_heads // world, swa_n_heads=cfg.swa_n_heads // world)
+
+
+class TPGroup:
+    def __init__(self, rank: int, world: int, device, max_tokens: int, hidden: int, group=None, comm: str = "fused",
+                 timeout_ns: int = None):
+        self.rank, self.world, self.comm = rank, world, comm
+        self.device = torch.device(device)
+        self.group = group or dist.group.WORLD
+        self.H = hidden
+        self.max_tokens = max_tokens
+        self.slot = max_tokens * hidden
+        self.timeout_ns = timeout_ns or native.DEFAULT_TIMEOUT_NS * 4
+        self.epoch = torch.zeros(1, dtype=torch.int64, device=self.device)
+        if comm == "fused":
+            import torch.distributed._symmetric_memory as symm
+            W = world
+
+            def alloc(shape, dtype):
+                t = symm.empty(*shape, dtype=dtype, device=self.device)
+                t.zero_()
+                h = symm.rendezvous(t, self.group)
+                ptrs = [h.get_buffer(r, tuple(shape), dtype).data_ptr() for r in range(W)]
+                return t, torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+
+            self.buf, self.buf_ptrs = alloc((2, W, self.slot), torch.float32)
+            self.flags, self.flag_ptrs = alloc((2, W), torch.int64)
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+        elif comm != "nccl":
+            raise ValueError(comm)
+
+    # ------------------------------------------------------------------------------------ fused GEMM path
+    def begin(self):
+        if self.comm == "fused":
+            native.C().tp_epoch(self.epoch)
+
+    def fan(self):
+        """wgemm fan-out arguments: write the GEMM output into slot [rank] of every rank's buffer."""
+        return (self.buf_ptrs, self.rank, self.slot, self.epoch)
+
+    def finish_into(self, h: torch.Tensor, T: int):
+        """h[:T] += sum of all ranks' partials (after a fan-out GEMM or a push)."""
+        n = T * self.H
+        native.C().tp_signal(self.flag_ptrs, self.rank, self.epoch)
+        native.C().tp_reduce(self.buf, self.flags, self.world, n, self.slot, self.epoch, h,
+                             True, native.err_word(self.device), self.timeout_ns)
+
+    # ------------------------------------------------------------------------------------ generic partial
+    def allreduce_add(self, h: torch.Tensor, partial: torch.Tensor):
+        """h += all-reduce(partial) for fp32 [T, H] tensors."""
+        T = partial.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} rows > TP buffer capacity {self.max_tokens}")
+        if self.comm == "nccl" or not partial.is_cuda:
+            dist.all_reduce(partial, group=self.group)
+            h += partial
+            return
+        self.begin()
+        native.C().tp_push(partial.contiguous(), self.buf_ptrs, self.rank, self.slot, self.epoch)
+        self.finish_into(h, T)
+
+    def linear_allreduce_add(self, model, x16, ws, h):
+        """h += all-reduce(x16 @ W_rank^T) with the GEMM epilogue writing into the peers (fused path)."""
+        from ..ops import wgemm
+        T = x16.shape[0]
+        if self.comm == "nccl" or not x16.is_cuda:
+            self.allreduce_add(h, model._mm(x16, ws))
+            return
+        if T > self.max_tokens:
+            raise ValueError(f"{T} rows > TP buffer capacity {self.max_tokens}")
+        self.begin()
+        dummy = torch.empty(T, ws.rows, dtype=torch.float32, device=x16.device)
+        wgemm.matmul(x16, ws, out=dummy, fan=self.fan())
+        self.finish_into(h, T)
+
+
+def shard_d3_weights(W: dict, cfg, rank: int, world: int) -> dict:
+    """Dense-form D3 weights of one TP rank: the rank's attention heads (q_b, kv_b, g rows; o columns) and its
+    contiguous share of every MoE layer's experts (router and correction bias stay whole: routing is global)."""
+    import copy
+    dn, dr, dv = cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim
+    out = {k: v for k, v in W.items() if k != "layers"}
+    out["layers"] = []
+    for l, L in enumerate(W["layers"]):
+        H = cfg.heads_of(l)
+        h0, h1 = rank * H // world, (rank + 1) * H // world
+        if getattr(cfg, "dense_fp8", False) and ((h1 - h0) * (dn + dr) % 128 or (h1 - h0) * dv % 128):
+            # a shard boundary inside a 128x128 FP8 block would re-quantize the block with a different scale
+            raise ValueError(f"layer {l}: {h1 - h0} heads per rank do not cover whole 128-wide FP8 blocks")
+        a = dict(L["attn"])
+        a["q_b"] = a["q_b"][h0 * (dn + dr):h1 * (dn + dr)]
+        a["kv_b"] = a["kv_b"][h0 * (dn + dv):h1 * (dn + dv)]
+        a["o"] = a["o"][:, h0 * dv:h1 * dv]
+        a["g"] = a["g"][h0:h1]
+        L2 = dict(L)
+        L2["attn"] = a
+        if "moe" in L:
+            m = dict(L["moe"])
+            lay = m["lowbit"]
+            E = len(lay.blobs)
+            e0, e1 = rank * E // world, (rank + 1) * E // world
+            lay2 = copy.copy(lay)
+            lay2.blobs = lay.blobs[e0:e1]
+            lay2.experts = lay.experts[e0:e1]
+            m["lowbit"] = lay2
+            m["experts_dense"] = m["experts_dense"][e0:e1]
+            m["expert_range"] = (e0, e1)
+            L2["moe"] = m
+        out["layers"].append(L2)
+    return out

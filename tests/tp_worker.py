@@ -1,0 +1,60 @@
+"""Worker for the tensor-parallel D3 tests: every rank runs its head/expert shard; logits of a prefill chunk and
+decode steps must equal the single-process model on the same weights."""
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from arcagi2_flashnext_dots3_b200.config import d3_small_config  # noqa: E402
+from arcagi2_flashnext_dots3_b200.engine.block_manager import BlockAllocator  # noqa: E402
+from arcagi2_flashnext_dots3_b200.models.d3 import D3Model, allocate_caches  # noqa: E402
+from arcagi2_flashnext_dots3_b200.models.d3_weights import random_dense, to_engine  # noqa: E402
+from arcagi2_flashnext_dots3_b200.ops import native  # noqa: E402
+from arcagi2_flashnext_dots3_b200.parallel.tp import TPGroup, shard_d3_weights, tp_config  # noqa: E402
+
+
+def run(model, ids, dev):
+    c = model.c
+    alloc = BlockAllocator(c.n_blocks, 2)
+    model.assign_blocks(0, 48, alloc)
+    s0 = torch.tensor([0], dtype=torch.int32, device=dev)
+    xs = [model.step(ids[:14].to(dev), s0, torch.tensor([0], dtype=torch.int32, device=dev), 14)]
+    for t in range(14, ids.shape[0]):
+        xs.append(model.step(ids[t:t + 1].to(dev), s0, torch.tensor([t], dtype=torch.int32, device=dev), 1))
+    return model.logits(torch.cat(xs)).float().cpu()
+
+
+def main():
+    comm = sys.argv[1]
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    cuda = comm == "fused" or os.environ.get("TP_DEVICE") == "cuda"
+    if cuda:
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+    dev = torch.device("cuda", torch.cuda.current_device()) if cuda else torch.device("cpu")
+    import datetime
+    dist.init_process_group("nccl" if cuda else "gloo", timeout=datetime.timedelta(seconds=120))
+    cfg = d3_small_config(num_layers=3, swa_n_heads=4, qk_nope_dim=64)
+    W = random_dense(cfg, seed=4)
+    ids = torch.randint(0, cfg.vocab_size, (24,), generator=torch.Generator().manual_seed(5))
+    ref = run(D3Model(cfg, to_engine(W, cfg, dev), allocate_caches(cfg, dev, 2, 64, block_size=16), dev), ids, dev)
+    lc = tp_config(cfg, world)
+    tp = TPGroup(rank, world, dev, max_tokens=32, hidden=cfg.hidden_size, comm=comm)
+    m = D3Model(lc, to_engine(shard_d3_weights(W, cfg, rank, world), lc, dev),
+                allocate_caches(lc, dev, 2, 64, block_size=16), dev, tp=tp)
+    got = run(m, ids, dev)
+    if cuda:
+        torch.cuda.synchronize()
+        native.check_error(dev)
+    err = (got - ref).abs().max() / ref.abs().max()
+    tol = 2e-2 if cuda else 1e-4
+    assert err < tol, (rank, float(err))
+    dist.barrier()
+    if rank == 0:
+        print("TP_OK", comm, world, float(err))
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
