@@ -12,6 +12,7 @@ void register_sample(pybind11::module& m);
 void register_ple(pybind11::module& m);
 void register_gemv(pybind11::module& m);
 void register_tp(pybind11::module& m);
+void register_mla(pybind11::module& m);
 
 void register_kernels(pybind11::module& m) {
   register_fn(m);
@@ -22,4 +23,5 @@ void register_kernels(pybind11::module& m) {
   register_ple(m);
   register_gemv(m);
   register_tp(m);
+  register_mla(m);
 }

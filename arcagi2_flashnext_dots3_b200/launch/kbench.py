@@ -4,6 +4,7 @@
     python -m arcagi2_flashnext_dots3_b200.launch.kbench dense [--tokens 64] [--reps 20]
     python -m arcagi2_flashnext_dots3_b200.launch.kbench attn  [--tokens 64] [--ctx 9000] [--reps 20]
     python -m arcagi2_flashnext_dots3_b200.launch.kbench gdn   [--tokens 64] [--reps 20]
+    python -m arcagi2_flashnext_dots3_b200.launch.kbench mla   [--tokens 64] [--ctx 9000] [--reps 20]
 
 Counterpart of the reference's micro-benchmarks and startup gates (dotsnote/kaggle/runtime_dataset/bench_*.py,
 run_l4.py:435 `run_bench`): each case prints one JSON line with the median device time and the achieved
@@ -157,9 +158,42 @@ def bench_gdn(args):
                       "GBps": round(b / t / 1e6, 1)}))
 
 
+def bench_mla(args):
+    """D3 latent attention: tcgen05 kernel vs the CUDA-core kernel, DSA (128 heads, 512+64, top-2048) and SWA
+    (64 heads, 1024+64, window 513) decode rows."""
+    from ..ops import d3_ops
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    T, ctx, bs = args.tokens, args.ctx, 64
+    for kind, H, kvr, topk, window in (("dsa", 128, 512, 2048, 0), ("swa", 64, 1024, 0, 513)):
+        D = kvr + 64
+        mb = (ctx + bs) // bs + 1
+        cache = (torch.randn(T * mb, bs, D, device=dev, generator=g) * 0.5).to(torch.float8_e4m3fn)
+        bt = torch.randperm(T * mb, device=dev, generator=g).to(torch.int32).view(T, mb).contiguous()
+        slots = torch.arange(T, dtype=torch.int32, device=dev)
+        pos = torch.full((T,), ctx - 1, dtype=torch.int32, device=dev)
+        q_lat = (torch.randn(H, T, kvr, device=dev, generator=g) * 0.3).bfloat16()
+        q_pe = torch.randn(T, H, 64, device=dev, generator=g) * 0.3
+        sel = None
+        if topk:
+            sel = torch.stack([torch.randperm(ctx, device=dev, generator=g)[:topk] for _ in range(T)]).to(torch.int32)
+        n = topk if topk else min(window, ctx)
+        flops = 2 * T * H * n * (D + kvr)
+        byts = T * n * D
+        row = {"case": f"mla_{kind}", "rows": T, "heads": H, "keys": n}
+        for impl, cc in (("tc", False), ("cuda_core", True)):
+            d3_ops._MLA_CUDA_CORE = cc
+            t = _time(lambda: d3_ops.mla_attn(q_lat, q_pe, cache, bt, slots, pos, 1, sel, window, 0.07), args.reps)
+            row[impl + "_us"] = round(t * 1e3, 1)
+            row[impl + "_TFLOPs"] = round(flops / t / 1e9, 1)
+        row["row_GBps_tc"] = round(byts / (row["tc_us"] * 1e-6) / 1e9, 1)
+        d3_ops._MLA_CUDA_CORE = False
+        print(json.dumps(row), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["moe", "dense", "attn", "gdn", "all"])
+    ap.add_argument("case", choices=["moe", "dense", "attn", "gdn", "mla", "all"])
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--experts", type=int, default=320)
     ap.add_argument("--ctx", type=int, default=9000)
@@ -167,7 +201,7 @@ def main():
     ap.add_argument("--sweep", action="store_true", help="dense: time every n_tile x split-K combination")
     ap.add_argument("--only", default="", help="dense: comma-separated case names")
     args = ap.parse_args()
-    cases = {"moe": bench_moe, "dense": bench_dense, "attn": bench_attn, "gdn": bench_gdn}
+    cases = {"moe": bench_moe, "dense": bench_dense, "attn": bench_attn, "gdn": bench_gdn, "mla": bench_mla}
     for name, fn in cases.items():
         if args.case in (name, "all"):
             fn(args)

@@ -8,6 +8,8 @@ stable descending sort), full causal attention while a query has at most `index_
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.nn.functional as F
 
@@ -138,12 +140,23 @@ def dsa_select(iq, iw, idx_cache, slots, positions, n_tok, topk: int, max_len: i
     return sel
 
 
+_MLA_CUDA_CORE = os.environ.get("FW_MLA_CUDA_CORE", "0") == "1"   # force the CUDA-core latent attention
+_MLA_SPLITS = int(os.environ.get("FW_MLA_SPLITS", "0"))              # > 0: fixed key-split count (tests)
+_MLA_TRACE = None   # int64 [64 * 8] device tensor: per-chunk phase timestamps of the first CTA (profiling)
+
+
 def mla_attn(q_lat, q_pe, cache, block_table, slots, positions, n_tok, sel, window: int, scale: float):
     """o_lat [H, T, kvr]: softmax over rows of (q_lat . c + q_pe . r) * scale, times the latent c."""
     H, T, kvr = q_lat.shape
     if _cuda(q_lat):
         o = torch.empty_like(q_lat)
-        native.C().d3_mla_attn(q_lat, q_pe, cache, block_table, slots, positions, n_tok, sel, window, scale, o)
+        C = native.C()
+        if not _MLA_CUDA_CORE and C.d3_mla_tc_supported(kvr, q_pe.shape[2]):
+            # tcgen05 path (csrc/k_mla.cu); the CUDA-core kernel stays for shapes it does not cover
+            C.d3_mla_attn_tc(q_lat, q_pe, cache, block_table, slots, positions, n_tok, sel, window, scale, o,
+                             native.err_word(q_lat.device), native.DEFAULT_TIMEOUT_NS, _MLA_SPLITS, _MLA_TRACE)
+        else:
+            C.d3_mla_attn(q_lat, q_pe, cache, block_table, slots, positions, n_tok, sel, window, scale, o)
         return o
     pos = _pos(positions, n_tok)
     sl = slots.long().repeat_interleave(n_tok)
