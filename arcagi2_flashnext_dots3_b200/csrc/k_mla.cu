@@ -3,25 +3,28 @@
 // Per query row t (a decode token or one row of a prefill chunk) and head h:
 //     s_j = (q_lat[h] . c_j[:kvr] + q_pe[h] . c_j[kvr:]) * scale,   o[h] = sum_j softmax(s)_j c_j[:kvr]
 // over the rows j of the DSA top-k list, the sliding window, or all causal rows. Every head reads the same
-// rows (multi-query form of MLA), so per key chunk the work is two small GEMMs:
-//     S   [heads x keys]   = Q [heads x D] . K^T            (M = 128 head rows, N = 32 keys, K = D = kvr + dr)
-//     O^T [kvr x heads]   += V^T [kvr x keys] . P^T          (M = 128 latent dims per tile, N = heads, K = 32 keys)
-// Heads are the M rows of the score MMA, so each thread of warps 0-1 owns one head's scores (tcgen05.ld of its
-// TMEM lane) and runs the online softmax without any cross-thread reduction. The P.V product is written
-// transposed so that O for up to 64 heads x 512 latent dims (or 32 x 1024) fits in TMEM next to S, and so that
+// rows (multi-query form of MLA), so per 32-key chunk the work is two small GEMMs:
+//     S   [heads x keys]  = Q [heads x D] . K^T           (M = 64 head rows, N = 32 keys, K = D = kvr + dr)
+//     O^T [kvr x heads]  += V^T [kvr x keys] . P^T         (M = 128 latent dims per tile, N = heads, K = 32 keys)
+// Heads are the M rows of the score MMA (M = 64: head 16w + l sits in TMEM lane 32w + l), so each softmax thread
+// owns one head's scores and runs the online softmax without cross-thread reductions. The P.V product is written
+// transposed so that O for up to 64 heads x 512 latent dims fits in TMEM next to two score buffers, and so that
 // V^T is the same shared-memory tile as the key chunk, read as an MN-major operand: one fp8 -> fp16 conversion
 // per chunk feeds both MMAs.
 //
-// CTA = (row t, head group, key split); 5 warps:
-//   warp 4      loader: resolves the chunk's 32 key positions to cache rows (DSA list / window / causal, paged
-//               block table) and fetches each 576- or 1088-byte FP8 row with a 1-D bulk copy into a ring stage
-//   warps 0-3   convert the stage to fp16 (128-byte-swizzled K-major tile), issue the MMAs (one thread),
-//               softmax (warps 0-1, lanes = heads), lazy O rescale (only when a head's max grows by > 2^8),
-//               epilogue (lanes = latent dims)
+// CTA = (row t, head group, key split); warp-specialized pipeline over chunks i:
+//   warp 8      loader: resolves the chunk's 32 key positions to cache rows (DSA list / window / causal, paged
+//               block table) and fetches each FP8 row with a 1-D bulk copy into a ring stage
+//   warps 4-7   convert stage -> fp16 key tile K[i & 1] (128-byte-swizzled K-major), record the key mask
+//   warp 9      MMA issuer (one thread): S(i) as soon as K[i & 1] is ready, then P.V(i - 1) once P(i - 1) is,
+//               so the score MMA of the next chunk runs under the softmax of the current one
+//   warps 0-3   softmax (lanes 0-15 = heads) into P[i & 1], lazy O rescale (only when a head's max grows by more
+//               than 2^8; waits for the previous P.V), epilogue (lanes = latent dims)
 // Q is staged once per CTA with only the group's heads; the score MMA's rows past them read the following shared
 // memory and produce rows that are never used. Key splits write unnormalized partials (O, running max, sum)
-// merged by mla_tc_combine_kernel. Every wait is bounded (%globaltimer); a timeout records an error code, the
-// loader drains its copies in flight and TMEM is released before the CTA exits.
+// merged by mla_tc_combine_kernel. Every wait is bounded (%globaltimer); a timeout records an error code, each
+// role drains out, the loader waits for its copies in flight and the MMA thread for its last MMAs, and TMEM is
+// released before the CTA exits.
 //
 // Replaces the reference's CUDA-core sparse MLA decode (dotsnote/engine/arcstats_pkg/arcstats/csrc/
 // offload_attn.cu, K2 "v5": 576-byte FP8 rows, online softmax over the selected rows) and the window-513 SWA
@@ -42,10 +45,12 @@ using namespace fw;
 #define STREAM at::cuda::getCurrentCUDAStream()
 
 constexpr int NK = 32;           // keys per chunk
-constexpr int kThreads = 160;    // warps 0-3 compute, warp 4 loads
+constexpr int kThreads = 320;    // warps 0-3 softmax/epilogue, 4-7 convert, 8 load, 9 MMA
 constexpr int kMaxStages = 3;
-static_assert(NK * 4 == 128, "the conversion maps 4 threads to each key of a chunk");
+constexpr int kMaxKB = 17;       // D / 64 <= 17 (kvr <= 1024, dr = 64)
 constexpr float kRescaleLog2 = 8.f;
+constexpr int NACC = 4;          // interleaved score accumulators: consecutive MMAs do not wait on each other
+static_assert(NK * 4 == 128, "the conversion maps 4 threads to each key of a chunk");
 
 struct MlaTcArgs {
   const __nv_bfloat16* q_lat;   // [H, T, kvr]
@@ -58,7 +63,7 @@ struct MlaTcArgs {
   const int* sel;               // [T, topk] positions (first entry -1 = no list) or null
   int topk, window;
   int T, H, kvr, dr, D;
-  int HGp;                      // heads per CTA (multiple of 16)
+  int HGp;                      // heads per CTA (multiple of 16, <= 64)
   int splits, stages;
   float scale_log2;
   __nv_bfloat16* o_lat;         // [H, T, kvr] when splits == 1
@@ -69,25 +74,39 @@ struct MlaTcArgs {
   unsigned long long* trace;    // optional: phase timestamps of CTA (0, 0, 0), [chunk][8]
 };
 
+// barrier indices (8 bytes each)
+enum : int {
+  kRawFull = 0,                  // [kMaxStages] loader -> converters (tx bytes)
+  kRawEmpty = kMaxStages,        // [kMaxStages] converters -> loader (4 warps)
+  kKcFull = 2 * kMaxStages,      // [2] converters -> MMA, softmax (4 warps)
+  kKcEmpty = kKcFull + 2,        // [2] MMA commit after P.V(i) -> converters
+  kSFull = kKcEmpty + 2,         // [2] MMA commit after S(i) -> softmax
+  kPFull = kSFull + 2,           // [2] softmax -> MMA (4 warps)
+  kPvDone = kPFull + 2,          // MMA commit after every P.V
+  kNumBars = kPvDone + 1
+};
+
 struct Smem {                   // byte offsets from the 1024-aligned base
-  uint32_t q, kc, p, raw, rows, corr, lsum, bars, misc, total;
+  uint32_t q, kc, p, raw, rows, vm, corr, lsum, bars, misc, total;
 };
 
 __host__ __device__ inline Smem smem_plan(int D, int HGp, int stages) {
   Smem s{};
   uint32_t o = 0;
+  const uint32_t kc_bytes = (D / 64) * NK * 128, p_bytes = ((HGp * 128 + 1023) / 1024) * 1024;
   s.q = o;  o += (D / 64) * HGp * 128;
-  s.kc = o; o += (D / 64) * NK * 128;
-  s.p = o;  o += ((HGp * 128 + 1023) / 1024) * 1024;
+  s.kc = o; o += 2 * kc_bytes;
+  s.p = o;  o += 2 * p_bytes;
   s.raw = o; o += ((stages * NK * D + 1023) / 1024) * 1024;
-  // the score MMA reads 128 rows of Q from the last k-block: keep that window inside the allocation
-  const uint32_t q_reach = s.q + (D / 64 - 1) * HGp * 128 + 128 * 128;
+  // the score MMA reads 64 rows of Q from the last k-block: keep that window inside the allocation
+  const uint32_t q_reach = s.q + (D / 64 - 1) * HGp * 128 + 64 * 128;
   if (o < q_reach) o = q_reach;
   s.rows = o; o += kMaxStages * NK * 4;
+  s.vm = o; o += 2 * 4;
   s.corr = o; o += 64 * 4;
   s.lsum = o; o += 64 * 4;
-  s.bars = o; o += (2 * kMaxStages + 2) * 8;
-  s.misc = o; o += 16;          // tmem base, abort word, rescale flag
+  s.bars = o; o += kNumBars * 8;
+  s.misc = o; o += 16;          // tmem base, abort word
   s.total = o + 1024;           // slack for aligning the dynamic base
   return s;
 }
@@ -129,7 +148,8 @@ __device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint3
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
 }
 
-__device__ __forceinline__ uint4 lds128(uint32_t a) {
+// no "memory" clobber: the caller orders these loads against the loader's writes with the stage barrier
+__device__ __forceinline__ uint4 lds128_nc(uint32_t a) {
   uint4 v;
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
   return v;
@@ -153,7 +173,7 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 }
 
 #define MLA_TRACE(chunk, slot)                                                                        \
-  if (a.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (chunk) < 64)              \
+  if (a.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (chunk) < 62)              \
     a.trace[(chunk) * 8 + (slot)] = globaltimer_ns();
 
 __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaTcArgs a) {
@@ -162,20 +182,20 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaTcArgs a) 
   uint8_t* gbase = smem_dyn + (base - smem_u32(smem_dyn));
   const Smem L = smem_plan(a.D, a.HGp, a.stages);
   const uint32_t sQ = base + L.q, sK = base + L.kc, sP = base + L.p, sRaw = base + L.raw;
+  const uint32_t kc_bytes = (a.D / 64) * NK * 128, p_bytes = ((a.HGp * 128 + 1023) / 1024) * 1024;
   int* rows = reinterpret_cast<int*>(gbase + L.rows);
+  volatile unsigned* vm_sm = reinterpret_cast<volatile unsigned*>(gbase + L.vm);
   float* corr_sm = reinterpret_cast<float*>(gbase + L.corr);
   float* l_sm = reinterpret_cast<float*>(gbase + L.lsum);
   const uint32_t bars = base + L.bars;
-  const uint32_t full0 = bars, empty0 = bars + kMaxStages * 8, bar_s = bars + 2 * kMaxStages * 8,
-                 bar_pv = bar_s + 8;
+  auto bar = [&](int i) -> uint32_t { return bars + 8u * (uint32_t)i; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + L.misc);
   volatile int* abort_w = reinterpret_cast<volatile int*>(gbase + L.misc + 4);
-  volatile int* flag_w = reinterpret_cast<volatile int*>(gbase + L.misc + 8);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t = blockIdx.x, g = blockIdx.y, sp = blockIdx.z;
   const int HGp = a.HGp, h0 = g * HGp, hn = min(HGp, a.H - h0);
-  const int D = a.D, kvr = a.kvr, RS = a.stages;
+  const int D = a.D, kvr = a.kvr, RS = a.stages, nkb = D / 64;
   const int b = t / a.n_tok;
   const int pos = a.positions[b] + t % a.n_tok, slot = a.slots[b];
   const int* sel = a.sel ? a.sel + (int64_t)t * a.topk : nullptr;
@@ -191,35 +211,38 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaTcArgs a) 
   const int per = (n_chunks + a.splits - 1) / a.splits;
   const int c0 = min(n_chunks, sp * per), nc = max(0, min(n_chunks, c0 + per) - c0);
   const int n_mt = kvr / 128;
-  const uint32_t O0 = NK;  // TMEM column of the first O^T tile
+  // TMEM: score buffer b, partial accumulator k at columns (b * NACC + k) * NK; O^T tiles from O0
+  const uint32_t O0 = 2 * NACC * NK;
 
-  if (tid == 0) { MLA_TRACE(62, 0) }
   if (tid == 0) {
     for (int s = 0; s < kMaxStages; ++s) {
-      mbar_init(full0 + 8 * s, 1);
-      mbar_init(empty0 + 8 * s, 4);
+      mbar_init(bar(kRawFull + s), 1);
+      mbar_init(bar(kRawEmpty + s), 4);
     }
-    mbar_init(bar_s, 1);
-    mbar_init(bar_pv, 1);
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(bar(kKcFull + k), 4);
+      mbar_init(bar(kKcEmpty + k), 1);
+      mbar_init(bar(kSFull + k), 1);
+      mbar_init(bar(kPFull + k), 4);
+    }
+    mbar_init(bar(kPvDone), 1);
     *abort_w = 0;
-    *flag_w = 0;
     fence_mbar_init();
   }
-  // TMEM: 32 score columns + (kvr / 128) O^T tiles of HGp columns, rounded up to a power of two
   uint32_t tcols = 32;
-  while (tcols < (uint32_t)(NK + (kvr / 128) * HGp)) tcols <<= 1;
+  while (tcols < (uint32_t)(O0 + n_mt * HGp)) tcols <<= 1;
   if (warp == 0) tmem_alloc_dyn(smem_u32(tmem_slot), tcols);
   // Q (fp16, K-major, 128-byte swizzle, HGp rows per 64-column block); padding heads are zero. Loads are issued
   // eight units at a time so their latencies overlap.
-  if (warp < 4) {
+  if (warp < 8) {
     const int cpr = D / 8, total = HGp * cpr;
-    for (int i0 = tid; i0 < total; i0 += 128 * 8) {
+    for (int i0 = tid; i0 < total; i0 += 256 * 8) {
       uint4 v0[8], v1[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         v0[k] = make_uint4(0u, 0u, 0u, 0u);
         v1[k] = make_uint4(0u, 0u, 0u, 0u);
-        const int i = i0 + k * 128;
+        const int i = i0 + k * 256;
         if (i < total) {
           const int h = i / cpr, d0 = (i % cpr) * 8;
           if (h < hn) {
@@ -236,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaTcArgs a) 
       }
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const int i = i0 + k * 128;
+        const int i = i0 + k * 256;
         if (i < total) {
           const int h = i / cpr, d0 = (i % cpr) * 8;
           uint32_t w[4];
@@ -258,18 +281,16 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaTcArgs a) 
         }
       }
     }
+    fence_proxy_async_smem();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (tid == 0) { MLA_TRACE(63, 7) }
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------------------------------ loader
     const uint64_t pol = a.H > HGp ? l2_policy_evict_last() : l2_policy_evict_first();
-    // cache row of key `lane` of chunk c (or -1); four chunks are resolved together so that the two dependent
-    // loads (list entry, block table) overlap across them
     auto resolve = [&](int c) -> int {
       const int kk = c * NK + lane;
       int p = -1;
@@ -284,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaTcArgs a) 
     int issued = 0;
     for (int i = 0; i < nc; ++i) {
       const int s = i % RS;
-      if ((i & 3) == 0) {
+      if ((i & 3) == 0) {  // four chunks resolved together: their dependent loads overlap
         const int p0 = resolve(c0 + i), p1 = i + 1 < nc ? resolve(c0 + i + 1) : -1,
                   p2 = i + 2 < nc ? resolve(c0 + i + 2) : -1, p3 = i + 3 < nc ? resolve(c0 + i + 3) : -1;
         cr0 = to_row(p0);
@@ -292,178 +313,215 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaTcArgs a) 
         cr2 = to_row(p2);
         cr3 = to_row(p3);
       }
-      if (i >= RS && !mbar_wait_warp(empty0 + 8 * s, ((i / RS) - 1) & 1, a.err, 7101, abort_w, a.timeout_ns)) break;
+      if (i >= RS && !mbar_wait_warp(bar(kRawEmpty + s), ((i / RS) - 1) & 1, a.err, 7101, abort_w, a.timeout_ns))
+        break;
       if (*abort_w) break;
       const int q = i & 3;
       const int crow = q == 0 ? cr0 : q == 1 ? cr1 : q == 2 ? cr2 : cr3;
       rows[s * NK + lane] = crow;
       const unsigned m = __ballot_sync(0xffffffffu, crow >= 0);
       __syncwarp();
-      if (lane == 0) mbar_arrive_expect_tx(full0 + 8 * s, (uint32_t)__popc(m) * (uint32_t)D);
+      if (lane == 0) mbar_arrive_expect_tx(bar(kRawFull + s), (uint32_t)__popc(m) * (uint32_t)D);
       __syncwarp();
-      if (crow >= 0) tma_bulk_g2s(sRaw + (s * NK + lane) * D, a.cache + (int64_t)crow * D, D, full0 + 8 * s, pol);
+      if (crow >= 0)
+        tma_bulk_g2s(sRaw + (s * NK + lane) * D, a.cache + (int64_t)crow * D, D, bar(kRawFull + s), pol);
       if (lane == 0) { MLA_TRACE(i, 0) }
       issued = i + 1;
     }
     // no copy may still be in flight when the CTA exits
     if (lane == 0)
       for (int i = max(0, issued - RS); i < issued; ++i) {
-        volatile int dummy_abort = 0;
-        mbar_wait(full0 + 8 * (i % RS), (i / RS) & 1, a.err, 7102, &dummy_abort, a.timeout_ns);
+        volatile int no_abort = 0;
+        mbar_wait(bar(kRawFull + i % RS), (i / RS) & 1, a.err, 7102, &no_abort, a.timeout_ns);
       }
     __syncwarp();
-  } else {
-    // ------------------------------------------------------------------------------------ compute warps
-    const uint32_t idesc_s = umma_idesc_f16(128, NK, 0);
-    const uint32_t idesc_pv = umma_idesc_f16(128, HGp, 0) | (1u << 15);  // A (V^T) MN-major
-    float m_run = -INFINITY, l_run = 0.f;
-    const bool head_lane = warp < 2 && warp * 32 + lane < HGp;
-    const int h = warp * 32 + lane;
-    int pv_issued = 0;
-    bool failed = false;
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------------------------------ converters
+    const int tc = tid - 128, j = tc >> 2, q = tc & 3;
+    const uint32_t c_lo = ((2 * q) ^ (j & 7)) << 4, c_hi = ((2 * q + 1) ^ (j & 7)) << 4;
     for (int i = 0; i < nc; ++i) {
-      const int s = i % RS;
-      bool ok = mbar_wait_warp(full0 + 8 * s, (i / RS) & 1, a.err, 7103, abort_w, a.timeout_ns);
-      if (ok && i > 0) ok = mbar_wait_warp(bar_pv, (i - 1) & 1, a.err, 7104, abort_w, a.timeout_ns);
+      const int s = i % RS, kb2 = i & 1;
+      if (!mbar_wait_warp(bar(kRawFull + s), (i / RS) & 1, a.err, 7103, abort_w, a.timeout_ns)) break;
+      // the whole row slice of this thread into registers, then the stage is free for the loader
+      const int row = rows[s * NK + j];
+      const unsigned vmask = __ballot_sync(0xffffffffu, rows[s * NK + lane] >= 0);
+      uint4 v[kMaxKB];
+      const uint32_t src = sRaw + (s * NK + j) * D + q * 16;
+#pragma unroll
+      for (int kb = 0; kb < kMaxKB; ++kb)
+        v[kb] = (kb < nkb && row >= 0) ? lds128_nc(src + kb * 64) : make_uint4(0u, 0u, 0u, 0u);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kRawEmpty + s));
+      if (i >= 2 && !mbar_wait_warp(bar(kKcEmpty + kb2), ((i >> 1) - 1) & 1, a.err, 7104, abort_w, a.timeout_ns))
+        break;
+      if (i < 62 && tc == 0) { MLA_TRACE(i, 1) }
+      const uint32_t dst = sK + kb2 * kc_bytes + j * 128;
+#pragma unroll
+      for (int kb = 0; kb < kMaxKB; ++kb) {
+        if (kb < nkb) {
+          const uint32_t r = dst + kb * (NK * 128);
+          sts128(r + c_lo, fp8x2_to_h2(v[kb].x), fp8x2_to_h2(v[kb].x >> 16), fp8x2_to_h2(v[kb].y),
+                 fp8x2_to_h2(v[kb].y >> 16));
+          sts128(r + c_hi, fp8x2_to_h2(v[kb].z), fp8x2_to_h2(v[kb].z >> 16), fp8x2_to_h2(v[kb].w),
+                 fp8x2_to_h2(v[kb].w >> 16));
+        }
+      }
+      if (tc == 0) vm_sm[kb2] = vmask;
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kKcFull + kb2));
+      if (tc == 0) { MLA_TRACE(i, 2) }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_s = umma_idesc_f16(64, NK, 0);
+      const uint32_t idesc_pv = umma_idesc_f16(128, HGp, 0) | (1u << 15);  // A (V^T) MN-major
+      const uint64_t qd0 = umma_desc_sw128(sQ);
+      int s_issued = 0, pv_issued = 0;
+      for (int i = 0; i <= nc; ++i) {
+        if (i < nc) {
+          const int kb2 = i & 1;
+          if (!mbar_wait(bar(kKcFull + kb2), (i >> 1) & 1, a.err, 7105, abort_w, a.timeout_ns)) break;
+          MLA_TRACE(i, 7)
+          tc_fence_after();
+          const uint64_t kd0 = umma_desc_sw128(sK + kb2 * kc_bytes);
+          // the 16-wide K steps of each 64-column block go to NACC separate accumulators (summed by the softmax)
+          const uint32_t d_s = tmem + kb2 * NACC * NK;
+          for (int kb = 0; kb < nkb; ++kb) {
+            const uint64_t qd = qd0 + (uint64_t)((kb * HGp * 128) >> 4), kd = kd0 + (uint64_t)((kb * NK * 128) >> 4);
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4)
+              umma_f16(d_s + (k4 % NACC) * NK, qd + 2 * k4, kd + 2 * k4, idesc_s, (kb > 0 || k4 >= NACC) ? 1u : 0u);
+          }
+          umma_commit(bar(kSFull + kb2));
+          s_issued = i + 1;
+          MLA_TRACE(i, 3)
+        }
+        if (i > 0) {
+          const int pi = i - 1, pb = pi & 1;
+          if (!mbar_wait(bar(kPFull + pb), (pi >> 1) & 1, a.err, 7106, abort_w, a.timeout_ns)) break;
+          tc_fence_after();
+          const uint64_t ad0 = umma_desc_sw128_mn(sK + pb * kc_bytes, NK * 128, 1024);
+          const uint64_t bd0 = umma_desc_sw128(sP + pb * p_bytes);
+#pragma unroll
+          for (int ks = 0; ks < NK / 16; ++ks)  // tiles inner: consecutive MMAs write different accumulators
+            for (int mt = 0; mt < n_mt; ++mt)
+              umma_f16(tmem + O0 + mt * HGp, ad0 + (uint64_t)(((2 * mt) * NK * 128 + (2 * ks) * 1024) >> 4),
+                       bd0 + 2 * ks, idesc_pv, (pi > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(bar(kKcEmpty + pb));
+          umma_commit(bar(kPvDone));
+          pv_issued = pi + 1;
+          MLA_TRACE(pi, 6)
+        }
+      }
+      // every issued MMA has finished before TMEM is released
+      volatile int no_abort = 0;
+      if (pv_issued > 0) mbar_wait(bar(kPvDone), (pv_issued - 1) & 1, a.err, 7107, &no_abort, a.timeout_ns);
+      if (s_issued > pv_issued)
+        mbar_wait(bar(kSFull + ((s_issued - 1) & 1)), ((s_issued - 1) >> 1) & 1, a.err, 7108, &no_abort,
+                  a.timeout_ns);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------------------------ softmax + epilogue
+    float m_run = -INFINITY, l_run = 0.f;
+    const int h = warp * 16 + lane;              // M = 64 score rows: head 16w + l in TMEM lane 32w + l
+    const bool head_lane = lane < 16 && h < HGp;
+    bool failed = false;
+    int done = 0;
+    for (int i = 0; i < nc; ++i) {
+      const int kb2 = i & 1;
+      bool ok = mbar_wait_warp(bar(kSFull + kb2), (i >> 1) & 1, a.err, 7109, abort_w, a.timeout_ns);
+      if (ok) ok = mbar_wait_warp(bar(kKcFull + kb2), (i >> 1) & 1, a.err, 7110, abort_w, a.timeout_ns);
       if (bar_any(1, 128, !ok || *abort_w)) {
         failed = true;
         break;
       }
-      if (tid == 0) { MLA_TRACE(i, 1) }
-      // key validity of this chunk, then fp8 -> fp16 K-major tile
-      const int* rw = rows + s * NK;
-      const unsigned vmask = __ballot_sync(0xffffffffu, rw[lane] >= 0);
-      {
-        // thread -> key j = tid / 4 and 16-byte unit q = tid % 4 of each 64-column block (NK = 32 keys x 4 units)
-        const int j = tid >> 2, q = tid & 3;
-        const bool valid = (vmask >> j) & 1u;
-        const uint32_t src = sRaw + (s * NK + j) * D + q * 16;
-        const uint32_t dst = sK + j * 128;
-        const uint32_t c_lo = ((2 * q) ^ (j & 7)) << 4, c_hi = ((2 * q + 1) ^ (j & 7)) << 4;
-        for (int kb = 0; kb < D / 64; ++kb) {
-          uint32_t o[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-          if (valid) {
-            const uint4 v = lds128(src + kb * 64);
-            o[0] = fp8x2_to_h2(v.x);
-            o[1] = fp8x2_to_h2(v.x >> 16);
-            o[2] = fp8x2_to_h2(v.y);
-            o[3] = fp8x2_to_h2(v.y >> 16);
-            o[4] = fp8x2_to_h2(v.z);
-            o[5] = fp8x2_to_h2(v.z >> 16);
-            o[6] = fp8x2_to_h2(v.w);
-            o[7] = fp8x2_to_h2(v.w >> 16);
-          }
-          const uint32_t row = dst + kb * (NK * 128);
-          sts128(row + c_lo, o[0], o[1], o[2], o[3]);
-          sts128(row + c_hi, o[4], o[5], o[6], o[7]);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty0 + 8 * s);
-      fence_proxy_async_smem();
-      named_barrier(1, 128);
-      if (tid == 0) {
-        MLA_TRACE(i, 2)
-        tc_fence_after();
-        // descriptors are affine in the address (bits 0-13 hold addr >> 4): step them instead of rebuilding
-        const uint64_t qd0 = umma_desc_sw128(sQ), kd0 = umma_desc_sw128(sK);
-        for (int kb = 0; kb < D / 64; ++kb) {
-          const uint64_t qd = qd0 + (uint64_t)((kb * HGp * 128) >> 4), kd = kd0 + (uint64_t)((kb * NK * 128) >> 4);
-#pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4)
-            umma_f16(tmem, qd + 2 * k4, kd + 2 * k4, idesc_s, (kb | k4) ? 1u : 0u);
-        }
-        umma_commit(bar_s);
-      }
-      ok = mbar_wait_warp(bar_s, i & 1, a.err, 7105, abort_w, a.timeout_ns);
-      if (bar_any(1, 128, !ok)) {
-        failed = true;
-        break;
-      }
       tc_fence_after();
-      if (tid == 0) { MLA_TRACE(i, 3) }
-      bool need = false;
-      if (warp < 2) {
-        uint32_t r0[16], r1[16];
-        const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16);
-        tmem_ld16(ta, r0);
-        tmem_ld16(ta + 16, r1);
+      if (tid == 0) { MLA_TRACE(i, 4) }
+      const unsigned vmask = vm_sm[kb2];
+      float sv[NK];
+      {
+        const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + kb2 * NACC * NK;
+        uint32_t r[NACC][NK];
+#pragma unroll
+        for (int k = 0; k < NACC; ++k) {
+          tmem_ld16(ta + k * NK, *reinterpret_cast<uint32_t(*)[16]>(&r[k][0]));
+          tmem_ld16(ta + k * NK + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[k][16]));
+        }
         tmem_ld_wait();
-        if (head_lane) {
-          float sv[NK];
-          float mx = -INFINITY;
 #pragma unroll
-          for (int j = 0; j < NK; ++j) {
-            const float x = __uint_as_float(j < 16 ? r0[j] : r1[j - 16]) * a.scale_log2;
-            sv[j] = ((vmask >> j) & 1u) ? x : -INFINITY;
-            mx = fmaxf(mx, sv[j]);
-          }
-          float corr = 1.f;
-          if (mx > m_run + kRescaleLog2) {   // also true when m_run is -inf and the chunk has a valid key
-            corr = m_run == -INFINITY ? 0.f : ex2_fast(m_run - mx);
-            m_run = mx;
-            need = i > 0;
-          }
-          uint32_t pw[NK / 2];
-          float sum = 0.f;
+        for (int jj = 0; jj < NK; ++jj) {
+          float x = 0.f;
 #pragma unroll
-          for (int j = 0; j < NK; j += 2) {
-            const float p0 = (h < hn && sv[j] != -INFINITY) ? ex2_fast(sv[j] - m_run) : 0.f;
-            const float p1 = (h < hn && sv[j + 1] != -INFINITY) ? ex2_fast(sv[j + 1] - m_run) : 0.f;
-            const __half2 hp = __floats2half2_rn(p0, p1);
-            const float2 back = __half22float2(hp);
-            sum += back.x + back.y;
-            pw[j / 2] = *reinterpret_cast<const uint32_t*>(&hp);
-          }
-          l_run = l_run * corr + sum;
-          corr_sm[h] = corr;
-          const uint32_t prow = sP + h * 128;
-#pragma unroll
-          for (int c = 0; c < NK / 8; ++c)
-            sts128(prow + ((c ^ (h & 7)) << 4), pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
+          for (int k = 0; k < NACC; ++k) x += __uint_as_float(r[k][jj]);
+          sv[jj] = ((vmask >> jj) & 1u) ? x * a.scale_log2 : -INFINITY;
         }
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      const bool rescale = bar_any(1, 128, need);
-      if (rescale) {
-        // O^T[:, h] *= corr[h] (each lane is one latent dim of each 128-row tile)
-        const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + O0;
+      bool need = false;
+      if (head_lane) {
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int jj = 0; jj < NK; ++jj) mx4[jj & 3] = fmaxf(mx4[jj & 3], sv[jj]);
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+        float corr = 1.f;
+        if (mx > m_run + kRescaleLog2) {   // also true when m_run is -inf and the chunk has a valid key
+          corr = m_run == -INFINITY ? 0.f : ex2_fast(m_run - mx);
+          m_run = mx;
+          need = i > 0;
+        }
+        uint32_t pw[NK / 2];
+        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+        // padding heads, and heads with no valid key yet: every p is exp2(-inf) = 0
+        const float mref = (h < hn && m_run != -INFINITY) ? m_run : INFINITY;
+#pragma unroll
+        for (int jj = 0; jj < NK; jj += 2) {
+          const float p0 = ex2_fast(sv[jj] - mref), p1 = ex2_fast(sv[jj + 1] - mref);
+          const __half2 hp = __floats2half2_rn(p0, p1);
+          const float2 back = __half22float2(hp);
+          sum4[(jj >> 1) & 3] += back.x + back.y;
+          pw[jj / 2] = *reinterpret_cast<const uint32_t*>(&hp);
+        }
+        l_run = l_run * corr + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+        corr_sm[h] = corr;
+        const uint32_t prow = sP + kb2 * p_bytes + h * 128;
+#pragma unroll
+        for (int c = 0; c < NK / 8; ++c)
+          sts128(prow + ((c ^ (h & 7)) << 4), pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
+      }
+      if (bar_any(1, 128, need)) {
+        // O^T[:, h] *= corr[h] once the previous P.V has landed (each lane is one latent dim of each tile)
+        ok = mbar_wait_warp(bar(kPvDone), (i - 1) & 1, a.err, 7111, abort_w, a.timeout_ns);
+        if (bar_any(1, 128, !ok)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t to = tmem + ((uint32_t)(warp * 32) << 16) + O0;
         for (int mt = 0; mt < n_mt; ++mt)
           for (int c16 = 0; c16 < HGp / 16; ++c16) {
             uint32_t r[16];
-            tmem_ld16(ta + mt * HGp + c16 * 16, r);
+            tmem_ld16(to + mt * HGp + c16 * 16, r);
             tmem_ld_wait();
 #pragma unroll
             for (int k = 0; k < 16; ++k) r[k] = __float_as_uint(__uint_as_float(r[k]) * corr_sm[c16 * 16 + k]);
-            tmem_st16(ta + mt * HGp + c16 * 16, r);
+            tmem_st16(to + mt * HGp + c16 * 16, r);
           }
         tmem_st_wait();
-        tc_fence_before();
-        named_barrier(1, 128);
       }
-      if (tid == 0) {
-        MLA_TRACE(i, 4)
-        tc_fence_after();
-        const uint64_t ad0 = umma_desc_sw128_mn(sK, NK * 128, 1024), bd0 = umma_desc_sw128(sP);
-        for (int mt = 0; mt < n_mt; ++mt)
-#pragma unroll
-          for (int ks = 0; ks < NK / 16; ++ks)
-            umma_f16(tmem + O0 + mt * HGp, ad0 + (uint64_t)(((2 * mt) * NK * 128 + (2 * ks) * 1024) >> 4),
-                     bd0 + 2 * ks, idesc_pv, (i > 0 || ks > 0) ? 1u : 0u);
-        umma_commit(bar_pv);
-        MLA_TRACE(i, 5)
-      }
-      pv_issued = i + 1;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kPFull + kb2));
+      if (tid == 0) { MLA_TRACE(i, 5) }
+      done = i + 1;
     }
-    // last P.V done (also on the failure path, so that TMEM is not released under a running MMA)
+    // last P.V done
     bool have_o = false;
-    if (pv_issued > 0) {
-      volatile int dummy_abort = 0;
-      have_o = mbar_wait_warp(bar_pv, (pv_issued - 1) & 1, a.err, 7106, failed ? &dummy_abort : abort_w,
-                              a.timeout_ns) && !failed;
-    }
-    have_o = !bar_any(1, 128, !have_o) && pv_issued == nc && nc > 0;
+    if (!failed && done == nc && nc > 0)
+      have_o = mbar_wait_warp(bar(kPvDone), (nc - 1) & 1, a.err, 7112, abort_w, a.timeout_ns);
+    have_o = !bar_any(1, 128, !have_o);
     tc_fence_after();
     if (head_lane) l_sm[h] = l_run;
     named_barrier(1, 128);
@@ -502,7 +560,6 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaTcArgs a) 
   }
   tc_fence_before();
   __syncthreads();
-  if (tid == 0) { MLA_TRACE(63, 6) }
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, tcols);
 }
@@ -543,7 +600,9 @@ int sm_count_cached() {
   return n;
 }
 
-bool tc_supported(int64_t kvr, int64_t dr) { return kvr % 128 == 0 && kvr <= 1024 && (kvr + dr) % 64 == 0 && dr % 8 == 0; }
+bool tc_supported(int64_t kvr, int64_t dr) {
+  return kvr % 128 == 0 && kvr <= 1024 && (kvr + dr) % 64 == 0 && (kvr + dr) / 64 <= kMaxKB && dr % 8 == 0;
+}
 
 void d3_mla_attn_tc(torch::Tensor q_lat, torch::Tensor q_pe, torch::Tensor cache, torch::Tensor block_table,
                     torch::Tensor slots, torch::Tensor positions, int64_t n_tok, c10::optional<torch::Tensor> sel,
@@ -583,10 +642,10 @@ void d3_mla_attn_tc(torch::Tensor q_lat, torch::Tensor q_pe, torch::Tensor cache
   }
   a.window = window;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
-  // heads per CTA: O^T needs (kvr / 128) x HGp TMEM columns next to the 32 score columns, and Q, the key tile
-  // and at least two loader stages must fit in shared memory
-  int hgp = std::min(std::min(64, 448 / (a.kvr / 128) / 16 * 16), (int)((a.H + 15) / 16 * 16));
-  while (hgp > 16 && smem_plan(a.D, hgp, 2).total > 227 * 1024) hgp -= 16;
+  // heads per CTA: O^T needs (kvr / 128) x HGp TMEM columns next to the double-buffered score accumulators,
+  // and Q, the two key tiles and a loader stage must fit in shared memory
+  int hgp = std::min(std::min(64, (512 - 2 * NACC * NK) / (a.kvr / 128) / 16 * 16), (int)((a.H + 15) / 16 * 16));
+  while (hgp > 16 && smem_plan(a.D, hgp, 1).total > 227 * 1024) hgp -= 16;
   a.HGp = hgp;
   const int G = (a.H + a.HGp - 1) / a.HGp;
   int stages = kMaxStages;
