@@ -89,6 +89,47 @@ __global__ void __launch_bounds__(256) add_rms_kernel(float* h, const float* y, 
   for (int i = threadIdx.x; i < n; i += blockDim.x) stf(out + row * n + i, hr[i] * r * w[i]);
 }
 
+// Same, for n % 4 == 0 and n <= 4 * 256 * NV: float4 accesses, the row kept in registers between the two passes.
+template <typename OT, int NV>
+__global__ void __launch_bounds__(256) add_rms_vec_kernel(float* h, const float* y, const float* w, int n, float eps,
+                                                          OT* out) {
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  float4* hr = reinterpret_cast<float4*>(h + row * n);
+  const float4* yr = y ? reinterpret_cast<const float4*>(y + row * n) : nullptr;
+  const int n4 = n >> 2;
+  float4 v[NV];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = threadIdx.x + k * 256;
+    v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < n4) {
+      v[k] = hr[i];
+      if (yr) {
+        const float4 u = yr[i];
+        v[k].x += u.x; v[k].y += u.y; v[k].z += u.z; v[k].w += u.w;
+        hr[i] = v[k];
+      }
+      ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+    }
+  }
+  const float r = rsqrtf(bsum(ss, red) / n + eps);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = threadIdx.x + k * 256;
+    if (i < n4) {
+      const float4 g = w4[i];
+      OT* o = out + row * n + 4 * i;
+      stf(o, v[k].x * r * g.x);
+      stf(o + 1, v[k].y * r * g.y);
+      stf(o + 2, v[k].z * r * g.z);
+      stf(o + 3, v[k].w * r * g.w);
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------ MLA prep
 struct PrepArgs {
   const float* P;
@@ -173,6 +214,7 @@ __global__ void __launch_bounds__(256) mla_prep_kernel(PrepArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------ q split
+// grid (rows, head groups of 8 then index-head groups of 8): enough blocks to cover the SMs at decode sizes
 __global__ void __launch_bounds__(256) mla_qsplit_kernel(const float* Q, int ldQ, int H, int dn, int dr, int iH,
                                                          int iD, const float* rope, int rope_len,
                                                          const int* positions, int n_tok, int T,
@@ -181,29 +223,35 @@ __global__ void __launch_bounds__(256) mla_qsplit_kernel(const float* Q, int ldQ
   const int pos = positions[row / n_tok] + row % n_tok;
   const float* rp = rope + (int64_t)min(pos, rope_len - 1) * dr;
   const float* q = Q + (int64_t)row * ldQ;
-  const int hd = dn + dr;
-  for (int i = threadIdx.x; i < H * hd; i += blockDim.x) {
-    const int h = i / hd, d = i % hd;
-    if (d < dn) {
-      q_nope[((int64_t)h * T + row) * dn + d] = __float2bfloat16_rn(q[i]);
-    } else {
-      const int e = d - dn, p2 = e >> 1;
-      const float c = rp[2 * p2], s = rp[2 * p2 + 1];
-      const float v = (e & 1) ? q[i] * c + q[i - 1] * s : q[i] * c - q[i + 1] * s;
-      q_pe[((int64_t)row * H + h) * dr + e] = v;
+  const int hd = dn + dr, hgroups = (H + 7) / 8;
+  if ((int)blockIdx.y < hgroups) {
+    const int h0 = blockIdx.y * 8, nh = min(8, H - h0);
+    for (int i = threadIdx.x; i < nh * hd; i += blockDim.x) {
+      const int hl = i / hd, d = i - hl * hd, h = h0 + hl;
+      const float* qh = q + (int64_t)h * hd;
+      if (d < dn) {
+        q_nope[((int64_t)h * T + row) * dn + d] = __float2bfloat16_rn(qh[d]);
+      } else {
+        const int e = d - dn, p2 = e >> 1;
+        const float c = rp[2 * p2], sn = rp[2 * p2 + 1];
+        const float v = (e & 1) ? qh[d] * c + qh[d - 1] * sn : qh[d] * c - qh[d + 1] * sn;
+        q_pe[((int64_t)row * H + h) * dr + e] = v;
+      }
     }
+    return;
   }
   if (!iq) return;
-  const float* qi = q + H * hd;
-  for (int i = threadIdx.x; i < iH * iD; i += blockDim.x) {
+  const int g0 = (blockIdx.y - hgroups) * 8, ng = min(8, iH - g0);
+  const float* qi = q + (int64_t)H * hd + (int64_t)g0 * iD;
+  for (int i = threadIdx.x; i < ng * iD; i += blockDim.x) {
     const int e = i % iD;
     float v = qi[i];
     if (e < dr) {
       const int p2 = e >> 1;
-      const float c = rp[2 * p2], s = rp[2 * p2 + 1];
-      v = (e & 1) ? qi[i] * c + qi[i - 1] * s : qi[i] * c - qi[i + 1] * s;
+      const float c = rp[2 * p2], sn = rp[2 * p2 + 1];
+      v = (e & 1) ? qi[i] * c + qi[i - 1] * sn : qi[i] * c - qi[i + 1] * sn;
     }
-    iq[(int64_t)row * iH * iD + i] = v;
+    iq[(int64_t)row * iH * iD + (int64_t)g0 * iD + i] = v;
   }
 }
 
@@ -393,12 +441,34 @@ __global__ void __launch_bounds__(256) mla_attn_kernel(AttnArgs a) {
   }
 }
 
+// grid (rows, head groups of 8); sigmoid(gate) once per head, 8 elements per thread when dv % 8 == 0
 __global__ void mla_out_kernel(const __nv_bfloat16* o, const float* gate, int H, int T, int dv, __half* out) {
-  const int t = blockIdx.x;
-  for (int i = threadIdx.x; i < H * dv; i += blockDim.x) {
-    const int h = i / dv, d = i % dv;
-    const float g = 1.f / (1.f + __expf(-gate[(int64_t)t * H + h]));
-    out[(int64_t)t * H * dv + i] = __float2half_rn(__bfloat162float(o[((int64_t)h * T + t) * dv + d]) * g);
+  __shared__ float gs[8];
+  const int t = blockIdx.x, h0 = blockIdx.y * 8, nh = min(8, H - h0);
+  if ((int)threadIdx.x < nh) gs[threadIdx.x] = 1.f / (1.f + __expf(-gate[(int64_t)t * H + h0 + threadIdx.x]));
+  __syncthreads();
+  if (dv % 8 == 0) {
+    const int per = dv / 8;
+    for (int i = threadIdx.x; i < nh * per; i += blockDim.x) {
+      const int hl = i / per, d0 = (i - hl * per) * 8, h = h0 + hl;
+      const uint4 v = *reinterpret_cast<const uint4*>(o + ((int64_t)h * T + t) * dv + d0);
+      const float g = gs[hl];
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+      uint32_t r[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[k]));
+        const __half2 hh = __floats2half2_rn(f.x * g, f.y * g);
+        r[k] = *reinterpret_cast<const uint32_t*>(&hh);
+      }
+      *reinterpret_cast<uint4*>(out + (int64_t)t * H * dv + (int64_t)h * dv + d0) = make_uint4(r[0], r[1], r[2], r[3]);
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < nh * dv; i += blockDim.x) {
+    const int hl = i / dv, d = i % dv, h = h0 + hl;
+    out[(int64_t)t * H * dv + (int64_t)h * dv + d] =
+        __float2half_rn(__bfloat162float(o[((int64_t)h * T + t) * dv + d]) * gs[hl]);
   }
 }
 
@@ -467,6 +537,23 @@ void d3_add_rms(torch::Tensor h, c10::optional<torch::Tensor> y, torch::Tensor w
   if (y) CK(y->scalar_type() == torch::kFloat && y->is_contiguous() && y->sizes() == h.sizes());
   if (!T) return;
   const float* yp = y ? y->data_ptr<float>() : nullptr;
+  if (n % 4 == 0 && n <= 4 * 256 * 8) {
+    const int nv = (n / 4 + 255) / 256;
+#define ARV(OT, PTR)                                                                                   \
+  if (nv <= 2) add_rms_vec_kernel<OT, 2><<<T, 256, 0, STREAM>>>(h.data_ptr<float>(), yp, w.data_ptr<float>(), n, \
+                                                               (float)eps, PTR);                        \
+  else if (nv <= 4) add_rms_vec_kernel<OT, 4><<<T, 256, 0, STREAM>>>(h.data_ptr<float>(), yp, w.data_ptr<float>(), \
+                                                                    n, (float)eps, PTR);                \
+  else add_rms_vec_kernel<OT, 8><<<T, 256, 0, STREAM>>>(h.data_ptr<float>(), yp, w.data_ptr<float>(), n, (float)eps, PTR);
+    if (out.scalar_type() == torch::kHalf) {
+      ARV(__half, (__half*)out.data_ptr())
+    } else {
+      CK(out.scalar_type() == torch::kFloat);
+      ARV(float, out.data_ptr<float>())
+    }
+#undef ARV
+    return;
+  }
   if (out.scalar_type() == torch::kHalf)
     add_rms_kernel<__half><<<T, 256, 0, STREAM>>>(h.data_ptr<float>(), yp, w.data_ptr<float>(), n, (float)eps,
                                                  (__half*)out.data_ptr());
@@ -519,7 +606,8 @@ void d3_mla_qsplit(torch::Tensor Q, int64_t H, int64_t dn, int64_t dr, int64_t i
   CK(q_nope.scalar_type() == torch::kBFloat16 && q_nope.size(0) == H && q_nope.size(1) == T && q_nope.size(2) == dn);
   CK(q_pe.size(0) == T && q_pe.size(1) == H && q_pe.size(2) == dr && rope.size(1) == dr / 2);
   if (!T) return;
-  mla_qsplit_kernel<<<T, 256, 0, STREAM>>>(Q.data_ptr<float>(), Q.size(1), H, dn, dr, iH, iD, rope.data_ptr<float>(),
+  const int gy = (int)((H + 7) / 8 + (iq ? (iH + 7) / 8 : 0));
+  mla_qsplit_kernel<<<dim3(T, gy), 256, 0, STREAM>>>(Q.data_ptr<float>(), Q.size(1), H, dn, dr, iH, iD, rope.data_ptr<float>(),
                                           rope.size(0), positions.data_ptr<int32_t>(), n_tok, T,
                                           (__nv_bfloat16*)q_nope.data_ptr(), q_pe.data_ptr<float>(),
                                           iq ? iq->data_ptr<float>() : nullptr);
@@ -603,8 +691,9 @@ void d3_mla_attn(torch::Tensor q_lat, torch::Tensor q_pe, torch::Tensor cache, t
 void d3_mla_out(torch::Tensor o, torch::Tensor gate, torch::Tensor out) {
   const int H = o.size(0), T = o.size(1), dv = o.size(2);
   CK(o.scalar_type() == torch::kBFloat16 && out.scalar_type() == torch::kHalf && out.size(1) == H * dv);
-  if (T) mla_out_kernel<<<T, 256, 0, STREAM>>>((const __nv_bfloat16*)o.data_ptr(), gate.data_ptr<float>(), H, T, dv,
-                                              (__half*)out.data_ptr());
+  CK(o.is_contiguous() && out.is_contiguous());
+  if (T) mla_out_kernel<<<dim3(T, (H + 7) / 8), 256, 0, STREAM>>>((const __nv_bfloat16*)o.data_ptr(), gate.data_ptr<float>(),
+                                                                 H, T, dv, (__half*)out.data_ptr());
 }
 
 void d3_route(torch::Tensor logits, int64_t E, torch::Tensor bias, int64_t k, double scale, torch::Tensor ids,

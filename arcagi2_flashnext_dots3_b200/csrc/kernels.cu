@@ -13,6 +13,7 @@ void register_ple(pybind11::module& m);
 void register_gemv(pybind11::module& m);
 void register_tp(pybind11::module& m);
 void register_mla(pybind11::module& m);
+void register_dsa(pybind11::module& m);
 
 void register_kernels(pybind11::module& m) {
   register_fn(m);
@@ -24,4 +25,5 @@ void register_kernels(pybind11::module& m) {
   register_gemv(m);
   register_tp(m);
   register_mla(m);
+  register_dsa(m);
 }

@@ -104,3 +104,51 @@ def to_engine(W: dict, cfg, device) -> dict:
                         "d": _ws(L["mlp"]["d"], cfg, dev)}
         E["layers"].append(M)
     return E
+
+
+def random_engine(cfg, device, seed: int = 0, tp=None) -> dict:
+    """Engine-form weights of the configured size generated and packed on `device`, without the dense fp32 copies
+    of :func:`random_dense` (the full 144-expert model would need ~0.6 TB of them): dense weights N(0, 0.02) in
+    their storage formats (fp16 fused down projection, block-FP8 elsewhere), experts N(0, 0.02) RTN-quantized to
+    ``cfg.bits_of(e)`` bits with group-128 scales. ``tp=(rank, world)`` builds one tensor-parallel rank's shard
+    (its heads, its contiguous expert range); pass the matching :func:`..parallel.tp.tp_config` view to the model."""
+    from .fn_weights import _random_experts
+    dev = torch.device(device)
+    rank, world = tp if tp is not None else (0, 1)
+    g = torch.Generator(device=dev).manual_seed(seed * 1000 + rank)
+    Hd, dn, dr, dv, qr = cfg.hidden_size, cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim, cfg.q_lora_rank
+
+    def rn(*s, std=STD):
+        return torch.randn(*s, generator=g, device=dev) * std
+
+    def ws16(rows, K):
+        return wgemm.build_weight_set([rt.pack_f16(rn(rows, K))], [16], rows, K, device=dev)
+
+    low = torch.float32 if dev.type == "cpu" else torch.bfloat16
+    E = {"embed": rn(cfg.vocab_size, Hd, std=1.0).to(low), "lm_head": _ws(rn(cfg.vocab_size, Hd), cfg, dev),
+         "norm": 1.0 + rn(Hd, std=0.1), "layers": []}
+    for l in range(cfg.num_layers):
+        H = cfg.heads_of(l) // world
+        kvr = cfg.latent_of(l)
+        dsa = cfg.layer_kind(l) == "dsa"
+        iH, iD = (cfg.index_heads, cfg.index_dim) if dsa else (0, 0)
+        rows_a = qr + kvr + dr + H + iD + iH
+        M = {"ln1": 1.0 + rn(Hd, std=0.1), "ln2": 1.0 + rn(Hd, std=0.1),
+             "attn": {"a": ws16(rows_a, Hd), "qb": _ws(rn(H * (dn + dr) + iH * iD, qr), cfg, dev),
+                      "uk": rn(H, dn, kvr, std=0.05).to(low),
+                      "uv": rn(H, dv, kvr, std=0.05).to(low),
+                      "o": _ws(rn(Hd, H * dv), cfg, dev),
+                      "q_ln": 1.0 + rn(qr, std=0.1), "kv_ln": 1.0 + rn(kvr, std=0.1), "kr_ln": 1.0 + rn(dr, std=0.1)}}
+        if dsa:
+            M["attn"].update({"ik_w": 1.0 + rn(iD, std=0.1), "ik_b": rn(iD, std=0.1)})
+        if cfg.is_moe(l):
+            e0, e1 = rank * cfg.n_experts // world, (rank + 1) * cfg.n_experts // world
+            gu, d = _random_experts(cfg, g, dev, lo=e0, hi=e1)
+            M["moe"] = {"router": ws16(cfg.n_experts, Hd), "bias": rn(cfg.n_experts, std=0.1), "gu": gu, "d": d,
+                        "sgu": _ws(rn(2 * cfg.shared_inter, Hd), cfg, dev, silu_pairs=True),
+                        "sd": _ws(rn(Hd, cfg.shared_inter), cfg, dev), "expert_range": (e0, e1)}
+        else:
+            M["mlp"] = {"gu": _ws(rn(2 * cfg.dense_inter, Hd), cfg, dev, silu_pairs=True),
+                        "d": _ws(rn(Hd, cfg.dense_inter), cfg, dev)}
+        E["layers"].append(M)
+    return E

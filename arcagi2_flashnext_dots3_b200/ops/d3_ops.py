@@ -116,13 +116,23 @@ def mla_qsplit(Q, cfg, l, rope, positions, n_tok):
     return q_nope, q_pe, iq
 
 
+_DSA_CUDA_CORE = os.environ.get("FW_DSA_CUDA_CORE", "0") == "1"   # force the CUDA-core indexer logits
+
+
 def dsa_select(iq, iw, idx_cache, slots, positions, n_tok, topk: int, max_len: int):
     """[T, topk] int32 selected key positions; a row whose first entry is -1 attends to all causal keys."""
     T = iq.shape[0]
     ld = (max_len + 255) // 256 * 256
     if _cuda(iq):
         scores = torch.empty(T, ld, dtype=torch.float32, device=iq.device)
-        native.C().d3_dsa_scores(iq, iw, idx_cache, slots, positions, n_tok, scores)
+        C = native.C()
+        if (not _DSA_CUDA_CORE and idx_cache.dtype == torch.bfloat16
+                and C.d3_dsa_tc_supported(iq.shape[1], iq.shape[2])):
+            # tcgen05 path (csrc/k_dsa.cu): keys as the MMA's M, one key per epilogue thread
+            C.d3_dsa_scores_tc(iq, iw, idx_cache, slots, positions, n_tok, scores, native.err_word(iq.device),
+                               native.DEFAULT_TIMEOUT_NS)
+        else:
+            C.d3_dsa_scores(iq, iw, idx_cache, slots, positions, n_tok, scores)
         sel = torch.empty(T, topk, dtype=torch.int32, device=iq.device)
         n_valid = (_pos(positions, n_tok) + 1).to(torch.int32)
         native.C().topk_rows(scores, n_valid, topk, sel)

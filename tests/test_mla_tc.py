@@ -92,3 +92,37 @@ def test_mla_tc_matches_cuda_core_kernel(monkeypatch):
     torch.cuda.synchronize()
     native.check_error(torch.device("cuda"))
     assert (a.float() - b.float()).abs().max() / b.float().abs().max() < 2e-2
+
+
+@pytest.mark.parametrize("iH,rows,ctx", [(64, 6, 3000), (16, 3, 300)])
+def test_dsa_scores_tc_matches_reference(iH, rows, ctx, monkeypatch):
+    """Indexer logits sum_h w_h relu(q_h . k_j) on tcgen05 against fp32 PyTorch; masked past each row's position."""
+    g = torch.Generator(device="cuda").manual_seed(iH)
+    iD, S, max_len = 128, rows + 1, ctx + 64
+    keys = (torch.randn(S, max_len, iD, generator=g, device="cuda") * 0.5).bfloat16()
+    iq = torch.randn(rows, iH, iD, generator=g, device="cuda") * 0.3
+    iw = torch.rand(rows, iH, generator=g, device="cuda")
+    slots = torch.randperm(S, generator=g, device="cuda")[:rows].to(torch.int32)
+    positions = torch.randint(1, ctx, (rows,), generator=g, device="cuda").to(torch.int32)
+    positions[0] = 5
+    ld = (max_len + 255) // 256 * 256
+    out = torch.empty(rows, ld, device="cuda")
+    native.C().d3_dsa_scores_tc(iq, iw, keys, slots, positions, 1, out, native.err_word(torch.device("cuda")),
+                                native.DEFAULT_TIMEOUT_NS)
+    torch.cuda.synchronize()
+    native.check_error(torch.device("cuda"))
+    for r in range(rows):
+        p = int(positions[r])
+        k = keys[int(slots[r]), : p + 1].float()
+        ref = (torch.relu(iq[r].bfloat16().float() @ k.t()) * iw[r][:, None]).sum(0)
+        got = out[r, : p + 1]
+        assert (got - ref).abs().max() / ref.abs().max() < 1e-3, r
+        assert bool((out[r, p + 1:] == -torch.finfo(torch.float32).max).all())
+    # the selection the engine builds on it agrees with the CUDA-core logits
+    monkeypatch.setattr(d3_ops, "_DSA_CUDA_CORE", False)
+    a = d3_ops.dsa_select(iq, iw, keys, slots, positions, 1, 64, max_len)
+    monkeypatch.setattr(d3_ops, "_DSA_CUDA_CORE", True)
+    b = d3_ops.dsa_select(iq, iw, keys, slots, positions, 1, 64, max_len)
+    for r in range(1, rows):
+        sa, sb = set(a[r].tolist()), set(b[r].tolist())
+        assert len(sa & sb) >= 60, (r, len(sa & sb))
