@@ -179,7 +179,7 @@ def gemv_grouped(xs16: torch.Tensor, ws: WeightSet, items: torch.Tensor, n_items
     xsum = torch.empty(R, K // 128, dtype=torch.int32, device=xs16.device)
     native.C().gemv_quant(xs16, xq, xsc, xsum)
     native.C().gemv_grouped(ws.blob, ws.exp_off, ws.exp_fmt, ws.row_tiles, ws.kg, items, n_items, max_items, xq, xsc,
-                            xsum, out, cols, epi, row_dst)
+                            xsum, out, cols, epi, row_dst, native.err_word(xs16.device), native.DEFAULT_TIMEOUT_NS)
     return out
 
 
