@@ -421,8 +421,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int g = wk.g0; g < wk.g1; ++g, ++k, ++j) {
         if ((int)(j % teams) != team) continue;
         const int s = k % S, p = j % P;
-        if (!mbar_wait(bar_w_full + 8 * s, (k / S) & 1, err, 4001, abort_flag, lim) ||
-            !mbar_wait(bar_ab_empty + 8 * p, ((j / P) & 1) ^ 1, err, 4002, abort_flag, lim)) {
+        // one poller per warp (a.dbg & 64: every thread polls, for comparison)
+        const bool waited = (a.dbg & 64)
+            ? (mbar_wait(bar_w_full + 8 * s, (k / S) & 1, err, 4001, abort_flag, lim) &&
+               mbar_wait(bar_ab_empty + 8 * p, ((j / P) & 1) ^ 1, err, 4002, abort_flag, lim))
+            : (mbar_wait_warp(bar_w_full + 8 * s, (k / S) & 1, err, 4001, abort_flag, lim) &&
+               mbar_wait_warp(bar_ab_empty + 8 * p, ((j / P) & 1) ^ 1, err, 4002, abort_flag, lim));
+        if (!waited) {
           ok = false;
           break;
         }

@@ -87,16 +87,30 @@ def bench_dense(args):
         x = torch.randn(T, K, device=dev).half()
         out = torch.empty(T, R, device=dev)
         t = _time(lambda: wgemm.matmul(x, ws, out=out), args.reps)
+        # device time without host launch gaps: 10 launches captured in one CUDA graph
+        wgemm.matmul(x, ws, out=out)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(10):
+                wgemm.matmul(x, ws, out=out)
+        t_graph = _time(g.replay, args.reps) / 10
         b = ws.nbytes()
         sweep = {}
         if args.sweep:
             for nt in (16, 32, 64):
                 for ks in (1, 2, 4, 8, 16):
                     if ks <= K // 128:
-                        sweep[f"n{nt}_k{ks}"] = round(1000 * _time(
-                            lambda: wgemm.matmul(x, ws, out=out, n_tile=nt, k_splits=ks), args.reps), 1)
+                        gs = torch.cuda.CUDAGraph()
+                        wgemm.matmul(x, ws, out=out, n_tile=nt, k_splits=ks)
+                        with torch.cuda.graph(gs):
+                            for _ in range(10):
+                                wgemm.matmul(x, ws, out=out, n_tile=nt, k_splits=ks)
+                        sweep[f"n{nt}_k{ks}"] = round(100 * _time(gs.replay, args.reps), 1)
+                        del gs
         print(json.dumps({"case": name, "rows": R, "K": K, "tokens": T, "ms": round(t, 4),
-                          "MB": round(b / 1e6, 2), "GBps": round(b / t / 1e6, 1), "sweep_us": sweep}))
+                          "graph_us": round(t_graph * 1e3, 1), "MB": round(b / 1e6, 2),
+                          "GBps": round(b / t_graph / 1e6, 1), "sweep_us": sweep}))
     native.check_error()
 
 

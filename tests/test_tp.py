@@ -29,3 +29,24 @@ def test_tp_two_gpus(comm):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     _run(2, comm, 29683 if comm == "fused" else 29685, {"NCCL_NVLS_ENABLE": "0", "TP_DEVICE": "cuda"})
+
+
+@pytest.mark.gpu
+def test_tp_reduce_wait_times_out_with_error_code():
+    """A source that never signals: the bounded wait of tp_reduce gives up, records 6401 + source and leaves the
+    context usable (no peer needed: both source slots live on this GPU)."""
+    from arcagi2_flashnext_dots3_b200.ops import native
+    dev = torch.device("cuda")
+    W, slot = 2, 4 * 256
+    buf = torch.zeros(2, W, slot, device=dev)
+    flags = torch.zeros(2, W, dtype=torch.int64, device=dev)
+    epoch = torch.ones(1, dtype=torch.int64, device=dev)
+    flags[1, 0] = 1          # source 0 signalled epoch 1 (parity 1); source 1 never does
+    h = torch.ones(4, 256, device=dev)
+    native.err_word(dev).zero_()
+    native.C().tp_reduce(buf, flags, W, 4 * 256, slot, epoch, h, True, native.err_word(dev), 50_000_000)
+    torch.cuda.synchronize()
+    with pytest.raises(native.DeviceWaitTimeout, match="6402"):
+        native.check_error(dev)
+    assert bool((h == 1).all())                    # nothing was added
+    assert float(torch.ones(3, device=dev).sum()) == 3.0   # the context still works
