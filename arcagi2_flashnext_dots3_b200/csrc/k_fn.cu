@@ -1438,7 +1438,7 @@ void register_fn(pybind11::module& m) {
 // Returns 0 on success, FW_NOALLOC_INVALID / FW_NOALLOC_TOO_BIG, or 1000 + cudaError_t.
 namespace {
 constexpr size_t kNoAllocScoreFloats = (size_t)1 << 19;
-__device__ __align__(256) float g_noalloc_scores[kNoAllocScoreFloats];
+static __device__ __align__(256) float g_noalloc_scores[kNoAllocScoreFloats];
 constexpr int kNoAllocMaxDevices = 64;
 std::atomic<float*> g_noalloc_ptr[kNoAllocMaxDevices];
 }  // namespace
