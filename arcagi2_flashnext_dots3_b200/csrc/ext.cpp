@@ -33,7 +33,8 @@ int* counter_pool(const torch::Device& dev, int64_t need) {
 }
 
 // y = x @ W^T with W in runtime tile blocks. x: fp16 [rows, K] (token matrix, K-contiguous).
-void wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, int64_t row_tiles, int64_t kg,
+// Returns the number of kernels launched (2 when the split-K partials get their own reduce launch).
+int64_t wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, int64_t row_tiles, int64_t kg,
            c10::optional<torch::Tensor> items, c10::optional<torch::Tensor> n_items, int64_t max_items,
            int64_t dense_T, torch::Tensor x, int64_t b_row0, torch::Tensor out, int64_t out_row0,
            int64_t out_cols, int64_t epi, bool accumulate, double alpha, int64_t n_tile, int64_t max_block_bytes,
@@ -141,21 +142,34 @@ void wgemm(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, in
   }
   a.k_splits = ks;
   torch::Tensor ws_t;
+  // split partials reduced by a second launch over all (tile, 16-token chunk) pairs instead of by the last split
+  // of each tile (FW_WGEMM_INKERNEL_REDUCE=1 always keeps the in-kernel reduction)
+  static const bool inkernel_reduce = getenv("FW_WGEMM_INKERNEL_REDUCE") && atoi(getenv("FW_WGEMM_INKERNEL_REDUCE"));
+  int64_t split_tiles = 0;
   if (ks > 1) {
-    const int64_t tiles = ((dense_T + n_tile - 1) / n_tile) * row_tiles;
-    ws_t = torch::empty({tiles * ks * n_tile * 128}, x.options().dtype(torch::kFloat));
+    split_tiles = ((dense_T + n_tile - 1) / n_tile) * row_tiles;
+    ws_t = torch::empty({split_tiles * ks * n_tile * 128}, x.options().dtype(torch::kFloat));
     a.workspace = ws_t.data_ptr<float>();
-    a.counters = counter_pool(x.device(), tiles);
+    // measured: gdn_out (4 splits) 29.5 -> 19.3 us, attn_o 26.0 -> 16.3 us; with 8 splits of a few tiles the extra
+    // launch costs more than the in-kernel reduction saves (router 12.9 -> 13.9 us)
+    a.ext_reduce = (inkernel_reduce || ks > 4) ? 0 : 1;
+    if (!a.ext_reduce) a.counters = counter_pool(x.device(), split_tiles);
   }
 
   CUtensorMap bmap;
   int rc = fw::make_tmap_2d_f16(&bmap, x.data_ptr(), x.size(0), x.size(1), x.size(1), 64, (uint32_t)n_tile, true);
   TORCH_CHECK(rc == 0, "cuTensorMapEncodeTiled failed: ", rc);
   const int64_t work = (dense_T >= 0 ? (dense_T + n_tile - 1) / n_tile : max_items) * row_tiles * ks;
-  if (work <= 0) return;
+  if (work <= 0) return 0;
   const int grid = (int)std::min<int64_t>((int64_t)sm_count() * cps, work);
   rc = fw::wgemm_launch(a, bmap, grid, at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(rc == 0, "wgemm launch failed: ", cudaGetErrorString((cudaError_t)rc));
+  if (a.ext_reduce) {
+    rc = fw::wgemm_splitk_reduce(a, (int)split_tiles, at::cuda::getCurrentCUDAStream());
+    TORCH_CHECK(rc == 0, "wgemm split-K reduce launch failed: ", cudaGetErrorString((cudaError_t)rc));
+    return 2;
+  }
+  return 1;
 }
 
 }  // namespace

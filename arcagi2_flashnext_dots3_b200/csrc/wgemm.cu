@@ -478,6 +478,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) part[((size_t)wk.split * N + c * 16 + i) * 128 + row] = __uint_as_float(v[i]);
         }
+      }
+      if (KS > 1 && emit && a.ext_reduce) {
+        emit = false;   // the follow-up reduce kernel sums and stores (stream order makes the partials visible)
+      } else if (KS > 1 && emit) {
+        const size_t tile_id = (size_t)wk.item * a.row_tiles + wk.tile;
         __threadfence();
         named_barrier(1, kEpiThreads);
         if (threadIdx.x == kEpiFirst) {
@@ -632,6 +637,89 @@ static int launch_n(const WGemmArgs& a, const CUtensorMap& map, int grid, size_t
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return (int)e;
   k<<<grid, kThreads, smem, st>>>(a, map);
+  return (int)cudaGetLastError();
+}
+
+// Split-K epilogue as its own launch: block (tile, chunk of 16 tokens), thread = weight row. The partials are
+// summed in split order (the same order, hence the same bits, as the in-kernel reduction) and the epilogue of the
+// GEMM is applied. silu(gate) * up: thread r < 64 sums gate row r and up row r + 64 of its tile.
+__global__ void __launch_bounds__(128) wgemm_splitk_reduce_kernel(const WGemmArgs a, int N, int KS) {
+  const int tile_id = blockIdx.x, c = blockIdx.y, row = threadIdx.x;
+  const int item = tile_id / a.row_tiles, tile = tile_id % a.row_tiles;
+  int e, t0, nt;
+  item_of(a, item, e, t0, nt);
+  const float* part = a.workspace + (size_t)tile_id * KS * N * 128;
+  const size_t orow0 = (size_t)(a.out_row0 + t0);
+  if (a.epi == WGEMM_EPI_STORE) {
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = 0.f;
+    for (int s = 0; s < KS; ++s) {
+      float t[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) t[i] = __ldcg(part + ((size_t)s * N + c * 16 + i) * 128 + row);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] += t[i];
+    }
+    const int col = tile * 128 + row;
+    if (col >= a.out_cols) return;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int n = c * 16 + i;
+      if (n >= nt) continue;
+      const float f = v[i] * a.alpha;
+      const size_t o = (orow0 + n) * a.out_ld + col;
+      if (a.fan_n > 0) {
+        const int64_t par = a.fan_epoch[0] & 1;
+        const int64_t off = (par * a.fan_n + a.fan_me) * a.fan_slot + o;
+        for (int pe = 0; pe < a.fan_n; ++pe) reinterpret_cast<float*>(a.fan_base[pe])[off] = f;
+      } else if (a.out_dtype == WGEMM_OUT_F32) {
+        float* op = reinterpret_cast<float*>(a.out) + o;
+        *op = a.accumulate ? *op + f : f;
+      } else if (a.out_dtype == WGEMM_OUT_BF16) {
+        reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(f);
+      } else {
+        reinterpret_cast<__half*>(a.out)[o] = __float2half_rn(f);
+      }
+    }
+  } else {
+    if (row >= 64) return;
+    float g[16], u[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) g[i] = u[i] = 0.f;
+    for (int s = 0; s < KS; ++s) {
+      float tg[16], tu[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        tg[i] = __ldcg(part + ((size_t)s * N + c * 16 + i) * 128 + row);
+        tu[i] = __ldcg(part + ((size_t)s * N + c * 16 + i) * 128 + row + 64);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        g[i] += tg[i];
+        u[i] += tu[i];
+      }
+    }
+    const int f = tile * 64 + row;
+    if (f >= a.out_cols) return;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int n = c * 16 + i;
+      if (n >= nt) continue;
+      const float y = silu_f(g[i]) * u[i];
+      const size_t o = (orow0 + n) * a.out_ld + f;
+      if (a.out_dtype == WGEMM_OUT_BF16)
+        reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(y);
+      else if (a.out_dtype == WGEMM_OUT_F32)
+        reinterpret_cast<float*>(a.out)[o] = y;
+      else
+        reinterpret_cast<__half*>(a.out)[o] = __float2half_rn(y);
+    }
+  }
+}
+
+int wgemm_splitk_reduce(const WGemmArgs& a, int tiles, cudaStream_t st) {
+  wgemm_splitk_reduce_kernel<<<dim3(tiles, a.n_tile / 16), 128, 0, st>>>(a, a.n_tile, a.k_splits);
   return (int)cudaGetLastError();
 }
 

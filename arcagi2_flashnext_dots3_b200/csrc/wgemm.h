@@ -64,6 +64,8 @@ struct WGemmArgs {
   int k_splits;
   float* workspace;
   int* counters;
+  int ext_reduce;           // 1: splits only park their partials; wgemm_splitk_reduce sums them (in split order)
+                            // and runs the epilogue in a second launch spread over every (tile, 16-token chunk)
   // pipeline
   int groups_per_stage;     // 128-column groups per pipeline stage (always 1 in this version)
   int teams;                // active dequant teams (<= 3); w_stages and ab_stages are multiples of it
@@ -86,5 +88,6 @@ size_t wgemm_smem_bytes(int n_tile, int g2, int w_stage_bytes, int w_stages, int
 int wgemm_groups_per_stage(int n_tile);
 constexpr int kWgemmMaxTeams = 3;
 int wgemm_launch(const WGemmArgs& a, const CUtensorMap& bmap, int grid, cudaStream_t st);
+int wgemm_splitk_reduce(const WGemmArgs& a, int tiles, cudaStream_t st);
 
 }  // namespace fw

@@ -86,8 +86,10 @@ def count_launches(model, step_fn):
         orig[n] = f
 
         def wrap(*a, _f=f, _n=n, **k):
-            counts[_n] = counts.get(_n, 0) + 1
-            return _f(*a, **k)
+            r = _f(*a, **k)
+            # wgemm reports how many kernels it launched (a split-K GEMM adds its reduce launch)
+            counts[_n] = counts.get(_n, 0) + (r if _n == "wgemm" and isinstance(r, int) else 1)
+            return r
         setattr(C, n, wrap)
     try:
         step_fn()
