@@ -68,3 +68,25 @@ class MTPHead:
 
     def reset_slot(self, slot):
         self.inner.reset_slot(slot)
+
+
+def random_mtp_dense(cfg, seed: int = 7) -> dict:
+    """Dense (trainable) form of the MTP weights: fc [H, 2H] rounded to its storage format, the two input-norm
+    weights, one attention + MoE layer and the stream mixer in the dense layout of :func:`fn_weights.random_dense`."""
+    mc = mtp_config(cfg)
+    D = fn_weights.random_dense(mc, seed=seed, symmetric=False)
+    g = torch.Generator().manual_seed(seed + 1)
+    H = cfg.hidden_size
+    return {"fc": fn_weights._round_dense(torch.randn(H, 2 * H, generator=g) * 0.02, mc),
+            "pe": torch.randn(H, generator=g) * 0.1, "ph": torch.randn(H, generator=g) * 0.1,
+            "layer": D["layers"][0], "mixer": D["mixer"]}
+
+
+def mtp_to_engine(dense: dict, cfg, main_dense: dict, device) -> dict:
+    """Dense MTP weights (e.g. a trained draft head's export) -> the engine form :class:`MTPHead` serves."""
+    mc = mtp_config(cfg)
+    E = fn_weights.to_engine({"embed": main_dense["embed"], "lm_head": main_dense["lm_head"], "mixer": dense["mixer"],
+                              "layers": [dense["layer"]]}, mc, device)
+    return {"fc": fn_weights._ws(fn_weights._round_dense(dense["fc"].float(), mc), mc, device),
+            "pe": dense["pe"].float().to(device), "ph": dense["ph"].float().to(device), "layer": E["layers"][0],
+            "mixer": E["mixer"]}
