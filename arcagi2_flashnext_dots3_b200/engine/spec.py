@@ -88,11 +88,11 @@ class MTPDrafter:
         """From MTP hidden rows xm [B, H] at positions q_last: draft 1 = argmax, then k - 1 chained steps."""
         dev = llm.device
         sl = torch.tensor([s.slot for s in seqs], dtype=torch.int32, device=dev)
-        d = ops.argmax(self.head.logits(xm)).to(torch.int32)
+        d = self.head.draft_ids(xm)
         drafts = [d]
         for i in range(1, k):
             xm = self.head.step(xm, d, sl, (q_last + i).to(torch.int32), 1)
-            d = ops.argmax(self.head.logits(xm)).to(torch.int32)
+            d = self.head.draft_ids(xm)
             drafts.append(d)
         dd = torch.stack(drafts, 1).tolist()
         for s, row in zip(seqs, dd):

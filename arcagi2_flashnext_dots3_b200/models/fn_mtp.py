@@ -39,7 +39,10 @@ def random_mtp(cfg, device, seed: int = 7) -> dict:
 
 class MTPHead:
     def __init__(self, cfg, main_W: dict, mtp_W: dict, device, n_slots: int, max_len: int, block_size: int = 64,
-                 kv_dtype: str = "fp8"):
+                 kv_dtype: str = "fp8", hot_ids: torch.Tensor = None):
+        """``hot_ids``: token ids of the draft vocabulary (the reference drafts over the 32,768 hottest tokens,
+        fnext/mtp/fnmtp.py:46); their LM-head rows are packed into a separate FP8 weight set, so a draft step reads
+        that share of the head instead of all of it."""
         self.cfg = cfg
         self.mc = mtp_config(cfg)
         self.W = mtp_W
@@ -49,6 +52,16 @@ class MTPHead:
                    "layers": [mtp_W["layer"]]}
         self.inner = FNModel(self.mc, inner_W, self.caches, device)
         self.device = torch.device(device)
+        self.hot = None
+        if hot_ids is not None:
+            from ..formats import runtime as rt
+            ws = main_W["lm_head"]
+            f = ws.fmts[0]
+            blob = ws.blob[: ws.row_tiles * ws.kg * rt.block_bytes(f)].view(ws.row_tiles, ws.kg, rt.block_bytes(f))
+            rows = rt.unpack_blocks(blob, f, ws.rows, ws.K)[hot_ids.to(blob.device).long()]
+            self.hot = hot_ids.to(device=self.device, dtype=torch.int32)
+            self.ws_hot = fn_weights._ws(rows.float(), self.mc, device)
+            del rows
 
     def step(self, x_prev: torch.Tensor, ids: torch.Tensor, slots, positions, n_tok: int = 1) -> torch.Tensor:
         """x_prev [T, H] (main or previous MTP hidden), ids [T] next tokens -> MTP hidden [T, H] (act)."""
@@ -62,6 +75,12 @@ class MTPHead:
 
     def logits(self, x):
         return self.inner.logits(x)
+
+    def draft_ids(self, x) -> torch.Tensor:
+        """Greedy draft token per row (int32): argmax over the hot vocabulary when one is set, else the full head."""
+        if self.hot is None:
+            return ops.argmax(self.logits(x)).to(torch.int32)
+        return self.hot[ops.argmax(self.inner._mm(x, self.ws_hot)).long()]
 
     def assign_blocks(self, slot, n_tokens, allocator):
         self.inner.assign_blocks(slot, n_tokens, allocator)

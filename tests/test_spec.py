@@ -67,3 +67,20 @@ def test_spec_gpu_matches_greedy(drafter):
     for g, w in zip(got, want):
         assert g[:4] == w[:4]
         assert sum(a == b for a, b in zip(g, w)) >= 0.8 * len(w)
+
+
+def test_mtp_hot_vocab_drafts():
+    """Hot-vocabulary draft head: with every token hot it drafts what the full head drafts; with a subset every
+    draft lies in the subset and the speculative output still equals plain greedy decoding."""
+    cfg = fn_small_config(num_layers=2, ple_layers=(0,), indexer_budget=1 << 20)
+    W, ec = _setup(cfg)
+    mtp = random_mtp(cfg, "cpu")
+    x = torch.randn(5, cfg.hidden_size)
+    full = MTPHead(cfg, W, mtp, "cpu", 4, 160, block_size=16)
+    every = MTPHead(cfg, W, mtp, "cpu", 4, 160, block_size=16, hot_ids=torch.arange(cfg.vocab_size))
+    assert torch.equal(full.draft_ids(x), every.draft_ids(x))
+    hot = torch.arange(0, cfg.vocab_size, 3)
+    sub = MTPHead(cfg, W, mtp, "cpu", 4, 160, block_size=16, hot_ids=hot)
+    assert set(sub.draft_ids(x).tolist()) <= set(hot.tolist())
+    want = LLM(cfg, W, "cpu", ec).generate(PROMPTS, max_new_tokens=8)
+    assert SpecDecoder(LLM(cfg, W, "cpu", ec), MTPDrafter(sub), k=3).generate(PROMPTS, max_new_tokens=8) == want
