@@ -109,7 +109,11 @@ def main():
                           "tok_per_s": round(B / ms * 1e3, 1), "graph": g is not None,
                           "build_s": round(build_s, 1),
                           "mem_GB": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1)}), flush=True)
+    # the graph may hold NCCL calls (--comm nccl): every reference to it, the bound replay method included, must
+    # be gone before destroy_process_group, or the process waits at exit
+    run = None
     del g
+    torch.cuda.synchronize()
     dist.barrier()
     dist.destroy_process_group()
 
