@@ -84,3 +84,21 @@ def test_mtp_hot_vocab_drafts():
     assert set(sub.draft_ids(x).tolist()) <= set(hot.tolist())
     want = LLM(cfg, W, "cpu", ec).generate(PROMPTS, max_new_tokens=8)
     assert SpecDecoder(LLM(cfg, W, "cpu", ec), MTPDrafter(sub), k=3).generate(PROMPTS, max_new_tokens=8) == want
+
+
+@pytest.mark.gpu
+def test_mtp_hot_vocab_drafts_gpu():
+    """GPU hot-vocabulary head (FP8 subset of the LM head on the tcgen05 GEMM): drafts stay inside the subset and
+    agree with the full-head argmax restricted to the subset."""
+    cfg = fn_small_config(num_layers=2, ple_layers=())
+    W = fn_weights.to_engine(fn_weights.random_dense(cfg, seed=0, symmetric=False), cfg, "cuda")
+    mtp = random_mtp(cfg, "cuda")
+    hot = torch.arange(1, cfg.vocab_size, 2)
+    head = MTPHead(cfg, W, mtp, "cuda", 2, 64, block_size=16, hot_ids=hot)
+    x = (torch.randn(6, cfg.hidden_size, device="cuda")).half()
+    got = head.draft_ids(x).cpu()
+    assert set(got.tolist()) <= set(hot.tolist())
+    full = head.logits(x).float().cpu()
+    ref = hot[full[:, hot].argmax(-1)]
+    agree = int((got == ref).sum())
+    assert agree >= 5, (got.tolist(), ref.tolist())
