@@ -39,6 +39,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
     ap.add_argument("--eager", action="store_true", help="no CUDA graph (for launch lists)")
+    ap.add_argument("--shard-vocab", action="store_true",
+                    help="with TP: each rank holds its slice of the LM head; tokens via the sharded pick")
     args = ap.parse_args()
     for k, v in (("RANK", "0"), ("WORLD_SIZE", "1"), ("MASTER_ADDR", "127.0.0.1"), ("MASTER_PORT", "29798")):
         os.environ.setdefault(k, v)
@@ -55,7 +57,8 @@ def main():
         from ..parallel.tp import TPGroup, tp_config
         lc = tp_config(cfg, world)
         tp = TPGroup(rank, world, dev, max_tokens=max(64, args.batch), hidden=cfg.hidden_size, comm=args.comm)
-    W = random_engine(cfg, dev, seed=0, tp=(rank, world) if world > 1 else None)
+    W = random_engine(cfg, dev, seed=0, tp=(rank, world) if world > 1 else None,
+                      shard_vocab=args.shard_vocab and world > 1)
     B, total = args.batch, args.ctx + args.warmup + args.steps + 16
     caches = allocate_caches(lc, dev, B, total, block_size=64)
     m = D3Model(lc, W, caches, dev, tp=tp)
@@ -70,7 +73,7 @@ def main():
 
     def step():
         x = m.step(ids, slots, pos, 1)
-        ids.copy_(ops.argmax(m.logits(x)))
+        ids.copy_(m.pick(x))
         pos.add_(1)
 
     torch.cuda.synchronize()

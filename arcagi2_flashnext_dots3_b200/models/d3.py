@@ -179,7 +179,22 @@ class D3Model:
         return d3.add_rms(h, y, W["norm"], cfg.rms_eps, self.act)
 
     def logits(self, x: torch.Tensor) -> torch.Tensor:
+        """Logits over the vocabulary this rank holds (all of it unless the head is split across a TP group)."""
         return self._mm(x, self.W["lm_head"])
+
+    def pick(self, x: torch.Tensor, temperature: float = 0.0, seed: int = 0, step: int = 0) -> torch.Tensor:
+        """Next token per row (int32): greedy, or Gumbel-max temperature sampling with the sampler's counter RNG.
+        With the LM head split over the TP ranks (``vocab_range`` in the weights) only one (value, index) pair
+        per row crosses the group."""
+        lg = self.logits(x)
+        if self.tp is not None and "vocab_range" in self.W:
+            from ..parallel.tp import sharded_pick
+            return sharded_pick(lg, self.W["vocab_range"][0], self.tp.group, temperature, seed, step)
+        if temperature <= 0:
+            return ops.argmax(lg)
+        from ..ops import sampling
+        u = sampling.uniform_torch(seed, step, torch.arange(lg.shape[1], device=lg.device))
+        return (lg.float() / temperature - torch.log(-torch.log(u))[None, :]).argmax(-1).to(torch.int32)
 
     # ------------------------------------------------------------------------------------------- engine hooks
     def assign_blocks(self, slot: int, n_tokens: int, allocator):

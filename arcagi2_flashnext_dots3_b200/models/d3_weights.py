@@ -65,6 +65,8 @@ def to_engine(W: dict, cfg, device) -> dict:
     low = torch.float32 if dev.type == "cpu" else torch.bfloat16
     E = {"embed": W["embed"].to(dev, torch.float32 if dev.type == "cpu" else torch.bfloat16),
          "lm_head": _ws(W["lm_head"], cfg, dev), "norm": _f32(W["norm"], dev), "layers": []}
+    if "vocab_range" in W:
+        E["vocab_range"] = W["vocab_range"]
     for l, L in enumerate(W["layers"]):
         a = L["attn"]
         H, kvr = cfg.heads_of(l), cfg.latent_of(l)
@@ -106,12 +108,13 @@ def to_engine(W: dict, cfg, device) -> dict:
     return E
 
 
-def random_engine(cfg, device, seed: int = 0, tp=None) -> dict:
+def random_engine(cfg, device, seed: int = 0, tp=None, shard_vocab: bool = False) -> dict:
     """Engine-form weights of the configured size generated and packed on `device`, without the dense fp32 copies
     of :func:`random_dense` (the full 144-expert model would need ~0.6 TB of them): dense weights N(0, 0.02) in
     their storage formats (fp16 fused down projection, block-FP8 elsewhere), experts N(0, 0.02) RTN-quantized to
     ``cfg.bits_of(e)`` bits with group-128 scales. ``tp=(rank, world)`` builds one tensor-parallel rank's shard
-    (its heads, its contiguous expert range); pass the matching :func:`..parallel.tp.tp_config` view to the model."""
+    (its heads, its contiguous expert range); pass the matching :func:`..parallel.tp.tp_config` view to the model.
+    ``shard_vocab``: the rank keeps only its slice of the LM head (next tokens via ``D3Model.pick``)."""
     from .fn_weights import _random_experts
     dev = torch.device(device)
     rank, world = tp if tp is not None else (0, 1)
@@ -125,8 +128,12 @@ def random_engine(cfg, device, seed: int = 0, tp=None) -> dict:
         return wgemm.build_weight_set([rt.pack_f16(rn(rows, K))], [16], rows, K, device=dev)
 
     low = torch.float32 if dev.type == "cpu" else torch.bfloat16
-    E = {"embed": rn(cfg.vocab_size, Hd, std=1.0).to(low), "lm_head": _ws(rn(cfg.vocab_size, Hd), cfg, dev),
+    v0, v1 = (rank * cfg.vocab_size // world, (rank + 1) * cfg.vocab_size // world) if shard_vocab else \
+        (0, cfg.vocab_size)
+    E = {"embed": rn(cfg.vocab_size, Hd, std=1.0).to(low), "lm_head": _ws(rn(v1 - v0, Hd), cfg, dev),
          "norm": 1.0 + rn(Hd, std=0.1), "layers": []}
+    if shard_vocab:
+        E["vocab_range"] = (v0, v1)
     for l in range(cfg.num_layers):
         H = cfg.heads_of(l) // world
         kvr = cfg.latent_of(l)

@@ -54,6 +54,32 @@ def uniform(seed: int, step: int, idx) -> np.ndarray:
     return (((h >> np.uint64(41)).astype(np.float32) + np.float32(0.5)) * np.float32(1.0 / 8388608.0))
 
 
+def _i64(c) -> int:
+    """uint64 constant as the int64 with the same bits (torch integer arithmetic wraps modulo 2^64)."""
+    c = int(c)
+    return c - (1 << 64) if c >= (1 << 63) else c
+
+
+_M = [_i64(0xBF58476D1CE4E5B9), _i64(0x94D049BB133111EB)]
+
+
+def _shr(z: torch.Tensor, n: int) -> torch.Tensor:
+    """Logical right shift of int64 bit patterns."""
+    return (z >> n) & ((1 << (64 - n)) - 1)
+
+
+def uniform_torch(seed: int, step: int, idx: torch.Tensor) -> torch.Tensor:
+    """:func:`uniform` on a torch int64 index tensor (any device), bit-identical: the same counter hash in
+    wrapping int64 arithmetic."""
+    with np.errstate(over="ignore"):
+        base = _i64(np.uint64(seed % (1 << 64)) * _C1 + np.uint64(step % (1 << 64)) * _C2 + np.uint64(1))
+    z = idx.long() * _i64(_C3) + base
+    z = (z ^ _shr(z, 30)) * _M[0]
+    z = (z ^ _shr(z, 27)) * _M[1]
+    z = z ^ _shr(z, 31)
+    return (_shr(z, 41).float() + 0.5) * (1.0 / 8388608.0)
+
+
 def _sample_row(x: torch.Tensor, T: float, k: int, p: float, seed: int, step: int) -> int:
     V = x.shape[0]
     if T <= 0:

@@ -99,12 +99,56 @@ class TPGroup:
         self.finish_into(h, T)
 
 
-def shard_d3_weights(W: dict, cfg, rank: int, world: int) -> dict:
+def vocab_range(V: int, rank: int, world: int):
+    """[v0, v1) of the vocabulary whose LM-head rows this rank holds when the head is split over the TP group."""
+    return rank * V // world, (rank + 1) * V // world
+
+
+def sharded_pick(local_logits: torch.Tensor, v0: int, group=None, temperature: float = 0.0, seed: int = 0,
+                 step: int = 0) -> torch.Tensor:
+    """Next token per row when every TP rank holds the logits of its own vocabulary slice [v0, v0 + V_local).
+
+    The reference samples on the vocab-parallel logits shard and all-gathers 8 floats per row instead of the
+    logits (dotsnote/engine/arcstats_pkg/arcstats/shard_sample.py:3-14, 67, 119). Here each rank reduces its
+    slice to one (value, global index) pair per row: the max logit for greedy decoding, or for temperature
+    sampling the Gumbel-max key logit / T - log(-log u) with u drawn from the sampler's counter hash at the
+    token's GLOBAL index (ops.sampling.uniform_torch). The pairs are all-gathered and the largest value wins,
+    lowest index on ties. Because the noise of a token does not depend on which rank holds it, the result is
+    exactly the token the unsharded sampler (ops.sampling, top-k and top-p off) picks. Returns int32 [T]."""
+    from ..ops import sampling
+    x = local_logits.float()
+    T, Vl = x.shape
+    if temperature > 0:
+        u = sampling.uniform_torch(seed, step, torch.arange(v0, v0 + Vl, device=x.device))
+        x = x * (1.0 / temperature) - torch.log(-torch.log(u))[None, :]
+    if Vl:
+        idx = x.argmax(-1)   # first index among equal values
+        val = x.gather(1, idx[:, None])[:, 0]
+    else:
+        val, idx = x.new_full((T,), -float("inf")), torch.zeros(T, dtype=torch.long, device=x.device)
+    pair = torch.stack([val, (idx + v0).float()], 1).contiguous()          # indices < 2^24 are exact in fp32
+    world = dist.get_world_size(group)
+    if dist.get_backend(group) == "nccl":
+        allp = torch.empty(world, T, 2, dtype=pair.dtype, device=pair.device)
+        dist.all_gather_into_tensor(allp, pair, group=group)
+    else:
+        parts = [torch.empty_like(pair) for _ in range(world)]
+        dist.all_gather(parts, pair, group=group)
+        allp = torch.stack(parts)
+    best = allp[:, :, 0].argmax(0)   # ranks hold increasing vocabulary ranges: the first max has the lowest index
+    return allp[best, torch.arange(T, device=pair.device), 1].to(torch.int32)
+
+
+def shard_d3_weights(W: dict, cfg, rank: int, world: int, shard_vocab: bool = False) -> dict:
     """Dense-form D3 weights of one TP rank: the rank's attention heads (q_b, kv_b, g rows; o columns) and its
     contiguous share of every MoE layer's experts (router and correction bias stay whole: routing is global)."""
     import copy
     dn, dr, dv = cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim
     out = {k: v for k, v in W.items() if k != "layers"}
+    if shard_vocab:   # this rank's rows of the LM head; next tokens through sharded_pick (D3Model.pick)
+        v0, v1 = vocab_range(cfg.vocab_size, rank, world)
+        out["lm_head"] = W["lm_head"][v0:v1]
+        out["vocab_range"] = (v0, v1)
     out["layers"] = []
     for l, L in enumerate(W["layers"]):
         H = cfg.heads_of(l)

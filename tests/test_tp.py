@@ -50,3 +50,14 @@ def test_tp_reduce_wait_times_out_with_error_code():
         native.check_error(dev)
     assert bool((h == 1).all())                    # nothing was added
     assert float(torch.ones(3, device=dev).sum()) == 3.0   # the context still works
+
+
+@pytest.mark.parametrize("nproc", [2, 3])
+def test_vocab_sharded_pick_cpu(nproc):
+    """Greedy and Gumbel-max temperature sampling over a vocabulary split across ranks equal the unsharded
+    sampler exactly (ties resolved to the lowest index)."""
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={nproc}",
+           "--master-addr=127.0.0.1", f"--master-port={29690 + nproc}", os.path.join(HERE, "vocab_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "VOCAB_OK" in r.stdout, (r.stdout[-2000:], r.stderr[-3000:])

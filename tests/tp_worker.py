@@ -15,7 +15,7 @@ from arcagi2_flashnext_dots3_b200.ops import native  # noqa: E402
 from arcagi2_flashnext_dots3_b200.parallel.tp import TPGroup, shard_d3_weights, tp_config  # noqa: E402
 
 
-def run(model, ids, dev):
+def run(model, ids, dev, hidden=False):
     c = model.c
     alloc = BlockAllocator(c.n_blocks, 2)
     model.assign_blocks(0, 48, alloc)
@@ -23,7 +23,8 @@ def run(model, ids, dev):
     xs = [model.step(ids[:14].to(dev), s0, torch.tensor([0], dtype=torch.int32, device=dev), 14)]
     for t in range(14, ids.shape[0]):
         xs.append(model.step(ids[t:t + 1].to(dev), s0, torch.tensor([t], dtype=torch.int32, device=dev), 1))
-    return model.logits(torch.cat(xs)).float().cpu()
+    x = torch.cat(xs)
+    return x if hidden else model.logits(x).float().cpu()
 
 
 def main():
@@ -50,6 +51,12 @@ def main():
     err = (got - ref).abs().max() / ref.abs().max()
     tol = 2e-2 if cuda else 1e-4
     assert err < tol, (rank, float(err))
+    if not cuda:
+        # LM head split across the ranks too: the sharded greedy pick equals the argmax of the full logits
+        m2 = D3Model(lc, to_engine(shard_d3_weights(W, cfg, rank, world, shard_vocab=True), lc, dev),
+                     allocate_caches(lc, dev, 2, 64, block_size=16), dev, tp=tp)
+        picks = m2.pick(run(m2, ids, dev, hidden=True))
+        assert picks.tolist() == ref.argmax(-1).tolist(), rank
     dist.barrier()
     if rank == 0:
         print("TP_OK", comm, world, float(err))

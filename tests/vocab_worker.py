@@ -1,0 +1,34 @@
+"""Worker for the vocabulary-sharded pick test: every rank holds a slice of the same logits; the sharded greedy
+and Gumbel-max picks must equal the unsharded sampler's."""
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from arcagi2_flashnext_dots3_b200.ops import sampling  # noqa: E402
+from arcagi2_flashnext_dots3_b200.parallel.tp import sharded_pick, vocab_range  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dist.init_process_group("gloo")
+    V, T = 1003, 6
+    logits = torch.randn(T, V, generator=torch.Generator().manual_seed(1)) * 3
+    logits[2, 10] = logits[2, 900] = logits[2].max() + 1     # a tie across ranks: the lower index wins
+    v0, v1 = vocab_range(V, rank, world)
+    got = sharded_pick(logits[:, v0:v1], v0)
+    assert got.tolist() == logits.argmax(-1).tolist(), (got.tolist(), logits.argmax(-1).tolist())
+    for seed, step, temp in [(3, 0, 1.0), (77, 12, 0.7)]:
+        got = sharded_pick(logits[:, v0:v1], v0, temperature=temp, seed=seed, step=step)
+        want = [sampling._sample_row(logits[r], temp, 0, 1.0, seed, step) for r in range(T)]
+        assert got.tolist() == want, (got.tolist(), want)
+    dist.barrier()
+    if rank == 0:
+        print("VOCAB_OK", world)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
