@@ -36,7 +36,11 @@ def test_exported_head_serves_like_training_module():
     cfg, main, mtp, ids, h, _ = _setup()
     m = DraftHeadTrain(cfg, main, mtp, "cpu")
     with torch.no_grad():
-        m.fc.add_(0.01 * torch.randn_like(m.fc))   # a changed parameter must survive the export
+        # a changed parameter must survive the export; it is kept on the FP8 grid the export stores it in, so
+        # both sides multiply the same values
+        from arcagi2_flashnext_dots3_b200.models.fn_mtp import mtp_config
+        g = torch.Generator().manual_seed(11)
+        m.fc.copy_(fn_weights._round_dense(m.fc + 0.01 * torch.randn(m.fc.shape, generator=g), mtp_config(cfg)))
         x_train = m.step(h[:20], ids[1:21], 0)
         lg_train = m.logits(x_train)
     ex = m.export()
