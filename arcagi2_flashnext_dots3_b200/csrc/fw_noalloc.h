@@ -15,7 +15,9 @@ extern "C" {
 // Indexer top-k: for each row, the `nblk` highest-scoring complete compressed blocks of its sequence
 // (score = sum over heads of relu(iq . comp) / sqrt(iD)); rows with at most nblk complete blocks get sparse = 0
 // and sel = -1. iq [rows, iH, iD] fp32; comp [S, max_comp, iD] bf16 (comp_bf16 = 1) or fp32; slots, positions
-// [rows / n_tok] int32; sel [rows, nblk] int32; sparse [rows] int32.
+// [rows / n_tok] int32; sel [rows, nblk] int32; sparse [rows] int32. comp must be 16-byte aligned (bf16) or
+// 32-byte aligned (fp32), else FW_NOALLOC_INVALID. The entry point cannot see the cache's slot count S, so the
+// caller guarantees 0 <= slots[i] < S (blocks at or beyond max_comp are never read).
 int fw_qsa_select_noalloc(const float* iq, const void* comp, int comp_bf16, const int* slots, const int* positions,
                           int* sel, int* sparse, int rows, int iH, int iD, int max_comp, int nblk, int r, int n_tok,
                           cudaStream_t stream);

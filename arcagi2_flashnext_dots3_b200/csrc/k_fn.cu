@@ -1456,6 +1456,9 @@ extern "C" __attribute__((visibility("default"))) int fw_qsa_select_noalloc(
   if (rows < 0 || iH <= 0 || iH > 32 || iD <= 0 || max_comp <= 0 || nblk <= 0 || r <= 0 || n_tok <= 0 ||
       rows % n_tok || !iq || !comp || !slots || !positions || !sel || !sparse)
     return FW_NOALLOC_INVALID;
+  // the score kernel reads comp 8 elements at a time (16 bytes of bf16, 32 of fp32); iq is read per float
+  const uintptr_t comp_align = comp_bf16 ? 16 : 32;
+  if (reinterpret_cast<uintptr_t>(comp) % comp_align) return FW_NOALLOC_INVALID;
   const size_t smem = (size_t)iH * iD * sizeof(float);
   if (smem > 48 * 1024) return FW_NOALLOC_INVALID;
   const int chunks = (max_comp + 255) / 256;

@@ -28,6 +28,14 @@ from ..ops.sampling import SamplingParams
 from .block_manager import BlockAllocator
 
 
+def greedy_ids(model, x: torch.Tensor) -> torch.Tensor:
+    """Greedy next token per row (int32). A model whose LM head is split over a TP group (``vocab_sharded``)
+    picks through its own cross-rank pick, since its local logits are indexed by its vocabulary slice."""
+    if getattr(model, "vocab_sharded", False):
+        return model.pick(x)
+    return ops.argmax(model.logits(x))
+
+
 class ContextFull(ValueError):
     """A push would exceed max_model_len."""
 
@@ -79,7 +87,7 @@ class DecodeGraph:
             nxt, lp = sampling.sample(m.logits(x), *self.sp)
             self.next_lp.copy_(lp)
         else:
-            nxt = ops.argmax(m.logits(x))
+            nxt = greedy_ids(m, x)
         self.next_ids.copy_(nxt)
         if self.advance:
             self.ids.copy_(nxt)
@@ -211,6 +219,12 @@ class LLM:
 
     def _append_sample(self, seq: Sequence, x_last):
         """Sample the next token of `seq` from the hidden state of its last fed token."""
+        if getattr(self.model, "vocab_sharded", False):
+            if seq.sp.temperature > 0:
+                raise NotImplementedError("sampling over a vocabulary-sharded LM head: only greedy picks are sharded")
+            seq.out.append(int(greedy_ids(self.model, x_last)[0]))
+            seq.lps.append(0.0)
+            return
         ts = sampling.params_tensors([seq.sp], [len(seq.out)], self.device)
         ids, lp = sampling.sample(self.model.logits(x_last).float(), *[t.to(self.device) for t in ts])
         seq.out.append(int(ids[0]))
@@ -226,8 +240,9 @@ class LLM:
         bucket = next((b for b in self.ec.graph_batch_sizes if b >= n), n)
         g = self.graphs.get(bucket)
         if g is None:
+            # a vocabulary-sharded head has greedy picks only (temperature > 0 is refused at add time)
             g = DecodeGraph(self.model, bucket, advance=False, use_graph=self.ec.cuda_graphs,
-                            scratch_slot=self.scratch, sample=True)
+                            scratch_slot=self.scratch, sample=not getattr(self.model, "vocab_sharded", False))
             g.capture()
             self.graphs[bucket] = g
         return g

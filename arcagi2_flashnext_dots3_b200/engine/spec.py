@@ -22,6 +22,7 @@ import torch
 
 from ..ops import fn_ops as ops
 from .block_manager import BlockAllocator
+from .llm import greedy_ids
 
 
 class NgramDrafter:
@@ -150,7 +151,7 @@ class SpecDecoder:
         sl = torch.tensor([s.slot for s in seqs], dtype=torch.int32, device=dev)
         pos = torch.tensor([s.pos for s in seqs], dtype=torch.int32, device=dev)
         x = llm.model.step(torch.tensor(ids, dtype=torch.int32, device=dev).view(-1), sl, pos, k1, verify=True)
-        y = ops.argmax(llm.model.logits(x)).view(len(seqs), k1).tolist()
+        y = greedy_ids(llm.model, x).view(len(seqs), k1).tolist()
         accepted = []
         for d, yy in zip(drafts, y):
             a = 0

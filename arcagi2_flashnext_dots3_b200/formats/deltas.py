@@ -5,8 +5,8 @@ Two delta formats exist, both kept file-compatible with the reference:
 * **FN delta directory** (flashnext/kaggle/code_dataset/delta_build.py:12-79): ``scales-LNN.pt`` =
   ``{expert_id: {"gu_s", "d_s"}}`` (fp16 scales), ``router-LNN.pt``, ``keep.json``, optional extra files and a
   ``manifest.json`` of ``{name: {"bytes", "md5"}}``. :func:`make` extracts a delta from a derived build,
-  :func:`build` rebuilds a full build from base + deltas (manifest-verified), :func:`check` compares two builds
-  (md5-identical or tensor-identical).
+  :func:`build` rebuilds a full build from base + deltas (manifest-verified), :func:`verify_build` compares two
+  builds (byte-identical, or identical content digests).
 * **D3 ulp overlay** (dotsnote/engine/arcstats_pkg/arcstats/delta_overlay.py:1-20): one safetensors file with, per
   layer, ``lowbit.LNN.experts`` (int64 ids), ``lowbit.LNN.gu_s`` / ``.d_s`` (int8 or int16 differences of the fp16
   scale bit patterns, in ulp steps), ``lowbit.LNN.base_ck`` (checksum of the base scale bits; a different base is
@@ -19,6 +19,7 @@ import json
 import os
 import re
 import shutil
+from dataclasses import dataclass, field
 from pathlib import Path
 
 import torch
@@ -110,36 +111,68 @@ def build(base_dir, deltas, out_dir):
                 shutil.copy2(f"{d}/{n}", f"{out_dir}/{n}")
 
 
-def tree_equal(x, y) -> bool:
-    if isinstance(x, dict):
-        return isinstance(y, dict) and list(x) == list(y) and all(tree_equal(x[k], y[k]) for k in x)
-    if isinstance(x, (list, tuple)):
-        return type(x) == type(y) and len(x) == len(y) and all(tree_equal(a, b) for a, b in zip(x, y))
-    if torch.is_tensor(x):
-        return torch.is_tensor(y) and x.dtype == y.dtype and x.shape == y.shape and torch.equal(x, y)
-    return x == y
+def content_digest(obj) -> str:
+    """SHA-256 of a loaded checkpoint tree's content, independent of how the pickle was written: containers
+    contribute their type, length and (for dicts, in insertion order) their keys; tensors their dtype, shape and
+    raw bytes; other leaves their repr. Two trees with equal digests hold the same keys and bit-identical
+    tensors."""
+    h = hashlib.sha256()
+    stack = [obj]
+    while stack:
+        x = stack.pop()
+        if torch.is_tensor(x):
+            t = x.detach().cpu().contiguous()
+            h.update(f"T{t.dtype}{tuple(t.shape)}".encode())
+            h.update(t.view(torch.uint8).numpy().tobytes() if t.numel() else b"")
+        elif isinstance(x, dict):
+            h.update(f"D{len(x)}".encode())
+            for k in x:
+                h.update(("K" + repr(k)).encode())
+            stack.extend(reversed(list(x.values())))
+        elif isinstance(x, (list, tuple)):
+            h.update(f"{type(x).__name__[0]}{len(x)}".encode())
+            stack.extend(reversed(list(x)))
+        else:
+            h.update(("V" + repr(x)).encode())
+    return h.hexdigest()
 
 
-def check(rebuilt_dir, derived_dir):
-    """Compare two builds file by file: returns (ok, n_md5_same, n_tensor_same, bad_names)."""
-    names = [f"lowbit-L{l:02d}.pt" for l in _layers(derived_dir)]
-    names += [f"router-L{l:02d}.pt" for l in _layers(derived_dir)]
-    if os.path.exists(f"{derived_dir}/keep.json"):
-        names.append("keep.json")
-    same_md5 = same_t = 0
-    bad = []
-    for n in names:
-        if md5(f"{rebuilt_dir}/{n}") == md5(f"{derived_dir}/{n}"):
-            same_md5 += 1
-            continue
-        if n.endswith(".pt"):
-            x = torch.load(f"{rebuilt_dir}/{n}", map_location="cpu", weights_only=False)
-            y = torch.load(f"{derived_dir}/{n}", map_location="cpu", weights_only=False)
-            if tree_equal(x, y):
-                same_t += 1
-                continue
-        bad.append(n)
-    return (not bad), same_md5, same_t, bad
+@dataclass
+class BuildDiff:
+    """Result of :func:`verify_build`: files byte-identical, files whose loaded contents are identical though
+    their bytes differ (a re-pickled but equal tensor tree), and files that differ or are missing."""
+    identical: list = field(default_factory=list)
+    same_content: list = field(default_factory=list)
+    differ: list = field(default_factory=list)
+
+    @property
+    def ok(self) -> bool:
+        return not self.differ
+
+
+def _build_files(d) -> list:
+    layers = _layers(d)
+    names = [f"{kind}-L{l:02d}.pt" for kind in ("lowbit", "router") for l in layers]
+    return names + (["keep.json"] if os.path.exists(f"{d}/keep.json") else [])
+
+
+def verify_build(rebuilt_dir, derived_dir) -> BuildDiff:
+    """Check that a build rebuilt from base + deltas reproduces the derived build it was extracted from (the
+    reference's delta_build.py `check` step): every low-bit layer, router and keep file of the derived build must
+    be byte-identical in the rebuilt one, or, for .pt files, identical in content (:func:`content_digest`)."""
+    res = BuildDiff()
+    for name in _build_files(derived_dir):
+        a, b = Path(rebuilt_dir) / name, Path(derived_dir) / name
+        if not a.exists():
+            res.differ.append(name)
+        elif a.stat().st_size == b.stat().st_size and md5(a) == md5(b):
+            res.identical.append(name)
+        elif name.endswith(".pt") and content_digest(torch.load(a, map_location="cpu", weights_only=False)) == \
+                content_digest(torch.load(b, map_location="cpu", weights_only=False)):
+            res.same_content.append(name)
+        else:
+            res.differ.append(name)
+    return res
 
 
 # ------------------------------------------------------------------------------------------ D3 ulp overlay

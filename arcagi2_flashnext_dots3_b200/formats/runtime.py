@@ -162,6 +162,28 @@ def unpack_blocks(blob: torch.Tensor, fmt: int, R: int, K: int) -> torch.Tensor:
     return w.reshape(T * TILE, K)[:R]
 
 
+def tensor_core_operands(blob: torch.Tensor, fmt: int, R: int, K: int) -> torch.Tensor:
+    """fp16 [R, K]: the weight values exactly as the GEMM's dequant stage writes them into shared memory for the
+    tensor core. FP8 blocks: fp16(e4m3) times the block scale rounded to fp16, one fp16 rounding of the product;
+    integer formats: (q - z), exact in fp16, times the fp16 group scale, one rounding; fp16 blocks: unchanged.
+    Rows gathered from this tensor into an fp16 weight set give the same products as the source blocks, whatever
+    block scale their source tile had."""
+    if fmt == 16:
+        return unpack_blocks(blob, fmt, R, K).half()
+    T, KG, _ = blob.shape
+    if fmt == 8:
+        b = blob[..., : 32 * 512].contiguous().view(T, KG, 32, TILE, 4).permute(0, 3, 1, 2, 4)
+        v = b.reshape(T * TILE, KG, 128).contiguous().view(torch.float8_e4m3fn).half()
+        sc = blob[..., 32 * 512: 32 * 512 + 4].contiguous().view(torch.float32).view(T, KG).half()
+        out = v * sc.repeat_interleave(TILE, 0)[:, :, None]
+        return out.reshape(T * TILE, K)[:R].contiguous()
+    NW = FMT_WORDS[fmt]
+    qz = unpack_qz(blob, fmt, R, K).half()
+    sb = blob[..., NW * 512: NW * 512 + 256].contiguous().view(torch.float16).view(T, KG, TILE)
+    s = sb.permute(0, 2, 1).reshape(T * TILE, KG)[:R]
+    return (qz.view(R, KG, 128) * s[:, :, None]).reshape(R, K).contiguous()
+
+
 def unpack_qz(blob: torch.Tensor, fmt: int, R: int, K: int) -> torch.Tensor:
     """(q - z) as fp32 [R, K] of an integer-format expert's blocks [tiles, KG, bytes] (scales not applied)."""
     T, KG, _ = blob.shape

@@ -103,7 +103,7 @@ def main():
         torch.cuda.synchronize()
         dist.barrier()   # ranks finish building at different times; the fused all-reduce waits are bounded
         if args.eager:
-            ms = _time(lambda: m.logits(m.step(ids, slots, pos, 1)), args.steps, args.warmup)
+            ms = _time(lambda: m.pick(m.step(ids, slots, pos, 1)), args.steps, args.warmup)
             native.check_error(dev)
             out.update({"batch": B, "ctx": args.ctx, "ms_per_step": round(ms, 4), "graph": False})
             if rank == 0:
@@ -115,12 +115,12 @@ def main():
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
             for _ in range(2):
-                m.logits(m.step(ids, slots, pos, 1))
+                m.pick(m.step(ids, slots, pos, 1))
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            lg = m.logits(m.step(ids, slots, pos, 1))
+            lg = m.pick(m.step(ids, slots, pos, 1))
         ms = _time(g.replay, args.steps, args.warmup)
         native.check_error(dev)
         out.update({"batch": B, "ctx": args.ctx, "ms_per_step": round(ms, 4)})

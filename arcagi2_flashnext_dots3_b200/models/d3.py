@@ -178,16 +178,25 @@ class D3Model:
                 y = self._mm(sact, L["mlp"]["d"])
         return d3.add_rms(h, y, W["norm"], cfg.rms_eps, self.act)
 
+    @property
+    def vocab_sharded(self) -> bool:
+        """True when the LM head is split over the TP ranks: each rank holds only its vocabulary slice, so next
+        tokens must come from :meth:`pick` (a local argmax would return slice-local indices)."""
+        return self.tp is not None and "vocab_range" in self.W
+
     def logits(self, x: torch.Tensor) -> torch.Tensor:
-        """Logits over the vocabulary this rank holds (all of it unless the head is split across a TP group)."""
+        """Logits over the whole vocabulary. Refused when the head is split over a TP group, since this rank then
+        holds only a slice whose indices are not token ids: use :meth:`pick`."""
+        if self.vocab_sharded:
+            raise RuntimeError("D3Model.logits: the LM head is vocabulary-sharded; select tokens with pick()")
         return self._mm(x, self.W["lm_head"])
 
     def pick(self, x: torch.Tensor, temperature: float = 0.0, seed: int = 0, step: int = 0) -> torch.Tensor:
         """Next token per row (int32): greedy, or Gumbel-max temperature sampling with the sampler's counter RNG.
         With the LM head split over the TP ranks (``vocab_range`` in the weights) only one (value, index) pair
         per row crosses the group."""
-        lg = self.logits(x)
-        if self.tp is not None and "vocab_range" in self.W:
+        lg = self._mm(x, self.W["lm_head"])
+        if self.vocab_sharded:
             from ..parallel.tp import sharded_pick
             return sharded_pick(lg, self.W["vocab_range"][0], self.tp.group, temperature, seed, step)
         if temperature <= 0:

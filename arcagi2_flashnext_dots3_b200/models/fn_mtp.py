@@ -41,8 +41,11 @@ class MTPHead:
     def __init__(self, cfg, main_W: dict, mtp_W: dict, device, n_slots: int, max_len: int, block_size: int = 64,
                  kv_dtype: str = "fp8", hot_ids: torch.Tensor = None):
         """``hot_ids``: token ids of the draft vocabulary (the reference drafts over the 32,768 hottest tokens,
-        fnext/mtp/fnmtp.py:46); their LM-head rows are packed into a separate FP8 weight set, so a draft step reads
-        that share of the head instead of all of it."""
+        fnext/mtp/fnmtp.py:46). Their LM-head rows go into a separate fp16 weight set holding the exact operand
+        values the tensor core reads for those rows of the full head (``rt.tensor_core_operands``), so on the GPU a
+        draft step computes the full head's products restricted to the hot rows while reading only that share of
+        the head. The rows are not re-quantized: FP8 would need new 128x128 block scales, and the hot logits
+        would then differ from the full head's."""
         self.cfg = cfg
         self.mc = mtp_config(cfg)
         self.W = mtp_W
@@ -58,9 +61,9 @@ class MTPHead:
             ws = main_W["lm_head"]
             f = ws.fmts[0]
             blob = ws.blob[: ws.row_tiles * ws.kg * rt.block_bytes(f)].view(ws.row_tiles, ws.kg, rt.block_bytes(f))
-            rows = rt.unpack_blocks(blob, f, ws.rows, ws.K)[hot_ids.to(blob.device).long()]
+            rows = rt.tensor_core_operands(blob, f, ws.rows, ws.K)[hot_ids.to(blob.device).long()]
             self.hot = hot_ids.to(device=self.device, dtype=torch.int32)
-            self.ws_hot = fn_weights._ws(rows.float(), self.mc, device)
+            self.ws_hot = wgemm.dense_f16(rows, device)
             del rows
 
     def step(self, x_prev: torch.Tensor, ids: torch.Tensor, slots, positions, n_tok: int = 1) -> torch.Tensor:

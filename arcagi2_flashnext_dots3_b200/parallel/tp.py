@@ -113,8 +113,11 @@ def sharded_pick(local_logits: torch.Tensor, v0: int, group=None, temperature: f
     slice to one (value, global index) pair per row: the max logit for greedy decoding, or for temperature
     sampling the Gumbel-max key logit / T - log(-log u) with u drawn from the sampler's counter hash at the
     token's GLOBAL index (ops.sampling.uniform_torch). The pairs are all-gathered and the largest value wins,
-    lowest index on ties. Because the noise of a token does not depend on which rank holds it, the result is
-    exactly the token the unsharded sampler (ops.sampling, top-k and top-p off) picks. Returns int32 [T]."""
+    lowest index on ties. Because the noise of a token does not depend on which rank holds it, the result
+    equals the token the unsharded CPU sampler (ops.sampling's torch path, top-k and top-p off) picks. The GPU
+    sampler kernel evaluates the same noise with its own logf, which may differ from torch.log in the last bit,
+    so a near-tie between two tokens can resolve differently there. Top-k and top-p are not supported on the
+    sharded path: only greedy and full-vocabulary temperature sampling. Returns int32 [T]."""
     from ..ops import sampling
     x = local_logits.float()
     T, Vl = x.shape

@@ -21,7 +21,8 @@ GOOD = "def transform(g):\n    return [row[::-1] for row in g]\n"
 def test_arckit_basics():
     g = ak.grid([[0, 0, 0], [0, 4, 4], [0, 4, 0]])
     assert ak.bg(g) == 0 and ak.palette(g) == [0, 4]
-    assert ak.bbox(g != 0) == (1, 1, 3, 3)
+    assert ak.bbox(g != 0) == (1, 1, 2, 2)                       # inclusive box
+    assert ak.crop(g, ak.bbox(g != 0)).tolist() == [[4, 4], [4, 0]]
     assert ak.trim(g).tolist() == [[4, 4], [4, 0]]
     objs = ak.objects(g)
     assert len(objs) == 1 and objs[0].size == 3 and objs[0].colour == 4
@@ -31,6 +32,54 @@ def test_arckit_basics():
     assert ak.find_sub([[1, 2, 3], [4, 5, 6]], [[5, 6]]) == [(1, 1)]
     assert ak.downscale(ak.scale([[1, 2]], 3), 3).tolist() == [[1, 2]]
     assert ak.enclosed([[1, 1, 1], [1, 0, 1], [1, 1, 1]], bgc=0)[1, 1]
+
+
+def test_arckit_reference_contract():
+    """Semantics model-written programs rely on: orderings, tie rules, conventions and the added helpers."""
+    assert list(ak.counts([[1, 1, 0], [2, 2, 2]])) == [2, 1, 0]
+    assert ak.bg([[1, 2], [2, 1]]) == 1 and ak.bg([[0, 3], [3, 0]]) == 0
+    assert ak.task_bg([{"input": [[5, 5]], "output": [[5, 0]]}]) == 5
+    assert ak.d8([[1, 2], [3, 4]], "rot90").tolist() == [[3, 1], [4, 2]]
+    assert ak.d8([[1, 2], [3, 4]], "antitranspose").tolist() == [[4, 2], [3, 1]]
+    assert list(ak.d8([[1]])) == list(ak.D8)
+    assert ak.ray([[0, 0, 3, 0]], 0, 0, 0, 1, 5, stop=3).tolist() == [[0, 5, 3, 0]]
+    assert ak.ray([[0, 2, 0]], 0, 0, 0, 1, 5, overwrite=False).tolist() == [[0, 2, 5]]
+    g = [[0, 3, 0], [0, 0, 0]]
+    assert ak.move(g, ak.objects(g)[0], 1, 1).tolist() == [[0, 0, 0], [0, 0, 3]]
+    sg = [[0, 0, 8, 0, 0], [0, 1, 8, 0, 0], [8, 8, 8, 8, 8], [0, 0, 8, 0, 2], [0, 0, 8, 0, 0]]
+    s = ak.split_grid(sg)
+    assert s["colour"] == 8 and s["rows"] == [2] and s["cols"] == [2]
+    assert s["boxes"] == [[(0, 0, 1, 1), (0, 3, 1, 4)], [(3, 0, 4, 1), (3, 3, 4, 4)]]
+    assert s["cells"][1][1].tolist() == [[0, 2], [0, 0]]
+    assert ak.period([[1, 2, 1, 2], [1, 2, 9, 2]], ignore=9) == (1, 2)
+    assert ak.repair_period([[1, 2, 1, 2], [1, 2, 9, 2]], 9).tolist() == [[1, 2, 1, 2], [1, 2, 1, 2]]
+    assert ak.symmetries([[1, 2, 9], [3, 4, 3]], ignore=9) == ["fliplr"]
+    assert ak.complete_symmetry([[1, 2, 9], [3, 4, 3]], 9).tolist() == [[1, 2, 1], [3, 4, 3]]
+    assert ak.downscale([[0, 0], [0, 3]], 2).tolist() == [[0]]
+    assert ak.downscale([[0, 0], [0, 3]], 2, how="any").tolist() == [[3]]
+    with pytest.raises(ValueError):
+        ak.line([[0] * 4] * 4, 0, 0, 1, 3, 1)
+    o = ak.objects([[0, 4, 4], [0, 4, 0]])[0]
+    assert repr(o) == "Obj(colour=4 size=3 box=(0,1,1,2) 2x2 border)" and o.box == (0, 1, 1, 2)
+    ring = ak.objects([[1, 1, 1], [1, 0, 1], [1, 1, 1]], bgc=0)[0]
+    assert ring.holes == 1 and ring.size == 8 and not ring.rect
+    ev = ak.obj_diff([[1, 0, 0], [0, 0, 0]], [[0, 0, 0], [0, 0, 1]])
+    assert [e[0] for e in ev] == ["moved"] and ev[0][3] == (1, 2)
+    ev = ak.obj_diff([[1, 1, 0], [0, 0, 0]], [[2, 2, 0], [0, 0, 0]])
+    assert ev[0][0] == "recoloured" and ev[0][3] == (1, 2)
+    assert str(ak.diff([[1, 2]], [[1, 3]])) == "same shape; 1/2 cells change in box (0, 1, 0, 1); 2->3:1"
+    assert "output = input scaled x2x2" in str(ak.diff([[1, 2]], ak.scale([[1, 2]], 2)))
+    assert ak.size_rule(TASK["train"]).kind == "same as input"
+    assert ak.gravity([[1, 1, 0], [0, 0, 0], [0, 0, 0]], rigid=True).tolist() == [[0, 0, 0], [0, 0, 0], [1, 1, 0]]
+    assert ak.gravity([[1, 0], [2, 0], [0, 0]], "down").tolist() == [[0, 0], [1, 0], [2, 0]]
+    ns = {}
+    exec(GOOD, ns)
+    rep = ak.check(ns["transform"], TASK["train"], [TASK["test"][0]["input"]], verbose=False)
+    assert rep["ok"] and rep["text"].startswith("check: 2/2 training pairs correct")
+    assert rep["tests"][0]["out"].tolist() == [[0, 0, 5], [7, 0, 0]]
+    bad = ak.check(lambda g: g, TASK["train"], verbose=False)
+    assert not bad["ok"] and "cells wrong in box" in bad["pairs"][0]["why"]
+    assert "2 train pairs; task background 0" in ak.describe(TASK["train"], [TASK["test"][0]["input"]])
 
 
 def test_invariants_and_flag():
@@ -141,3 +190,16 @@ def test_session_client_against_cpu_server():
         server.should_exit = True
         th.join(timeout=10)
         eng.stop()
+
+
+def test_vote_partial_weights_and_verified_override():
+    """Partial evidence weighs 0.5 x pass rate; a grid with any verified vote ranks only by its votes."""
+    g1, g2, g3 = [[1]], [[2]], [[3]]
+    part = lambda g, ok: {"verified": False, "tests": [g], "n_ok": ok, "n_train": 4}
+    recs = [{"progs": [part(g1, 4)], "answer": [g2]},          # g2 answer 1.0, g1 partial 0.5
+            {"progs": [part(g3, 2)], "answer": [g3]},          # g3 answer 1.0 + partial 0.25
+            {"progs": [{"verified": True, "tests": [g1], "n_ok": 4, "n_train": 4}]}]
+    r = rank(recs, 1)[0]
+    assert r["attempts"] == [g1, g3] and r["from"] == ["ver", "fb"] and r["n_verified"] == 1
+    r = rank(recs[:2], 1)[0]
+    assert r["attempts"] == [g3, g2] and r["votes"] == [0, 0]

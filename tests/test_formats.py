@@ -64,6 +64,25 @@ def test_runtime_blocks_roundtrip():
     assert torch.allclose(rt.unpack_blocks(rt.pack_f16(wh), 16, 64, 128), wh.half().float())
 
 
+def test_tensor_core_operands_are_fp16_products():
+    """The operand view equals the dequant stage's arithmetic: fp16 value times fp16 scale, rounded once."""
+    g = torch.Generator().manual_seed(3)
+    for bits in (2, 3, 4):
+        R, K = 200, 256
+        q = torch.randint(0, 1 << bits, (R, K), generator=g, dtype=torch.int32)
+        s = (torch.rand(R, K // 128, generator=g) * 0.01 + 1e-3).half()
+        z = torch.randint(0, 1 << bits, (R, K // 128), generator=g).to(torch.uint8)
+        op = rt.tensor_core_operands(rt.pack_q(q, s, z, bits), bits, R, K)
+        want = ((q.view(R, 2, 128) - z.int()[..., None]).half() * s[..., None]).view(R, K)
+        assert op.dtype == torch.float16 and torch.equal(op, want)
+    w = torch.randn(130, 256, generator=g) * 0.05
+    w8, sc = rt.quantize_fp8_blocks(w)
+    op = rt.tensor_core_operands(rt.pack_fp8(w8, sc), 8, 130, 256)
+    s16 = sc.half().repeat_interleave(128, 0)[:130].repeat_interleave(128, 1)
+    assert torch.equal(op, w8.half() * s16)
+    assert (op.float() - rt.dequant_fp8_blocks(w8, sc)).abs().max() <= rt.dequant_fp8_blocks(w8, sc).abs().max() * 2e-3
+
+
 def test_gate_up_perm():
     p = rt.gate_up_perm(128)
     assert p[:64].tolist() == list(range(64)) and p[64:128].tolist() == list(range(128, 192))
@@ -96,8 +115,10 @@ def test_lowbit_files_and_fn_delta_roundtrip(tmp_path):
     assert (delta / "manifest.json").exists()
     reb = tmp_path / "reb"
     deltas.build(base, [delta], reb)
-    ok, n_md5, n_t, bad = deltas.check(reb, der)
-    assert ok, bad
+    diff = deltas.verify_build(reb, der)
+    assert diff.ok and diff.identical, diff
+    assert deltas.content_digest({"a": torch.ones(2)}) != deltas.content_digest({"a": torch.ones(2).half()})
+    assert deltas.content_digest([1, (2, 3)]) != deltas.content_digest([1, [2, 3]])
     # a corrupted delta is refused by its manifest
     with open(delta / "router-L00.pt", "ab") as f:
         f.write(b"x")

@@ -81,3 +81,29 @@ def test_train_two_ranks_resume_and_export(tmp_path):
     e = 3
     want = (base.blobs[e].gu_s.float() * t3["moe.1.t_gu"][e].exp()).half()
     assert torch.equal(lay.blobs[e].gu_s, want)
+
+
+def test_vocab_logprob_matches_autograd():
+    """Chunked log-prob with recomputed backward equals log_softmax + gather under plain autograd."""
+    g = torch.Generator().manual_seed(0)
+    h = torch.randn(37, 16, generator=g, requires_grad=True)
+    W = torch.randn(50, 16, generator=g, requires_grad=True)
+    y = torch.randint(0, 50, (37,), generator=g)
+    wgt = torch.randn(37, generator=g)
+    lp = rl.VocabLogProb.apply(h, W, y, 8)
+    (lp * wgt).sum().backward()
+    h2, W2 = h.detach().clone().requires_grad_(), W.detach().clone().requires_grad_()
+    ref = torch.log_softmax(h2 @ W2.t(), -1).gather(1, y[:, None])[:, 0]
+    (ref * wgt).sum().backward()
+    torch.testing.assert_close(lp, ref)
+    torch.testing.assert_close(h.grad, h2.grad)
+    torch.testing.assert_close(W.grad, W2.grad)
+
+
+def test_ppo_surrogate_clips_ratio():
+    lp = torch.tensor([0.0, -1.0, -2.0])
+    old = torch.tensor([0.0, -1.5, -1.0])
+    obj, n = rl.surrogate(lp, 1.0, old, eps=0.2)
+    rho = torch.exp(lp - old)
+    assert n == 2 and abs(float(obj) - float(torch.minimum(rho, rho.clamp(0.8, 1.2)).sum())) < 1e-6
+    assert float(rl.surrogate(lp, -2.0)[0]) == 6.0

@@ -77,3 +77,16 @@ def test_noalloc_rejects_oversize_request():
            cfg.indexer_heads, cfg.indexer_dim, max_comp, 16, cfg.indexer_ratio, 1,
            torch.cuda.current_stream().cuda_stream)
     assert rc == 2
+
+
+def test_noalloc_rejects_misaligned_keys():
+    """A key pointer that the 16-byte vector loads cannot read is refused before any launch."""
+    f, _ = _fn()
+    cfg = fn_small_config(indexer_budget=64)
+    iq, comp, slots, pos = _inputs(cfg, 4, 1, 300, seed=5)
+    sel = torch.zeros(4, 16, dtype=torch.int32, device="cuda")
+    sparse = torch.zeros(4, dtype=torch.int32, device="cuda")
+    rc = f(iq.data_ptr(), comp.data_ptr() + 2, 1, slots.data_ptr(), pos.data_ptr(), sel.data_ptr(),
+           sparse.data_ptr(), 4, cfg.indexer_heads, cfg.indexer_dim, comp.shape[1], 16, cfg.indexer_ratio, 1,
+           torch.cuda.current_stream().cuda_stream)
+    assert rc == 1
