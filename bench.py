@@ -25,14 +25,15 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-BASELINE_TOKS = 1120.0  # published FN generated tok/s (4x L4, RC9)
+BASELINE_TOKS = 1120.0  # the reference's published FN generated tok/s (4x L4, RC9 Kaggle run)
 METRIC = "generated tok/s (box, max over ranks) 3/4-bit MoE decode @1/2/4/8 B200; p50 TPOT"
 
 
 def reference_arm(args):
     reason = ("the reference serves Qwen3.8-Flash-Next only through vLLM 0.32 with its `fnext` overlay patches "
               "(model class qwen4_exp); this image has vLLM 0.22, which has no qwen4_exp model, and the reference "
-              "ships no engine of its own (only the `arcstats` plugin installs, into baseline/_ref)")
+              "ships no engine of its own. Its installable `arcstats` package (baseline/_ref) carries its MoE and "
+              "FP8 GEMM kernels, which launch/ref_kernels.py times against ours on identical decode shapes")
     print(json.dumps({"impl": "reference", "metric": METRIC, "unavailable": reason, "n_gpus": args.gpus}))
 
 
@@ -225,7 +226,9 @@ def main():
         out = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": Wm, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": round(value / BASELINE_TOKS, 3), "dtype": "bf16",
+            "vs_baseline": round(value / BASELINE_TOKS, 3),
+            "dtype": "fp16 activations x fp8 weights (dense); int8 activations per 128-column group x 4/3-bit "
+                     "weights (decode MoE); fp32 accumulation",
             "data": "synthetic (random-init weights N(0,0.02); random cache state for 6k-12k-token contexts)",
             "config": {"model": f"flashnext-shaped {cfg.num_layers}L h{cfg.hidden_size} {cfg.n_experts}/"
                                  f"{cfg.n_experts_orig} experts top-{cfg.top_k} 4/3-bit g128 + FP8 128x128 dense",

@@ -167,3 +167,44 @@ def test_gemv_grouped_matches_reference(epi):
         wgemm.gemv_grouped(xs, ws, items, n_items, items.shape[0], out_g, row_dst=addr)
         torch.cuda.synchronize()
         assert torch.allclose(dst[perm_rows].cpu(), out_g.cpu())
+
+
+@pytest.mark.gpu
+def test_moe_layer_fullsize_error_bound():
+    """A full-size FN decode MoE layer (320 experts, hidden 2560, expert FFN 640, top-10, 4/3-bit, 64 tokens) on the
+    decode path (int8 activations per 128-column group, fp16 intermediate) against an fp32 oracle on the same
+    dequantized weights: the error this precision choice costs, bounded."""
+    from arcagi2_flashnext_dots3_b200.config import fn_config
+    from arcagi2_flashnext_dots3_b200.models import fn_weights
+    from arcagi2_flashnext_dots3_b200.ops import fn_ops, wgemm
+    cfg = fn_config()
+    E, H, I, k, T = cfg.n_experts, cfg.hidden_size, cfg.moe_inter, cfg.top_k, 64
+    g = torch.Generator(device="cuda").manual_seed(11)
+    gu, dn = fn_weights._random_experts(cfg, g, torch.device("cuda"))
+    x = torch.randn(T, H, generator=g, device="cuda").half()
+    ids, w = fn_ops.moe_route(torch.randn(T, E + 1, generator=g, device="cuda"), E, k)
+    P = T * k
+    n_tile = wgemm.GEMV_MAX_TOK
+    max_items = (P + n_tile - 1) // n_tile + E
+    pair_pos, items, n_items = fn_ops.moe_plan(ids, E, n_tile, max_items)
+    xs = fn_ops.moe_scatter(x, pair_pos)
+    act = torch.empty(P, I, dtype=torch.float16, device="cuda")
+    ypair = torch.empty(P, H, dtype=torch.float32, device="cuda")
+    wgemm.gemv_grouped(xs, gu, items, n_items, max_items, act, epi=wgemm.EPI_SILU_MUL)
+    wgemm.gemv_grouped(act, dn, items, n_items, max_items, ypair)
+    h = torch.zeros(T, H, dtype=torch.float32, device="cuda")
+    fn_ops.moe_combine(h, ypair, pair_pos, w, torch.zeros(T, H, device="cuda"),
+                       torch.full((T,), float("-inf"), device="cuda"), torch.ones(T, 1, device="cuda"))
+    ref = torch.zeros(T, H, dtype=torch.float64, device="cuda")
+    ids_l, x32 = ids.long(), x.float()
+    for e in torch.unique(ids_l).tolist():
+        t, j = (ids_l == e).nonzero(as_tuple=True)
+        a = wgemm._ref_apply(x32[t] @ gu.dense(e).t(), wgemm.EPI_SILU_MUL)
+        y = a @ dn.dense(e).t()
+        ref.index_add_(0, t, (y * w[t, j, None]).double())
+        gu._dense_cache = dn._dense_cache = None
+    ref = ref.float()
+    err = (h - ref).abs()
+    rel_max = float(err.max() / ref.abs().max())
+    rel_mean = float(err.mean() / ref.abs().mean())
+    assert rel_max < 3e-2 and rel_mean < 1e-2, (rel_max, rel_mean)
