@@ -141,7 +141,8 @@ class D3Config:
     kv_rescale: bool = True              # MLA q/kv LoRA rescale sqrt(hidden / rank)
     dense_fp8: bool = True               # dense weights block-FP8 128x128
     eos_token_id: int = 1
-    dsa_pattern: str = "FFSFSFSFSFFSF"   # index-share pattern over the DSA layers
+    dsa_pattern: str = "FFSFSFSFSFFSF"   # index-share pattern over the DSA layers (used when index_share is on)
+    index_share: bool = False            # DSA layers marked 'S' reuse the top-k of the latest 'F' layer
     dsa_every: int = 0                   # 0: DSA layers spread evenly (13 of 46)
     n_dsa_layers: int = 13
     index_heads: int = 64
@@ -170,6 +171,20 @@ class D3Config:
         step = self.num_layers / self.n_dsa_layers
         dsa = {int(i * step) for i in range(self.n_dsa_layers)}
         return "dsa" if l in dsa else "swa"
+
+    def dsa_layers(self) -> list:
+        return [l for l in range(self.num_layers) if self.layer_kind(l) == "dsa"]
+
+    def shared_index_layers(self) -> set:
+        """DSA layers that skip their own indexer and reuse the top-k of the most recent indexing ('F') layer
+        (the reference's index_share.py: one 'F'/'S' character per DSA layer in model order, the first 'F')."""
+        if not self.index_share:
+            return set()
+        dsa = self.dsa_layers()
+        p = self.dsa_pattern.strip().upper()
+        if len(p) != len(dsa) or set(p) - {"F", "S"} or p[0] != "F":
+            raise ValueError(f"dsa_pattern {self.dsa_pattern!r}: need {len(dsa)} characters of F/S starting with F")
+        return {l for l, c in zip(dsa, p) if c == "S"}
 
     def bits_of(self, e: int) -> int:
         # 96 experts at 3-bit and 48 at 2-bit in the shipped build

@@ -13,8 +13,9 @@ dotsnote/engine/vllm_patch/vllm/models/dots3_note/nvidia/model.py:513):
     o[h] = o_lat[h] @ W_UV[h]^T, times sigmoid(g)     absorption back + gate
     h += o @ W_o^T ; x = rms(h, ln2) ; h += MoE(x) (sigmoid router + bias, 3/2-bit experts, shared expert)
 
-Every projection runs on the tcgen05 weight-dequant GEMM; the two per-head absorption products are batched
-cuBLAS GEMMs (small dense bf16 matrices); the rest are the kernels of csrc/k_d3.cu and the FN MoE kernels.
+Every projection runs on the tcgen05 weight-dequant GEMM, the two per-head absorption products too (one grouped
+launch each, every head an "expert" of an fp16 weight set); the rest are the kernels of csrc/k_d3.cu and the FN
+MoE kernels.
 """
 from __future__ import annotations
 
@@ -48,8 +49,9 @@ def allocate_caches(cfg, device, n_slots: int, max_len: int, block_size: int = 6
         D = cfg.latent_of(l) + cfg.qk_rope_dim
         latent.append(torch.zeros(n_blocks, block_size, D, dtype=torch.float32 if cpu else torch.float8_e4m3fn,
                                   device=dev))
+        own_index = cfg.layer_kind(l) == "dsa" and l not in cfg.shared_index_layers()
         idx.append(torch.zeros(n_slots, max_len, cfg.index_dim, dtype=torch.float32 if cpu else torch.bfloat16,
-                               device=dev) if cfg.layer_kind(l) == "dsa" else None)
+                               device=dev) if own_index else None)
     return D3Caches(latent, idx, torch.zeros(n_slots, max_blocks, dtype=torch.int32, device=dev), block_size,
                     n_blocks, max_len)
 
@@ -67,32 +69,64 @@ class D3Model:
         self.act = ops.act_dtype(self.device)
         self.rope = d3.rope_table(caches.max_len + 8, cfg.qk_rope_dim, cfg.rope_theta, self.device)
         self.scale = (cfg.qk_nope_dim + cfg.qk_rope_dim) ** -0.5
+        self.shared_index = cfg.shared_index_layers()
+        self.overlap = None     # utils.observe.TopkOverlap: per-step top-k overlap between DSA layers (eval only)
 
     def _mm(self, x, ws, epi=wgemm.EPI_STORE, out_dtype=torch.float32):
         if not x.is_cuda:
             return wgemm.matmul(x.float(), ws, epi=epi, out_dtype=torch.float32)
         return wgemm.matmul(x, ws, epi=epi, out_dtype=out_dtype)
 
-    def _bmm(self, a, b):
-        """[H, T, k] x [H, k, n] -> [H, T, n] (bf16 on GPU)."""
-        return torch.bmm(a, b)
+    def _head_items(self, H: int, T: int, n_tile: int):
+        """Grouped-GEMM plan with one expert per head: items (h, first row h*T + s, count, 0) over n_tile chunks."""
+        key = (H, T, n_tile)
+        cache = self.__dict__.setdefault("_items", {})
+        if key not in cache:
+            it = [[h, h * T + s, min(n_tile, T - s), 0] for h in range(H) for s in range(0, T, n_tile)]
+            cache[key] = (torch.tensor(it, dtype=torch.int32, device=self.device),
+                          torch.tensor([len(it)], dtype=torch.int32, device=self.device))
+        return cache[key]
+
+    def _absorb(self, x: torch.Tensor, p: dict, which: str) -> torch.Tensor:
+        """Per-head latent absorption [H, T, k] -> [H, T, n]: q_lat = q_nope[h] @ uk[h] (which="uk") or
+        o[h] = o_lat[h] @ uv[h]^T (which="uv"). On the GPU one tcgen05 grouped GEMM over all heads (every head is
+        an expert of a fp16 weight set); on the CPU torch.bmm on the dense matrices."""
+        if not x.is_cuda:
+            return torch.bmm(x, p["uk"]) if which == "uk" else torch.bmm(x, p["uv"].transpose(1, 2))
+        ws = p[which + "_ws"]
+        H, T, K = x.shape
+        n_tile = wgemm.pick_n_tile(T)
+        items, n_items = self._head_items(H, T, n_tile)
+        out = torch.empty(H, T, ws.rows, dtype=torch.bfloat16, device=x.device)
+        x16 = x.reshape(H * T, K).half()
+        if ws.K != K:   # zero-padded K (small head dims)
+            x16 = torch.nn.functional.pad(x16, (0, ws.K - K))
+        wgemm.grouped(x16, ws, items, n_items, items.shape[0], out.view(H * T, ws.rows), n_tile=n_tile)
+        return out
 
     def _attn(self, x, p, l, slots, positions, n_tok):
         cfg, c = self.cfg, self.c
         P = self._mm(x, p["a"])
+        shared = l in self.shared_index
         qc, gate, iw = d3.mla_prep(P, cfg, l, p, self.rope, c.latent[l], c.block_table, c.idx[l], slots, positions,
-                                   n_tok)
+                                   n_tok, index=not shared)
         Q = self._mm(qc, p["qb"])
         q_nope, q_pe, iq = d3.mla_qsplit(Q, cfg, l, self.rope, positions, n_tok)
-        q_lat = self._bmm(q_nope, p["uk"])                      # [H, T, kvr]
+        q_lat = self._absorb(q_nope, p, "uk")                   # [H, T, kvr]
         if cfg.layer_kind(l) == "dsa":
-            sel = d3.dsa_select(iq, iw, c.idx[l], slots, positions, n_tok, cfg.index_topk, c.max_len)
+            if shared:     # index sharing: the latest indexing layer's selection, no scoring of our own
+                sel = self._sel
+            else:
+                sel = d3.dsa_select(iq, iw, c.idx[l], slots, positions, n_tok, cfg.index_topk, c.max_len)
+                self._sel = sel
+            if self.overlap is not None:
+                self.overlap.add(l, sel, positions, n_tok)
             window = 0
         else:
             sel, window = None, cfg.swa_window
         o_lat = d3.mla_attn(q_lat, q_pe, c.latent[l], c.block_table, slots, positions, n_tok, sel, window,
                             self.scale)
-        o = self._bmm(o_lat, p["uv"].transpose(1, 2))           # [H, T, dv]
+        o = self._absorb(o_lat, p, "uv")                        # [H, T, dv]
         if self.tp is not None:  # row-parallel o-projection fused with the all-reduce; adds into h itself
             self.tp.linear_allreduce_add(self, d3.mla_out(o, gate), p["o"], self._h)
             return None

@@ -59,6 +59,25 @@ def _f32(t, device):
     return t.float().to(device)
 
 
+def absorb_sets(uk: torch.Tensor, uv: torch.Tensor, device) -> dict:
+    """The per-head absorption matrices as two grouped fp16 weight sets, one "expert" per head, for the tcgen05
+    grouped GEMM: ``uk_ws`` rows = latent r, K = dn (head h holds uk[h]^T), ``uv_ws`` rows = dv, K = r (uv[h])."""
+    H, dn, r = uk.shape
+    dv = uv.shape[1]
+    kp = (dn + 127) // 128 * 128      # the GEMM's K is whole 128-column groups: zero columns pad a small dn
+    wk = [rt.pack_f16(torch.nn.functional.pad(uk[h].t().float(), (0, kp - dn))) for h in range(H)]
+    wv = [rt.pack_f16(uv[h].float()) for h in range(H)]
+    return {"uk_ws": wgemm.build_weight_set(wk, [16] * H, r, kp, device=device),
+            "uv_ws": wgemm.build_weight_set(wv, [16] * H, dv, r, device=device)}
+
+
+def _absorb_entries(uk, uv, dev, low) -> dict:
+    """CPU keeps the dense matrices (torch path); a GPU keeps only the grouped weight sets."""
+    if dev.type == "cpu":
+        return {"uk": uk.to(dev, low), "uv": uv.to(dev, low)}
+    return absorb_sets(uk.to(dev), uv.to(dev), dev)
+
+
 def to_engine(W: dict, cfg, device) -> dict:
     dev = torch.device(device)
     dn, dr, dv = cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim
@@ -78,8 +97,7 @@ def to_engine(W: dict, cfg, device) -> dict:
              "attn": {"a": wgemm.build_weight_set([rt.pack_f16(torch.cat(rows_a, 0))], [16],
                                                   sum(r.shape[0] for r in rows_a), cfg.hidden_size, device=dev),
                       "qb": _ws(torch.cat(rows_b, 0), cfg, dev),
-                      "uk": kvb[:, :dn, :].contiguous().to(dev, low),
-                      "uv": kvb[:, dn:, :].contiguous().to(dev, low),
+                      **_absorb_entries(kvb[:, :dn, :].contiguous(), kvb[:, dn:, :].contiguous(), dev, low),
                       "o": _ws(a["o"], cfg, dev),
                       **{k: _f32(a[k], dev) for k in ("q_ln", "kv_ln", "kr_ln")}}}
         if dsa:
@@ -142,8 +160,8 @@ def random_engine(cfg, device, seed: int = 0, tp=None, shard_vocab: bool = False
         rows_a = qr + kvr + dr + H + iD + iH
         M = {"ln1": 1.0 + rn(Hd, std=0.1), "ln2": 1.0 + rn(Hd, std=0.1),
              "attn": {"a": ws16(rows_a, Hd), "qb": _ws(rn(H * (dn + dr) + iH * iD, qr), cfg, dev),
-                      "uk": rn(H, dn, kvr, std=0.05).to(low),
-                      "uv": rn(H, dv, kvr, std=0.05).to(low),
+                      **_absorb_entries(rn(H, dn, kvr, std=0.05).to(low), rn(H, dv, kvr, std=0.05).to(low),
+                                        dev, low),
                       "o": _ws(rn(Hd, H * dv), cfg, dev),
                       "q_ln": 1.0 + rn(qr, std=0.1), "kv_ln": 1.0 + rn(kvr, std=0.1), "kr_ln": 1.0 + rn(dr, std=0.1)}}
         if dsa:

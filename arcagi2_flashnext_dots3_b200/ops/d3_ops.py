@@ -54,11 +54,12 @@ def add_rms(h, y, w, eps, out_dtype=torch.float16):
     return out
 
 
-def mla_prep(P, cfg, l, p, rope, cache, block_table, idx_cache, slots, positions, n_tok):
-    """Returns (qc [T, qr] act, gate logits [T, H], index weights [T, iH] or None); writes the cache rows."""
+def mla_prep(P, cfg, l, p, rope, cache, block_table, idx_cache, slots, positions, n_tok, index: bool = True):
+    """Returns (qc [T, qr] act, gate logits [T, H], index weights [T, iH] or None); writes the cache rows.
+    ``index=False`` (a DSA layer that shares another layer's top-k) skips the index key and weights."""
     T = P.shape[0]
     qr, kvr, dr, H = cfg.q_lora_rank, cfg.latent_of(l), cfg.qk_rope_dim, cfg.heads_of(l)
-    dsa = cfg.layer_kind(l) == "dsa"
+    dsa = cfg.layer_kind(l) == "dsa" and index
     iD, iH = (cfg.index_dim, cfg.index_heads) if dsa else (0, 0)
     off_g = qr + kvr + dr
     off_ik, off_iw = off_g + H, off_g + H + iD

@@ -144,3 +144,56 @@ def memory_census(weights: dict = None, caches=None, device=None) -> dict:
                             "reserved": s.get("reserved_bytes.all.current", 0),
                             "peak_allocated": s.get("allocated_bytes.all.peak", 0), "free": free, "total": total}
     return out
+
+
+class TopkOverlap:
+    """Top-k agreement between DSA layers (the statistic behind an index-sharing pattern; the reference's
+    index_share.py TopkOverlap). For every pair of DSA layers (a, b) and every query row with a sparse selection,
+    |topk_a & topk_b| / k is accumulated into bins of the number of visible keys. ``add`` collects one layer's
+    selection during a step, ``end_step`` scores the pairs and clears the step; ``table`` / ``save`` report means."""
+    BINS = (0, 2048, 4096, 8192, 16384, 32768, 1 << 30)
+
+    def __init__(self):
+        self._step = {}
+        self.sum = {}
+        self.cnt = {}
+
+    def add(self, layer: int, sel: torch.Tensor, positions: torch.Tensor, n_tok: int):
+        pos = positions.long().repeat_interleave(n_tok) + torch.arange(n_tok, device=positions.device).repeat(
+            positions.shape[0])
+        self._step[layer] = (sel.detach().clone(), pos + 1)
+
+    def end_step(self):
+        layers = sorted(self._step)
+        nb = len(self.BINS) - 1
+        for i, a in enumerate(layers):
+            sa, vis = self._step[a]
+            T, k = sa.shape
+            ok = sa[:, 0] >= 0
+            if not bool(ok.any()):
+                continue
+            L = int(vis.max())
+            mark = torch.zeros(T, L + 1, dtype=torch.bool, device=sa.device)
+            mark.scatter_(1, sa.long().clamp(0, L), True)
+            bins = torch.bucketize(vis, torch.tensor(self.BINS[1:-1], device=vis.device), right=True)
+            for b in layers[i + 1:]:
+                sb = self._step[b][0]
+                hit = (mark.gather(1, sb.long().clamp(0, L)) & (sb >= 0)).sum(1).float() / k
+                valid = ok & (sb[:, 0] >= 0)
+                s = torch.zeros(nb, device=sa.device).index_add_(0, bins[valid], hit[valid])
+                n = torch.zeros(nb, device=sa.device).index_add_(0, bins[valid], torch.ones_like(hit[valid]))
+                key = (a, b)
+                self.sum[key] = self.sum.get(key, 0) + s.cpu()
+                self.cnt[key] = self.cnt.get(key, 0) + n.cpu()
+        self._step = {}
+
+    def table(self) -> dict:
+        """{(layer_a, layer_b): [mean overlap per context bin, nan where empty]}."""
+        return {k: (self.sum[k] / self.cnt[k]).tolist() for k in self.sum}
+
+    def save(self, path: str):
+        import numpy as np
+        keys = sorted(self.sum)
+        np.savez(path, pairs=np.array(keys, dtype=np.int64), bins=np.array(self.BINS, dtype=np.int64),
+                 sum=np.stack([self.sum[k].numpy() for k in keys]) if keys else np.zeros((0, 6)),
+                 cnt=np.stack([self.cnt[k].numpy() for k in keys]) if keys else np.zeros((0, 6)))

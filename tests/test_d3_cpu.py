@@ -61,3 +61,33 @@ def test_d3_two_sequences_batched_decode():
     for i, q in enumerate(seqs):
         ref = R.forward(W, cfg, q)[-1]
         assert (lg[i] - ref).abs().max() < 2e-3 * ref.abs().max()
+
+
+def test_index_share_reuses_topk_and_overlap_stats():
+    """Index sharing: an 'S' DSA layer keeps no index-key cache and attends to the latest 'F' layer's top-k; the
+    overlap statistic reads 1.0 between them and stays in [0, 1] between independent indexers."""
+    import dataclasses
+    from arcagi2_flashnext_dots3_b200.utils.observe import TopkOverlap
+    base = d3_small_config()
+    dsa = base.dsa_layers()
+    assert len(dsa) == 2
+    W = random_dense(base, seed=0)
+    ids = torch.randint(0, base.vocab_size, (40,), generator=torch.Generator().manual_seed(2))
+    res = {}
+    for name, cfg in (("own", base), ("share", dataclasses.replace(base, index_share=True, dsa_pattern="FS"))):
+        m, alloc = _model(cfg, W)
+        m.overlap = TopkOverlap()
+        m.assign_blocks(0, 44, alloc)
+        x = m.step(ids, torch.tensor([0], dtype=torch.int32), torch.tensor([0], dtype=torch.int32), 40)
+        m.overlap.end_step()
+        res[name] = (x, m.overlap.table(), m)
+    assert res["share"][2].c.idx[dsa[1]] is None and res["own"][2].c.idx[dsa[1]] is not None
+    shared = res["share"][1][(dsa[0], dsa[1])]
+    assert all(v == 1.0 for v in shared if v == v) and any(v == v for v in shared)
+    own = [v for v in res["own"][1][(dsa[0], dsa[1])] if v == v]
+    assert own and all(0.0 <= v <= 1.0 for v in own)
+    try:
+        dataclasses.replace(base, index_share=True, dsa_pattern="SF").shared_index_layers()
+        raise AssertionError("pattern starting with S accepted")
+    except ValueError:
+        pass

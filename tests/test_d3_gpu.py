@@ -56,3 +56,17 @@ def test_d3_llm_greedy_matches_oracle_prefix():
     for p, o in zip(prompts, outs):
         ref = R.greedy(W, cfg, torch.tensor(p), 4)
         assert o[0] == ref[0]
+
+
+def test_d3_index_share_gpu_vs_cpu():
+    """Index sharing on the GPU (the shared layer's prep skips the index key; its attention reads the previous
+    layer's top-k) agrees with the CPU engine path under the same pattern."""
+    import dataclasses
+    cfg = dataclasses.replace(d3_small_config(), index_share=True, dsa_pattern="FS")
+    W = random_dense(cfg, seed=2)
+    g = torch.Generator().manual_seed(5)
+    ids = [torch.randint(0, cfg.vocab_size, (n,), generator=g) for n in (30,)]
+    a = _run("cpu", cfg, W, ids)
+    b = _run("cuda", cfg, W, ids)
+    err = (a[0] - b[0]).abs().max() / a[0].abs().max()
+    assert err < 3e-2, err
