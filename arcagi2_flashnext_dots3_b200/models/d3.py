@@ -231,6 +231,8 @@ class D3Model:
         per row crosses the group."""
         lg = self._mm(x, self.W["lm_head"])
         if self.vocab_sharded:
+            if getattr(self.tp, "fake", False):
+                return self.tp.sharded_pick(lg, self.W["vocab_range"][0], temperature, seed, step)
             from ..parallel.tp import sharded_pick
             return sharded_pick(lg, self.W["vocab_range"][0], self.tp.group, temperature, seed, step)
         if temperature <= 0:

@@ -61,3 +61,25 @@ def test_vocab_sharded_pick_cpu(nproc):
            "--master-addr=127.0.0.1", f"--master-port={29690 + nproc}", os.path.join(HERE, "vocab_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "VOCAB_OK" in r.stdout, (r.stdout[-2000:], r.stderr[-3000:])
+
+
+def test_fake_tp_rank_shapes_and_step():
+    """One process emulating rank 0 of TP-2: weights at the shard's shapes (half the heads, half the experts,
+    half the vocabulary), caches with the rank's heads, a decode step runs and picks ids inside the rank's slice."""
+    from arcagi2_flashnext_dots3_b200.config import d3_small_config
+    from arcagi2_flashnext_dots3_b200.models import d3_weights
+    from arcagi2_flashnext_dots3_b200.parallel.fake_tp import fake_rank_model
+    cfg = d3_small_config(num_layers=3, swa_n_heads=4, qk_nope_dim=64)
+    m, W, c, grp = fake_rank_model(cfg, 2, "cpu", n_slots=2, max_len=32, block_size=8, shard_vocab=True)
+    full = d3_weights.random_engine(cfg, "cpu", seed=0)
+    assert m.cfg.n_heads == cfg.n_heads // 2 and grp.buf.shape == (2, 2, 64 * cfg.hidden_size)
+    assert W["lm_head"].rows == full["lm_head"].rows // 2
+    l_moe = next(l for l in range(cfg.num_layers) if cfg.is_moe(l))
+    assert W["layers"][l_moe]["moe"]["gu"].n_experts == full["layers"][l_moe]["moe"]["gu"].n_experts // 2
+    from arcagi2_flashnext_dots3_b200.engine.block_manager import BlockAllocator
+    alloc = BlockAllocator(c.n_blocks, 2)
+    m.assign_blocks(0, 8, alloc)
+    x = m.step(torch.tensor([3, 4, 5], dtype=torch.int32), torch.tensor([0], dtype=torch.int32),
+               torch.tensor([0], dtype=torch.int32), 3)
+    ids = m.pick(x)
+    assert ids.shape == (3,) and int(ids.max()) < W["vocab_range"][1]
