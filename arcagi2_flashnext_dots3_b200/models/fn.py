@@ -93,6 +93,8 @@ class FNModel:
     def __init__(self, cfg, weights: dict, caches: FNCaches, device, ep=None):
         self.cfg = cfg
         self.ep = ep  # parallel.ep.EPGroup: expert-parallel MoE across GPUs (None = all experts local)
+        self.capture = None  # training.capture.RoutingCapture: records MoE inputs / router logits (eager steps)
+        self._layer = 0
         self.W = weights
         self.c = caches
         self.device = torch.device(device)
@@ -175,6 +177,8 @@ class FNModel:
         T = x.shape[0]
         E = cfg.n_experts
         logits = self._mm(x, p["router"])
+        if self.capture is not None:
+            self.capture.record(self._layer, x, logits[:, :E])
         side = self._side_stream(x)
         if side is not None:  # the shared expert runs concurrently with the routed experts (graph-capturable)
             side.wait_stream(torch.cuda.current_stream())
@@ -244,6 +248,7 @@ class FNModel:
                 y = self._attn(x, L["mix"], self.attn_idx[l], slots, positions, n_tok)
             ops.hc_residual(h, y, inj)
             x, inj = self._hc(h, L["mhc"])
+            self._layer = l
             self._moe(x, L["moe"], h, inj)
         x, _ = self._hc(h, W["mixer"], with_inj=False)
         return x

@@ -128,3 +128,30 @@ def test_student_backward_reaches_all_trainables():
     for p in st.parameters():
         assert p.grad is not None and torch.isfinite(p.grad).all()
     assert any(float(m.t_gu.grad.abs().sum()) > 0 for m in st.moe)
+
+
+def test_routing_capture_replay_feeds_keep_selection(tmp_path):
+    """Teacher-forced replay through the engine with the capture hook: per-layer rows and logits on disk, routing
+    counts consistent with top-k, and REAP keep selection from the captured rows."""
+    from arcagi2_flashnext_dots3_b200.config import EngineConfig, fn_small_config
+    from arcagi2_flashnext_dots3_b200.engine.llm import LLM
+    from arcagi2_flashnext_dots3_b200.models import fn_weights
+    from arcagi2_flashnext_dots3_b200.training import capture, compress
+    cfg = fn_small_config(num_layers=2, ple_layers=())
+    W = fn_weights.random_dense(cfg, seed=0, symmetric=False)
+    llm = LLM(cfg, fn_weights.to_engine(W, cfg, "cpu"), "cpu",
+              EngineConfig(max_seqs=2, max_model_len=128, block_size=16, graph_batch_sizes=(1,)))
+    seqs = [torch.randint(0, cfg.vocab_size, (n,), generator=torch.Generator().manual_seed(n)).tolist()
+            for n in (37, 50)]
+    cap = capture.RoutingCapture(tmp_path, cfg.top_k, every=2, flush_rows=16)
+    capture.replay(llm, seqs, cap, chunk=20)
+    st = capture.load_stats(tmp_path)
+    assert st["layers"] == [0, 1] and st["tokens"][0] == 87
+    assert int(st["counts"][0].sum()) == 87 * cfg.top_k
+    assert abs(float(st["wsum"][1].sum()) - 87) < 1e-4
+    x, lg = capture.load_layer(tmp_path, 1)
+    assert x.shape == (44, cfg.hidden_size) and lg.shape == (44, cfg.n_experts)
+    experts = W["layers"][1]["moe"]["experts_dense"]
+    sc = compress.reap_scores(x.float(), lg, experts, cfg.top_k)
+    keep, cov = compress.select_keep(sc, cfg.n_experts // 2, st["wsum"][1])
+    assert len(keep) == cfg.n_experts // 2 and 0 < cov <= 1 and float(sc.sum()) > 0
