@@ -107,3 +107,44 @@ def test_ppo_surrogate_clips_ratio():
     rho = torch.exp(lp - old)
     assert n == 2 and abs(float(obj) - float(torch.minimum(rho, rho.clamp(0.8, 1.2)).sum())) < 1e-6
     assert float(rl.surrogate(lp, -2.0)[0]) == 6.0
+
+
+def test_vocab_topk_grad_and_kl21():
+    from arcagi2_flashnext_dots3_b200.training import kd
+    g = torch.Generator().manual_seed(1)
+    h = torch.randn(21, 12, generator=g, requires_grad=True)
+    W = torch.randn(40, 12, generator=g, requires_grad=True)
+    ids = torch.randint(0, 40, (21, 5), generator=g)
+    wt = torch.randn(21, 5, generator=g)
+    (kd.VocabTopK.apply(h, W, ids, 4) * wt).sum().backward()
+    h2, W2 = h.detach().clone().requires_grad_(), W.detach().clone().requires_grad_()
+    (torch.log_softmax(h2 @ W2.t(), -1).gather(1, ids) * wt).sum().backward()
+    torch.testing.assert_close(h.grad, h2.grad)
+    torch.testing.assert_close(W.grad, W2.grad)
+    lp = torch.log_softmax(torch.randn(3, 40, generator=g), -1)
+    top = lp.topk(5, -1)
+    assert float(kd.kl21(top.values, top.indices, top.values).abs().max()) < 1e-6
+
+
+def test_kd_training_reduces_kl(tmp_path):
+    """KD records from a sharper teacher (the student's own logits x 4): a few optimizer steps on the student's
+    trainables (scales, router, norms) lower the mean top-20 + tail KL."""
+    from arcagi2_flashnext_dots3_b200.training import kd
+    from arcagi2_flashnext_dots3_b200.training.student import FNStudent
+    cfg = fn_small_config(num_layers=2, ple_layers=())
+    W = fn_weights.random_dense(cfg, seed=0, symmetric=False)
+    teacher = FNStudent(cfg, W, "cpu")
+    recs = []
+    for s in range(4):
+        ids = torch.randint(0, cfg.vocab_size, (40,), generator=torch.Generator().manual_seed(s))
+        with torch.no_grad():
+            lp = torch.log_softmax(4.0 * (teacher.hidden(ids) @ teacher.lm_head.float().t()), -1)  # sharper
+        top = lp[9:39].topk(20, -1)      # positions 10..39 scored from hidden rows 9..38
+        recs.append((ids.tolist(), 10, [[10, 40]], top.indices.numpy(), top.values.numpy()))
+    kd.write_kd_records(tmp_path / "d", recs)
+    out = tmp_path / "o"
+    kd.main(["--data", str(tmp_path / "d"), "--build", "random:fn-small", "--out", str(out), "--steps", "6",
+             "--per-step", "4", "--layers", "2", "--trainable", "scales,router,norms", "--lr-scales", "1e-2",
+             "--lr-router", "1e-3", "--lr-norms", "5e-2", "--warmup", "1"])
+    log = [json.loads(l) for l in open(out / "log.jsonl")]
+    assert len(log) == 6 and log[-1]["kl"] < log[0]["kl"], log
