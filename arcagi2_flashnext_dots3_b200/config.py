@@ -242,6 +242,7 @@ class EngineConfig:
     max_seqs: int = 64
     max_model_len: int = 20480
     block_size: int = 64                 # tokens per paged-KV block
+    kv_blocks: int = 0                   # paged-KV blocks in the pool (0: every slot can reach max_model_len)
     kv_dtype: str = "fp8"                # fp8 (e4m3) or bf16 attention KV
     state_dtype: str = "bf16"            # recurrent (GDN) state dtype
     cuda_graphs: bool = True

@@ -134,7 +134,7 @@ class LLM:
         self.scratch = ec.max_seqs
         alloc = getattr(model_cls, "allocate", None) or allocate_caches
         self.caches = alloc(cfg, self.device, ec.max_seqs + 1, ec.max_model_len, ec.block_size,
-                            kv_dtype=ec.kv_dtype, state_dtype=ec.state_dtype)
+                            n_blocks=ec.kv_blocks or None, kv_dtype=ec.kv_dtype, state_dtype=ec.state_dtype)
         self.model = (model_cls or FNModel)(cfg, weights, self.caches, self.device, ep=ep)
         self.alloc = BlockAllocator(self.caches.n_blocks, ec.max_seqs + 1)
         self.model.assign_blocks(self.scratch, 1, self.alloc)

@@ -85,7 +85,13 @@ def create_app(engine: EngineLoop, model_name: str = "arcagi2-b200"):
 
     @app.get("/arc/session/stats")
     async def stats():
-        return JSONResponse({k: int(v) for k, v in engine.stats.items()})
+        out = {k: int(v) for k, v in engine.stats.items()}
+        sched = getattr(engine, "sched", None)
+        if sched is not None:   # scheduler counters: admissions, preemptions, idle-session evictions, KV state
+            out.update({f"sched_{k}": int(v) for k, v in vars(sched.stats).items()})
+            out.update(waiting=len(sched.waiting), running=len(sched.running), idle_sessions=len(sched.idle),
+                       kv_blocks_free=int(engine.llm.alloc.n_free()))
+        return JSONResponse(out)
 
     @app.post("/v1/completions")
     async def completions(req: Request):

@@ -2,8 +2,10 @@
 
 All model work happens on this thread; HTTP handlers talk to it through a command queue and receive events on
 per-request asyncio queues (``loop.call_soon_threadsafe``). Each loop iteration applies the pending commands
-(start = prefill, push = incremental prefill of a kept sequence, close) and then runs one decode step for every
-running sequence (one CUDA-graph replay for the whole batch).
+(start = submit, push = extend a kept session, close) and then runs one iteration of the
+:class:`..engine.scheduler.Scheduler`: admission under the KV budget, a bounded amount of chunked prefill, one
+CUDA-graph decode step for every running sequence; idle sessions keep their KV and are evicted, least recently
+used first, when the cache deadlocks (their next push rebuilds them exactly).
 
 Session semantics follow the reference's `/arc/session` routes (flashnext/kaggle/code_dataset/fnext/session/
 session_ep.py:35-135): a session's KV stays resident between chunks; a chunk ends at its token budget
@@ -35,19 +37,25 @@ class Session:
     keep: bool = False
     oneshot: bool = False           # /v1/completions: end at the first chunk end
     want_lp: bool = False
-    seq: object = None
+    req: object = None              # engine.scheduler.Request
     n: int = 0
     sent: int = 0                   # tokens of seq.out already emitted
     closed: bool = False
     t_start: float = field(default_factory=time.time)
 
+    @property
+    def seq(self):
+        return self.req.seq if self.req is not None else None
+
 
 class EngineLoop:
-    def __init__(self, llm, tokenizer, idle_wait: float = 0.02):
+    def __init__(self, llm, tokenizer, idle_wait: float = 0.02, prefill_budget: int = 4096, chunk: int = 2048):
+        from ..engine.scheduler import Scheduler
         self.llm, self.tok = llm, tokenizer
+        self.sched = Scheduler(llm, prefill_budget=prefill_budget, chunk=chunk)
         self.cmds: queue.Queue = queue.Queue()
         self.sessions: dict = {}
-        self.by_slot: dict = {}
+        self.by_req: dict = {}
         self.stats = Counter()
         self.idle_wait = idle_wait
         self._stop = threading.Event()
@@ -104,9 +112,9 @@ class EngineLoop:
         if s.closed:
             return
         s.closed = True
-        if s.seq is not None:
-            self.by_slot.pop(s.seq.slot, None)
-            self.llm.release(s.seq)
+        if s.req is not None:
+            self.sched.close(s.req)
+            self.by_req.pop(s.req.rid, None)
         self.sessions.pop(s.rid, None)
         self.stats["open"] -= 1
         self._emit(s, {"end": why, "n": s.n})
@@ -118,49 +126,43 @@ class EngineLoop:
             fut.set_result((409, {"ok": False, "error": "session id in use"}))
             return
         try:
-            seq = self.llm.add(kw["prompt_ids"], max_new_tokens=max(1, sp.max_tokens), sp=sp)
+            req = self.sched.submit(kw["prompt_ids"], max_new_tokens=max(1, sp.max_tokens), sp=sp,
+                                    keep_kv=not s.oneshot)
         except (ValueError, RuntimeError) as e:
             fut.set_result((400 if isinstance(e, ValueError) else 503, {"ok": False, "error": str(e)}))
             return
-        s.seq = seq
+        s.req = req
         self.sessions[s.rid] = s
-        self.by_slot[seq.slot] = s
+        self.by_req[req.rid] = s
         self.stats["sessions"] += 1
         self.stats["open"] += 1
         self.stats["start_tokens"] += len(kw["prompt_ids"])
         fut.set_result((200, {"ok": True}))
-        self._emit_new_tokens(s)
-        if seq.done:
-            self._chunk_end(s)
 
     def _push(self, kw, fut):
         s = self.sessions.get(kw["rid"])
         if s is None or s.closed:
             fut.set_result((404, {"ok": False, "error": "no such session"}))
             return
-        seq = s.seq
-        if not seq.done:
+        req = s.req
+        if not req.done:
             fut.set_result((409, {"ok": False, "error": "session is generating"}))
             return
         sp: SamplingParams = kw.get("sp")
         if sp is not None:
-            sp.seed = seq.sp.seed if kw.get("seed") is None else sp.seed
-            seq.sp = sp
+            sp.seed = req.seq.sp.seed if kw.get("seed") is None else sp.seed
         s.keep = bool(kw.get("keep", s.keep))
         try:
-            self.llm.extend(seq, kw["prompt_ids"], max_new_tokens=max(1, int(kw["max_tokens"])))
+            self.sched.extend(req, kw["prompt_ids"], max(1, int(kw["max_tokens"])), sp=sp)
         except ContextFull:
             self.stats["push_refused"] += 1
-            fut.set_result((409, {"ok": False, "error": "ctx_full", "held": seq.pos,
+            fut.set_result((409, {"ok": False, "error": "ctx_full", "held": len(req.history),
                                   "max_model_len": self.llm.ec.max_model_len}))
             self._end(s, "ctx_full")
             return
         self.stats["pushes"] += 1
         self.stats["pushed_tokens"] += len(kw["prompt_ids"])
         fut.set_result((200, {"ok": True}))
-        self._emit_new_tokens(s)
-        if seq.done:
-            self._chunk_end(s)
 
     def _close(self, kw, fut):
         s = self.sessions.get(kw["rid"])
@@ -172,9 +174,9 @@ class EngineLoop:
         handlers = {"start": self._start, "push": self._push, "close": self._close}
         try:
             while not self._stop.is_set():
-                busy = any(not s.seq.done for s in self.sessions.values() if s.seq is not None)
+                busy = self.sched.has_work()
                 try:
-                    item = self.cmds.get(timeout=0 if busy else self.idle_wait) if not busy else self.cmds.get_nowait()
+                    item = self.cmds.get_nowait() if busy else self.cmds.get(timeout=self.idle_wait)
                 except queue.Empty:
                     item = None
                 while item is not None:
@@ -188,16 +190,19 @@ class EngineLoop:
                         item = self.cmds.get_nowait()
                     except queue.Empty:
                         item = None
-                live = [s for s in self.sessions.values() if s.seq is not None and not s.seq.done]
-                if live:
-                    self.llm.step()
-                    self.stats["steps"] += 1
-                    for s in live:
-                        if s.closed:
-                            continue
-                        self._emit_new_tokens(s)
-                        if s.seq.done:
-                            self._chunk_end(s)
+                if not self.sched.has_work():
+                    continue
+                produced = self.sched.step()
+                self.stats["steps"] += 1
+                for rid in produced:
+                    s = self.by_req.get(rid)
+                    if s is None or s.closed:
+                        continue
+                    self._emit_new_tokens(s)
+                for rid in produced:
+                    s = self.by_req.get(rid)
+                    if s is not None and not s.closed and s.req.done:
+                        self._chunk_end(s)
         except Exception:  # pragma: no cover - reported through /health
             self.error = traceback.format_exc()
             for s in list(self.sessions.values()):
