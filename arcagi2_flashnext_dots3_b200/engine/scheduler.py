@@ -57,6 +57,7 @@ class Request:
     t_submit: float = 0.0
     t_first: float = 0.0
     t_idle: float = 0.0
+    t_done: float = 0.0
     preemptions: int = 0
 
     @property
@@ -273,6 +274,7 @@ class Scheduler:
 
     def _chunk_done(self, r: Request):
         r.done = True
+        r.t_done = time.perf_counter()
         self.stats.finished += 1
         if r.keep_kv and not r.closed:
             r.t_idle = time.perf_counter()

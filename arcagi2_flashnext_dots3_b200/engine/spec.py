@@ -120,10 +120,76 @@ class MTPDrafter:
         self._chain(llm, seqs, xm[idx], pos0.long() + torch.tensor(accepted, device=dev), k)
 
 
+class SpecGraph:
+    """One speculative step for a fixed batch bucket, captured as a CUDA graph: verify the k + 1 tokens of every
+    row, count accepted drafts on the device (leading matches of drafts and verify argmaxes), commit the recurrent
+    states with those counts and, with an MTP head, run the head over the accepted rows and chain its next k
+    drafts, all without a host round trip. The accepted rows' next tokens are exactly the verify argmaxes
+    y[0..a], which is what the head reads. Padding rows use the engine's scratch slot."""
+
+    def __init__(self, llm, head, batch: int, k: int):
+        dev = llm.device
+        self.llm, self.head, self.B, self.k = llm, head, batch, k
+        k1 = k + 1
+        self.ids = torch.zeros(batch, k1, dtype=torch.int32, device=dev)
+        self.slots = torch.full((batch,), llm.scratch, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.y = torch.zeros(batch, k1, dtype=torch.int32, device=dev)
+        self.acc = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.nd = torch.zeros(batch, k, dtype=torch.int32, device=dev)
+        self.graph = None
+
+    def _body(self):
+        m, B, k, k1 = self.llm.model, self.B, self.k, self.k + 1
+        x = m.step(self.ids.view(-1), self.slots, self.pos, k1, verify=True)
+        y = greedy_ids(m, x).view(B, k1)
+        match = (self.ids[:, 1:] == y[:, :k]).to(torch.int32)
+        acc = torch.cumprod(match, 1).sum(1).to(torch.int32)
+        m.commit(acc + 1)
+        self.y.copy_(y)
+        self.acc.copy_(acc)
+        if self.head is not None:
+            h = self.head
+            xm = h.step(x, y.reshape(-1), self.slots, self.pos, k1)
+            rows = torch.arange(B, device=x.device) * k1 + acc.long()
+            xa = xm[rows]
+            q = self.pos + acc
+            d = h.draft_ids(xa)
+            drafts = [d]
+            for i in range(1, k):
+                xa = h.step(xa, d, self.slots, (q + i).to(torch.int32), 1)
+                d = h.draft_ids(xa)
+                drafts.append(d)
+            self.nd.copy_(torch.stack(drafts, 1))
+
+    def capture(self):
+        """Warm up on the scratch slot only (a verify step commits recurrent state), then capture."""
+        self.slots.fill_(self.llm.scratch)
+        self.pos.zero_()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self._body()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._body()
+        torch.cuda.synchronize()
+
+    def run(self):
+        self.graph.replay()
+
+
 class SpecDecoder:
-    def __init__(self, llm, drafter, k: int = 3):
+    def __init__(self, llm, drafter, k: int = 3, use_graph: bool = True):
         self.llm, self.drafter, self.k = llm, drafter, k
         self.stats = {"steps": 0, "drafted": 0, "accepted": 0, "emitted": 0}
+        self.use_graph = use_graph and llm.device.type == "cuda" and llm.ec.cuda_graphs
+        self.graphs = {}
+        if self.use_graph and isinstance(drafter, MTPDrafter) and \
+                drafter.head.caches.block_table.shape[0] <= llm.scratch:
+            raise ValueError("the MTP head needs a cache slot for the engine's scratch slot (n_slots > max_seqs)")
 
     def add(self, prompt, max_new_tokens: int = 64):
         llm = self.llm
@@ -135,6 +201,38 @@ class SpecDecoder:
             llm._keep_prefill_rows = False
         return seq
 
+    def _graph_step(self, seqs, drafts):
+        """Verify + commit (+ MTP chain) as one graph replay; returns (y rows, accepted counts) as host lists."""
+        llm, k = self.llm, self.k
+        k1 = k + 1
+        n = len(seqs)
+        bucket = next((b for b in llm.ec.graph_batch_sizes if b >= n), n)
+        g = self.graphs.get(bucket)
+        head = self.drafter.head if isinstance(self.drafter, MTPDrafter) else None
+        if g is None:
+            if head is not None:
+                head.assign_blocks(llm.scratch, 2 * k1 + 8, self.drafter.alloc)
+            llm.model.assign_blocks(llm.scratch, k1 + 1, llm.alloc)
+            g = self.graphs[bucket] = SpecGraph(llm, head, bucket, k)
+            g.capture()
+        for s in seqs:
+            llm.model.assign_blocks(s.slot, s.pos + k1 + 1, llm.alloc)
+            if head is not None:
+                head.assign_blocks(s.slot, s.pos + 2 * k1 + 8, self.drafter.alloc)
+        pad = bucket - n
+        ids = [[s.out[-1]] + list(d) for s, d in zip(seqs, drafts)] + [[0] * k1] * pad
+        g.ids.copy_(torch.tensor(ids, dtype=torch.int32))
+        g.slots.copy_(torch.tensor([s.slot for s in seqs] + [llm.scratch] * pad, dtype=torch.int32))
+        g.pos.copy_(torch.tensor([s.pos for s in seqs] + [0] * pad, dtype=torch.int32))
+        g.run()
+        out = torch.cat([g.y, g.acc[:, None], g.nd], 1).cpu()
+        y = out[:n, :k1].tolist()
+        accepted = out[:n, k1].tolist()
+        if head is not None:
+            for s, row in zip(seqs, out[:n, k1 + 1:].tolist()):
+                self.drafter.next[s.slot] = row
+        return y, accepted
+
     def step(self) -> dict:
         llm, k = self.llm, self.k
         k1 = k + 1
@@ -145,6 +243,9 @@ class SpecDecoder:
             raise ValueError("speculative decoding verifies greedy sequences only")
         dev = llm.device
         drafts = self.drafter.propose(llm, seqs, k)
+        if self.use_graph:
+            y, accepted = self._graph_step(seqs, drafts)
+            return self._advance(seqs, drafts, y, accepted)
         ids = [[s.out[-1]] + list(d) for s, d in zip(seqs, drafts)]
         for s in seqs:
             llm.model.assign_blocks(s.slot, s.pos + k1 + 1, llm.alloc)
@@ -159,6 +260,12 @@ class SpecDecoder:
                 a += 1
             accepted.append(a)
         llm.model.commit(torch.tensor([a + 1 for a in accepted], dtype=torch.int32, device=dev))
+        res = self._advance(seqs, drafts, y, accepted)
+        self.drafter.observe(llm, seqs, x, ids, accepted, k)
+        return res
+
+    def _advance(self, seqs, drafts, y, accepted) -> dict:
+        llm, k = self.llm, self.k
         res = {}
         for s, d, yy, a in zip(seqs, drafts, y, accepted):
             s.pos += a + 1
@@ -173,7 +280,6 @@ class SpecDecoder:
         self.stats["steps"] += 1
         self.stats["drafted"] += k * len(seqs)
         self.stats["accepted"] += sum(accepted)
-        self.drafter.observe(llm, seqs, x, ids, accepted, k)
         return res
 
     def generate(self, prompts, max_new_tokens: int = 64) -> list:

@@ -5,6 +5,7 @@
     python -m arcagi2_flashnext_dots3_b200.launch.kbench attn  [--tokens 64] [--ctx 9000] [--reps 20]
     python -m arcagi2_flashnext_dots3_b200.launch.kbench gdn   [--tokens 64] [--reps 20]
     python -m arcagi2_flashnext_dots3_b200.launch.kbench mla   [--tokens 64] [--ctx 9000] [--reps 20]
+    python -m arcagi2_flashnext_dots3_b200.launch.kbench absorb [--tokens 32] [--reps 20]
 
 Counterpart of the reference's micro-benchmarks and startup gates (dotsnote/kaggle/runtime_dataset/bench_*.py,
 run_l4.py:435 `run_bench`): each case prints one JSON line with the median device time and the achieved
@@ -205,9 +206,44 @@ def bench_mla(args):
         print(json.dumps(row), flush=True)
 
 
+def bench_absorb(args):
+    """D3 per-head latent absorption (q_lat = q_nope[h] @ uk[h], o[h] = o_lat[h] @ uv[h]^T): this framework's
+    grouped tcgen05 GEMM (one expert per head) against torch.bmm (cuBLAS), CUDA-graph timed over weight copies
+    larger than L2."""
+    from ..models import d3_weights
+    from ..models.d3 import D3Model
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    T = args.tokens
+    for kind, H, r in (("dsa", 128, 512), ("swa", 64, 1024)):
+        copies = 4
+        uk = [(torch.randn(H, 128, r, device=dev, generator=g) * 0.05).bfloat16() for _ in range(copies)]
+        uv = [(torch.randn(H, 128, r, device=dev, generator=g) * 0.05).bfloat16() for _ in range(copies)]
+        sets = [d3_weights.absorb_sets(a, b, dev) for a, b in zip(uk, uv)]
+        m = D3Model.__new__(D3Model)
+        m.device = dev
+        qn = (torch.randn(H, T, 128, device=dev, generator=g)).bfloat16()
+        ol = (torch.randn(H, T, r, device=dev, generator=g)).bfloat16()
+        row = {"case": f"absorb_{kind}", "heads": H, "latent": r, "tokens": T,
+               "weight_MB_per_call": round(H * 128 * r * 2 / 2**20, 1)}
+        for which, x in (("uk", qn), ("uv", ol)):
+            def ours(i, which=which, x=x):
+                m._absorb(x, sets[i % copies], which)
+
+            def ref(i, which=which, x=x):
+                if which == "uk":
+                    torch.bmm(x, uk[i % copies])
+                else:
+                    torch.bmm(x, uv[i % copies].transpose(1, 2))
+            for name, fn in (("ours", ours), ("cublas", ref)):
+                from .ref_kernels import _graph_time
+                row[f"{which}_{name}_us"] = round(_graph_time(fn, args.reps) * 1e3, 1)
+        print(json.dumps(row), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["moe", "dense", "attn", "gdn", "mla", "all"])
+    ap.add_argument("case", choices=["moe", "dense", "attn", "gdn", "mla", "absorb", "all"])
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--experts", type=int, default=320)
     ap.add_argument("--ctx", type=int, default=9000)
@@ -215,7 +251,8 @@ def main():
     ap.add_argument("--sweep", action="store_true", help="dense: time every n_tile x split-K combination")
     ap.add_argument("--only", default="", help="dense: comma-separated case names")
     args = ap.parse_args()
-    cases = {"moe": bench_moe, "dense": bench_dense, "attn": bench_attn, "gdn": bench_gdn, "mla": bench_mla}
+    cases = {"moe": bench_moe, "dense": bench_dense, "attn": bench_attn, "gdn": bench_gdn, "mla": bench_mla,
+             "absorb": bench_absorb}
     for name, fn in cases.items():
         if args.case in (name, "all"):
             fn(args)

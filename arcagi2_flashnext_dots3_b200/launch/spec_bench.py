@@ -4,8 +4,9 @@
 
 Random-init weights and random cache state for 6k-12k-token contexts (as in bench.py). With random weights the
 MTP head's drafts are uncorrelated with the model, so its acceptance is a floor; prompt lookup (n-gram) accepts
-whenever the random model repeats itself. The plain (k = 0) row is the same engine without drafts, decoding eagerly
-like the spec path, for an apples-to-apples ratio. One JSON line per (drafter, batch).
+whenever the random model repeats itself. The plain (k = 0) row is the same engine without drafts through the same (graph-captured) verify path.
+``oracle@P`` drafts the model's own greedy continuation with each token kept with probability P, which measures
+the cost/benefit curve at controlled acceptance. One JSON line per (drafter, batch).
 """
 from __future__ import annotations
 
@@ -14,6 +15,41 @@ import json
 import time
 
 import torch
+
+
+class ControlledDrafter:
+    """Drafts the model's own recorded greedy continuation (``ref[slot]``, from a plain decode of the same
+    synthetic context), each draft token kept with probability p and otherwise replaced by a wrong token, so the
+    acceptance rate is controlled: the cost/benefit curve of speculative decoding with random weights."""
+
+    def __init__(self, ref: dict, p: float, vocab: int, seed: int = 0):
+        self.ref, self.p, self.vocab = ref, p, vocab
+        self.g = torch.Generator().manual_seed(seed)
+
+    def propose(self, llm, seqs, k):
+        out = []
+        for s in seqs:
+            n = len(s.out) - 1          # ref[0] follows the context's first pending token, out[0]
+            want = (self.ref[s.slot][n:n + k] + [0] * k)[:k]
+            keep = torch.rand(k, generator=self.g) < self.p
+            out.append([w if kp else (w + 1) % self.vocab for w, kp in zip(want, keep.tolist())])
+        return out
+
+    def observe(self, llm, seqs, x, ids, accepted, k):
+        pass
+
+
+def _reference_outputs(cfg, W, dev, ec, lengths, n_new):
+    """Greedy continuations of the synthetic contexts by plain graph decoding (same seed as the spec run)."""
+    from ..engine.llm import LLM
+    llm = LLM(cfg, W, dev, ec)
+    seqs = llm.synthesize_context(lengths, n_new + 8)
+    while min(len(s.out) for s in seqs) < n_new + 1:
+        llm.step()
+    ref = {s.slot: list(s.out[1:]) for s in seqs}
+    del llm
+    torch.cuda.empty_cache()
+    return ref
 
 
 def run(args):
@@ -41,6 +77,13 @@ def run(args):
                 sd = SpecDecoder(llm, NgramDrafter(), k=0)
             elif drafter == "ngram":
                 sd = SpecDecoder(llm, NgramDrafter(), k=args.k)
+            elif drafter.startswith("oracle@"):
+                del llm
+                torch.cuda.empty_cache()
+                ref = _reference_outputs(cfg, W, dev, ec, lengths, (args.k + 1) * (steps + 3))
+                llm = LLM(cfg, W, dev, ec)
+                seqs = llm.synthesize_context(lengths, (args.k + 1) * (steps + 4))
+                sd = SpecDecoder(llm, ControlledDrafter(ref, float(drafter.split("@")[1]), cfg.vocab_size), k=args.k)
             else:
                 head = MTPHead(cfg, W, mtp_w, dev, max_b + 1, max_len, block_size=64)
                 d = MTPDrafter(head)
@@ -70,7 +113,8 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--small", action="store_true")
     ap.add_argument("--batches", default="1,16,64")
-    ap.add_argument("--drafters", default="none,ngram,mtp")
+    ap.add_argument("--drafters", default="none,ngram,mtp",
+                    help="none, ngram, mtp and oracle@P (recorded greedy continuation, each token kept with prob P)")
     ap.add_argument("--k", type=int, default=3)
     ap.add_argument("--steps", type=int, default=16)
     ap.add_argument("--ctx-min", type=int, default=6144)
