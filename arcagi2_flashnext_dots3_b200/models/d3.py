@@ -13,9 +13,9 @@ dotsnote/engine/vllm_patch/vllm/models/dots3_note/nvidia/model.py:513):
     o[h] = o_lat[h] @ W_UV[h]^T, times sigmoid(g)     absorption back + gate
     h += o @ W_o^T ; x = rms(h, ln2) ; h += MoE(x) (sigmoid router + bias, 3/2-bit experts, shared expert)
 
-Every projection runs on the tcgen05 weight-dequant GEMM, the two per-head absorption products too (one grouped
-launch each, every head an "expert" of an fp16 weight set); the rest are the kernels of csrc/k_d3.cu and the FN
-MoE kernels.
+Every projection runs on the tcgen05 weight-dequant GEMM; the two per-head absorption products are batched GEMMs
+(cuBLAS by default, faster at decode batch than the grouped tcgen05 form available with FW_D3_ABSORB=grouped);
+the rest are the kernels of csrc/k_d3.cu and the FN MoE kernels.
 """
 from __future__ import annotations
 
@@ -89,9 +89,10 @@ class D3Model:
 
     def _absorb(self, x: torch.Tensor, p: dict, which: str) -> torch.Tensor:
         """Per-head latent absorption [H, T, k] -> [H, T, n]: q_lat = q_nope[h] @ uk[h] (which="uk") or
-        o[h] = o_lat[h] @ uv[h]^T (which="uv"). On the GPU one tcgen05 grouped GEMM over all heads (every head is
-        an expert of a fp16 weight set); on the CPU torch.bmm on the dense matrices."""
-        if not x.is_cuda:
+        o[h] = o_lat[h] @ uv[h]^T (which="uv"): a batched GEMM on the dense per-head matrices (cuBLAS on a GPU), or
+        with the grouped weight sets (FW_D3_ABSORB=grouped) one tcgen05 grouped GEMM over all heads, every head an
+        expert of an fp16 weight set."""
+        if not x.is_cuda or which + "_ws" not in p:
             return torch.bmm(x, p["uk"]) if which == "uk" else torch.bmm(x, p["uv"].transpose(1, 2))
         ws = p[which + "_ws"]
         H, T, K = x.shape

@@ -25,6 +25,8 @@ from ..ops import wgemm
 from .fn_weights import rank_pad
 
 GEMV_MOE = os.environ.get("FW_MOE_GEMV", "1") != "0"   # decode MoE on the CUDA-core grouped GEMV
+# the GEMV serves MoE calls with at most this many (token, expert) pairs per expert on average (above: tcgen05)
+GEMV_PAIRS_PER_EXPERT = float(os.environ.get("FW_MOE_GEMV_PAIRS", "4"))
 SIDE_STREAM = os.environ.get("FW_SIDE_STREAM", "1") != "0"  # shared expert concurrent with the routed experts
 
 
@@ -187,7 +189,7 @@ class FNModel:
                 ysh = self._mm(sact, p["sd"])
         ids, w = ops.moe_route(logits, E, cfg.top_k)
         P = T * cfg.top_k
-        gemv = x.is_cuda and GEMV_MOE and P <= 4 * E   # decode: a few tokens per expert -> CUDA-core GEMV
+        gemv = x.is_cuda and GEMV_MOE and P <= GEMV_PAIRS_PER_EXPERT * E   # decode-sized: CUDA-core GEMV
         n_tile = wgemm.GEMV_MAX_TOK if gemv else (wgemm.pick_n_tile(max(1, (2 * P) // E)) if x.is_cuda else 16)
         max_items = (P + n_tile - 1) // n_tile + E
         pair_pos, items, n_items = ops.moe_plan(ids, E, n_tile, max_items)
