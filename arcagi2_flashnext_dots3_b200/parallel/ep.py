@@ -44,7 +44,12 @@ class EPGroup:
         self.max_tokens = max_tokens
         self.cap = max_tokens * self.k            # pairs one source can send to one owner (worst case)
         # token tile of the expert GEMMs: average pairs per expert over the whole job
-        self.n_tile = n_tile or wgemm.pick_n_tile(max(1, (2 * world * self.cap) // cfg.n_experts))
+        # decode-sized exchanges (few pairs per local expert on average) run the experts on the int8 GEMV, whose
+        # plans are built with items of at most GEMV_MAX_TOK rows; larger ones on the tcgen05 grouped GEMM
+        pairs_per_expert = world * self.cap / cfg.n_experts
+        self.use_gemv = not n_tile and pairs_per_expert <= EP_GEMV_PAIRS and wgemm_gemv_ok(cfg)
+        self.n_tile = n_tile or (wgemm.GEMV_MAX_TOK if self.use_gemv else
+                                 wgemm.pick_n_tile(max(1, (2 * world * self.cap) // cfg.n_experts)))
         self.timeout_ns = timeout_ns or native.DEFAULT_TIMEOUT_NS * 4
         dev, W, H = self.device, world, self.H
         self.max_rows = W * self.cap
@@ -134,10 +139,16 @@ class EPGroup:
         C.ep_gather(self.flags, self.counts, self.meta, self.xrecv.view(-1, self.H), self.cap, self.world, self.e_loc,
                     self.epoch, self.ybuf_ptrs, self.n_tile, self.sorted_src, self.items, self.n_items, self.row_dst,
                     self.n_rows, self.xs, err, self.timeout_ns)
-        wgemm.grouped(self.xs, p["gu"], self.items, self.n_items, self.max_items, self.act, epi=wgemm.EPI_SILU_MUL,
-                      n_tile=self.n_tile)
-        wgemm.grouped(self.act, p["d"], self.items, self.n_items, self.max_items, self.yout, n_tile=self.n_tile,
-                      row_dst=self.row_dst)
+        if self.use_gemv:
+            wgemm.gemv_grouped(self.xs, p["gu"], self.items, self.n_items, self.max_items, self.act,
+                               epi=wgemm.EPI_SILU_MUL)
+            wgemm.gemv_grouped(self.act, p["d"], self.items, self.n_items, self.max_items, self.yout,
+                               row_dst=self.row_dst)
+        else:
+            wgemm.grouped(self.xs, p["gu"], self.items, self.n_items, self.max_items, self.act,
+                          epi=wgemm.EPI_SILU_MUL, n_tile=self.n_tile)
+            wgemm.grouped(self.act, p["d"], self.items, self.n_items, self.max_items, self.yout, n_tile=self.n_tile,
+                          row_dst=self.row_dst)
         C.ep_done(self.done_ptrs, self.rank, self.world, self.epoch)
 
     def _nccl_exchange(self, x, ids, w, p):
@@ -157,9 +168,13 @@ class EPGroup:
         pp, items, n_items = ops.moe_plan(lid, self.e_loc + 1, self.n_tile, self.max_items)
         n_loc = ((items[:, 0] < self.e_loc) & (self.item_idx < n_items)).sum().to(torch.int32).view(1)
         xs = ops.moe_scatter(self.xg, pp)
-        wgemm.grouped(xs, p["gu"], items, n_loc, self.max_items, self.act, epi=wgemm.EPI_SILU_MUL,
-                      n_tile=self.n_tile)
-        wgemm.grouped(self.act, p["d"], items, n_loc, self.max_items, self.yout, n_tile=self.n_tile)
+        if self.use_gemv and xs.is_cuda:
+            wgemm.gemv_grouped(xs, p["gu"], items, n_loc, self.max_items, self.act, epi=wgemm.EPI_SILU_MUL)
+            wgemm.gemv_grouped(self.act, p["d"], items, n_loc, self.max_items, self.yout)
+        else:
+            wgemm.grouped(xs, p["gu"], items, n_loc, self.max_items, self.act, epi=wgemm.EPI_SILU_MUL,
+                          n_tile=self.n_tile)
+            wgemm.grouped(self.act, p["d"], items, n_loc, self.max_items, self.yout, n_tile=self.n_tile)
         y = self.yout[pp.reshape(-1).long()].view(W * Tm, k, H)
         part = (torch.where(owned[..., None], y, 0.0) * self.wg[..., None]).sum(1)
         if part.is_cuda:
@@ -174,6 +189,15 @@ class EPGroup:
             dist.all_gather_into_tensor(out, inp, group=self.group)
         else:
             dist.all_gather(list(out.chunk(self.world)), inp, group=self.group)
+
+EP_GEMV_PAIRS = float(__import__("os").environ.get("FW_EP_GEMV_PAIRS", "8"))
+
+
+def wgemm_gemv_ok(cfg) -> bool:
+    """The int8 GEMV serves 2/3/4-bit experts only, and only when the decode-MoE GEMV is switched on."""
+    from ..models import fn as fn_model
+    return fn_model.GEMV_MOE and all(cfg.bits_of(e) <= 4 for e in range(cfg.n_experts))
+
 
 def shard_experts(ws: wgemm.WeightSet, lo: int, hi: int) -> wgemm.WeightSet:
     """Sub-WeightSet of experts [lo, hi) (experts are stored contiguously in order)."""
