@@ -156,6 +156,11 @@ class LLM:
             from ..utils.steplog import StepLog
             self.steplog = StepLog(os.environ["FW_STEPLOG"])
         self.stats = {"steps": 0, "tokens": 0, "prefill_tokens": 0}
+        if os.environ.get("FW_FLAG_LOG"):   # record which optional paths this engine runs with
+            import json
+            from ..utils.observe import flag_report
+            with open(os.environ["FW_FLAG_LOG"], "a") as f:
+                f.write(json.dumps({"engine": type(self.model).__name__, "flags": flag_report()}) + "\n")
 
     # ---------------------------------------------------------------------------------- admission
     def add(self, prompt, max_new_tokens: int = 64, prefill_chunk: int = 2048, sp: SamplingParams = None) -> Sequence:

@@ -197,3 +197,61 @@ class TopkOverlap:
         np.savez(path, pairs=np.array(keys, dtype=np.int64), bins=np.array(self.BINS, dtype=np.int64),
                  sum=np.stack([self.sum[k].numpy() for k in keys]) if keys else np.zeros((0, 6)),
                  cnt=np.stack([self.cnt[k].numpy() for k in keys]) if keys else np.zeros((0, 6)))
+
+
+# ------------------------------------------------------------------------------------------ runtime flags
+RUNTIME_FLAGS = {
+    "FW_MOE_GEMV": ("1", "decode MoE on the int8 grouped GEMV (0: tcgen05 grouped GEMM)"),
+    "FW_MOE_GEMV_PAIRS": ("4", "largest mean (token, expert) pairs per expert served by the GEMV"),
+    "FW_EP_GEMV_PAIRS": ("8", "same crossover under expert parallelism"),
+    "FW_SIDE_STREAM": ("1", "shared expert on a side stream concurrent with the routed experts"),
+    "FW_DENSE_PLAN": ("", "'old': dense GEMMs without the token-tile/split-K launch plan"),
+    "FW_MLA_CUDA_CORE": ("0", "D3 latent attention on the CUDA-core kernel instead of tcgen05"),
+    "FW_MLA_SPLITS": ("0", "fixed key-split count of the latent attention (0: automatic)"),
+    "FW_DSA_CUDA_CORE": ("0", "DSA indexer scores on the CUDA-core kernel instead of tcgen05"),
+    "FW_D3_ABSORB": ("bmm", "D3 per-head absorption: batched GEMM or 'grouped' tcgen05"),
+    "FW_WAIT_TIMEOUT_MS": ("", "bound of every in-kernel wait before it reports an error"),
+    "FW_STEPLOG": ("", "path of the binary per-step engine log"),
+}
+
+
+def flag_report(env=None) -> list:
+    """Every runtime switch with its effective value, whether it differs from the default, and what it does; the
+    engine logs this at start-up so a run records which optional paths were active."""
+    import os
+    env = os.environ if env is None else env
+    out = []
+    for name, (default, what) in RUNTIME_FLAGS.items():
+        val = env.get(name, default)
+        out.append({"flag": name, "value": val, "changed": name in env and env[name] != default, "what": what})
+    return out
+
+
+def reclaim(llm=None, keep_graphs: bool = True) -> dict:
+    """Give memory back: drop dense-copy caches of weight sets (test/oracle views), optionally the captured decode
+    graphs (their private pools), then release the caching allocator's free blocks. Returns bytes freed per kind
+    (the reference's mem_reclaim.py frees vLLM's unused workspaces the same way after start-up)."""
+    import gc
+    import torch
+    freed = {"dense_caches": 0, "graphs": 0, "allocator": 0}
+    if llm is not None:
+        def walk(x):
+            if hasattr(x, "_dense_cache") and x._dense_cache:
+                freed["dense_caches"] += sum(t.numel() * t.element_size() for t in x._dense_cache.values())
+                x._dense_cache = None
+            elif isinstance(x, dict):
+                for v in x.values():
+                    walk(v)
+            elif isinstance(x, (list, tuple)):
+                for v in x:
+                    walk(v)
+        walk(llm.model.W)
+        if not keep_graphs and getattr(llm, "graphs", None):
+            freed["graphs"] = len(llm.graphs)
+            llm.graphs.clear()
+    gc.collect()
+    if torch.cuda.is_available():
+        before = torch.cuda.memory_reserved()
+        torch.cuda.empty_cache()
+        freed["allocator"] = before - torch.cuda.memory_reserved()
+    return freed

@@ -148,3 +148,30 @@ def test_kd_training_reduces_kl(tmp_path):
              "--lr-router", "1e-3", "--lr-norms", "5e-2", "--warmup", "1"])
     log = [json.loads(l) for l in open(out / "log.jsonl")]
     assert len(log) == 6 and log[-1]["kl"] < log[0]["kl"], log
+
+
+def test_monitor_flags_spikes_nonfinite_and_trend(tmp_path):
+    from arcagi2_flashnext_dots3_b200.training import monitor
+    p = tmp_path / "log.jsonl"
+    rows = [{"step": i + 1, "kl": 1.0 + 0.05 * i, "grad_norm": 1.0} for i in range(40)]
+    rows[25]["grad_norm"] = 50.0
+    rows[30]["kl"] = float("nan")
+    p.write_text("\n".join(json.dumps(r) for r in rows) + "\n{\"step\": 41, \"kl\"")   # a half-written last line
+    s = monitor.summarize(monitor.read_log(p), window=10)
+    kinds = {(a["key"], a["kind"]) for a in s["anomalies"]}
+    assert s["steps"] == 40 and ("grad_norm", "spike") in kinds and ("kl", "non-finite") in kinds
+    assert ("kl", "trend") in kinds
+
+
+def test_flag_report_and_reclaim():
+    from arcagi2_flashnext_dots3_b200.utils import observe
+    rep = {r["flag"]: r for r in observe.flag_report({"FW_MOE_GEMV": "0"})}
+    assert rep["FW_MOE_GEMV"]["changed"] and rep["FW_MOE_GEMV"]["value"] == "0" and not rep["FW_SIDE_STREAM"]["changed"]
+    from arcagi2_flashnext_dots3_b200.config import EngineConfig
+    from arcagi2_flashnext_dots3_b200.engine.llm import LLM
+    cfg = fn_small_config(num_layers=2, ple_layers=())
+    llm = LLM(cfg, fn_weights.to_engine(fn_weights.random_dense(cfg, seed=0, symmetric=False), cfg, "cpu"), "cpu",
+              EngineConfig(max_seqs=2, max_model_len=64, block_size=16, graph_batch_sizes=(1,)))
+    llm.generate([[1, 2, 3]], max_new_tokens=2)          # CPU matmuls fill the dense-copy caches
+    freed = observe.reclaim(llm)
+    assert freed["dense_caches"] > 0
