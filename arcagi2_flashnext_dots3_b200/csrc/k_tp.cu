@@ -140,6 +140,193 @@ void tp_reduce(torch::Tensor buf, torch::Tensor flags, int64_t W, int64_t n, int
                                              err.data_ptr<int32_t>() + 1);
 }
 
+// ------------------------------------------------------------------------------------------------------------
+// Quantized two-shot all-reduce fused with the residual add: h[:n] += sum over ranks of x_r[:n].
+//
+// The n elements are cut into W chunks of `chunk` elements (a multiple of 128); rank c owns chunk c. Per group
+// of 128 elements a warp computes the absmax, scale = absmax / 127 and int8 codes round(x / scale). One launch,
+// three phases, CTA b handling the groups g = b, b + G, ... of every chunk:
+//   1. reduce-scatter: quantize the local partial; the codes and scale of chunk c's groups go into slot [me] of
+//      owner c's RS area; then flag rs[me][b] = epoch on owner c (system fence, st.release.sys);
+//   2. reduce: wait (bounded) for rs[s][b] >= epoch from every source s, dequantize and sum in rank order
+//      (deterministic), quantize the sum and store it into slot [me] of every rank's AG area; flag ag[me][b];
+//   3. gather: wait for ag[o][b] from every owner o, dequantize and add into h.
+// The owner reads back its own quantized sum like every other rank, so all ranks add identical values. Per rank
+// 2 (W - 1) / W bytes per element cross NVLink (plus 4 bytes of scale per 128), against 4 (W - 1) for the fp32
+// fan-out. Waits only ever involve CTAs with the same index on other GPUs, and the grid never exceeds one CTA per
+// SM, so every CTA a wait depends on is resident. Two parities (epoch & 1) make the areas reusable: a rank
+// writes parity p again two epochs later only after the owners' AG flags of the epoch in between, which they
+// set after their reads of parity p. A timed-out wait records 6410 + peer and raises the abort word; CTAs that
+// see it return.
+struct QArLayout {   // byte offsets inside one rank's symmetric area
+  int64_t rs_q, rs_s, ag_q, ag_s, flags;
+  int64_t chunk, groups;     // elements per chunk, 128-element groups per chunk
+};
+
+__device__ __forceinline__ float warp_absmax(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t pack_q8(float4 v, float inv) {
+  const int a = __float2int_rn(v.x * inv), b = __float2int_rn(v.y * inv), c = __float2int_rn(v.z * inv),
+            d = __float2int_rn(v.w * inv);
+  return (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) | ((uint32_t)(c & 0xff) << 16) | ((uint32_t)(d & 0xff) << 24);
+}
+
+__device__ __forceinline__ float4 unpack_q8(uint32_t q, float s) {
+  return make_float4((float)(int8_t)(q & 0xff) * s, (float)(int8_t)((q >> 8) & 0xff) * s,
+                     (float)(int8_t)((q >> 16) & 0xff) * s, (float)(int8_t)(q >> 24) * s);
+}
+
+// Bounded wait of one thread for flag >= e; false on timeout (error 6410 + peer) or abort.
+__device__ bool wait_epoch(const int64_t* flag, int64_t e, int peer, int* err, int* abort_word, uint64_t limit_ns) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    if (ld_acquire_sys(flag) >= e) return true;
+    if (*(volatile int*)abort_word) return false;
+    if ((it & 63) == 63) {
+      const uint64_t now = gtimer();
+      if (!t0) t0 = now;
+      else if (now - t0 > limit_ns) {
+        atomicCAS(err, 0, 6410 + peer);
+        *(volatile int*)abort_word = 1;
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(128) tp_qar_kernel(const float* __restrict__ x, float* __restrict__ h, int64_t n,
+                                                     const uint64_t* bases, int me, int W, QArLayout L,
+                                                     const int64_t* epoch, int* err, uint64_t limit_ns) {
+  __shared__ int ok;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = gridDim.x, b = blockIdx.x;
+  const int64_t e = epoch[0];
+  const int par = (int)(e & 1);
+  int* abort_word = err + 1;
+  char* mine = reinterpret_cast<char*>(bases[me]);
+  int64_t* my_flags = reinterpret_cast<int64_t*>(mine + L.flags);     // [2 par][2 phase][W][G]
+  auto flag_at = [&](char* base, int phase, int src) {
+    return reinterpret_cast<int64_t*>(base + L.flags) + (((int64_t)par * 2 + phase) * W + src) * G + b;
+  };
+  // ---- phase 1: quantize the partial, scatter each chunk's groups to its owner
+  for (int c = 0; c < W; ++c) {
+    char* peer = reinterpret_cast<char*>(bases[c]);
+    int8_t* q = reinterpret_cast<int8_t*>(peer + L.rs_q) + ((int64_t)par * W + me) * L.chunk;
+    float* sc = reinterpret_cast<float*>(peer + L.rs_s) + ((int64_t)par * W + me) * L.groups;
+    for (int64_t g = b + (int64_t)warp * G; g < L.groups; g += 4LL * G) {
+      const int64_t i0 = (int64_t)c * L.chunk + g * 128 + lane * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i0 + 3 < n) v = *reinterpret_cast<const float4*>(x + i0);
+      else if (i0 < n) { v.x = x[i0]; if (i0 + 1 < n) v.y = x[i0 + 1]; if (i0 + 2 < n) v.z = x[i0 + 2]; }
+      const float amax = warp_absmax(fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      const float s = amax > 0.f ? amax / 127.f : 1.f;
+      reinterpret_cast<uint32_t*>(q + g * 128)[lane] = pack_q8(v, 1.f / s);
+      if (lane == 0) sc[g] = s;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < W) st_release_sys(flag_at(reinterpret_cast<char*>(bases[threadIdx.x]), 0, me), e);
+  // ---- phase 2: reduce this rank's chunk
+  if (threadIdx.x == 0) {
+    ok = 1;
+    for (int s2 = 0; s2 < W && ok; ++s2) ok = wait_epoch(flag_at(mine, 0, s2), e, s2, err, abort_word, limit_ns);
+  }
+  __syncthreads();
+  if (!ok) return;
+  {
+    const int8_t* rq = reinterpret_cast<const int8_t*>(mine + L.rs_q) + (int64_t)par * W * L.chunk;
+    const float* rs = reinterpret_cast<const float*>(mine + L.rs_s) + (int64_t)par * W * L.groups;
+    for (int64_t g = b + (int64_t)warp * G; g < L.groups; g += 4LL * G) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int s2 = 0; s2 < W; ++s2) {
+        const uint32_t qq = reinterpret_cast<const uint32_t*>(rq + (int64_t)s2 * L.chunk + g * 128)[lane];
+        const float4 d = unpack_q8(qq, rs[(int64_t)s2 * L.groups + g]);
+        acc.x += d.x; acc.y += d.y; acc.z += d.z; acc.w += d.w;
+      }
+      const float amax = warp_absmax(fmaxf(fmaxf(fabsf(acc.x), fabsf(acc.y)), fmaxf(fabsf(acc.z), fabsf(acc.w))));
+      const float s = amax > 0.f ? amax / 127.f : 1.f;
+      const uint32_t packed = pack_q8(acc, 1.f / s);
+      for (int o = 0; o < W; ++o) {
+        char* peer = reinterpret_cast<char*>(bases[o]);
+        reinterpret_cast<uint32_t*>(reinterpret_cast<int8_t*>(peer + L.ag_q) + ((int64_t)par * W + me) * L.chunk +
+                                    g * 128)[lane] = packed;
+        if (lane == 0) reinterpret_cast<float*>(peer + L.ag_s)[((int64_t)par * W + me) * L.groups + g] = s;
+      }
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < W) st_release_sys(flag_at(reinterpret_cast<char*>(bases[threadIdx.x]), 1, me), e);
+  // ---- phase 3: gather every owner's reduced chunk into h
+  if (threadIdx.x == 0) {
+    ok = 1;
+    for (int o = 0; o < W && ok; ++o) ok = wait_epoch(flag_at(mine, 1, o), e, o, err, abort_word, limit_ns);
+  }
+  __syncthreads();
+  if (!ok) return;
+  const int8_t* aq = reinterpret_cast<const int8_t*>(mine + L.ag_q) + (int64_t)par * W * L.chunk;
+  const float* as = reinterpret_cast<const float*>(mine + L.ag_s) + (int64_t)par * W * L.groups;
+  for (int o = 0; o < W; ++o) {
+    for (int64_t g = b + (int64_t)warp * G; g < L.groups; g += 4LL * G) {
+      const int64_t i0 = (int64_t)o * L.chunk + g * 128 + lane * 4;
+      if (i0 >= n) continue;
+      const float4 d = unpack_q8(reinterpret_cast<const uint32_t*>(aq + (int64_t)o * L.chunk + g * 128)[lane],
+                                 as[(int64_t)o * L.groups + g]);
+      if (i0 + 3 < n) {
+        float4 t = *reinterpret_cast<float4*>(h + i0);
+        t.x += d.x; t.y += d.y; t.z += d.z; t.w += d.w;
+        *reinterpret_cast<float4*>(h + i0) = t;
+      } else {
+        h[i0] += d.x;
+        if (i0 + 1 < n) h[i0 + 1] += d.y;
+        if (i0 + 2 < n) h[i0 + 2] += d.z;
+      }
+    }
+  }
+}
+
+// Layout of one rank's quantized all-reduce area for up to n_max elements over W ranks and G CTAs.
+QArLayout qar_layout(int64_t n_max, int W, int G) {
+  QArLayout L;
+  L.chunk = ((n_max + W - 1) / W + 127) / 128 * 128;
+  L.groups = L.chunk / 128;
+  auto al = [](int64_t v) { return (v + 255) / 256 * 256; };
+  L.rs_q = 0;
+  L.rs_s = al(L.rs_q + 2LL * W * L.chunk);
+  L.ag_q = al(L.rs_s + 2LL * W * L.groups * 4);
+  L.ag_s = al(L.ag_q + 2LL * W * L.chunk);
+  L.flags = al(L.ag_s + 2LL * W * L.groups * 4);
+  return L;
+}
+
+int64_t tp_qar_bytes(int64_t n_max, int64_t W, int64_t G) {
+  const QArLayout L = qar_layout(n_max, (int)W, (int)G);
+  return L.flags + 2LL * 2 * W * G * 8;
+}
+
+void tp_qar(torch::Tensor x, torch::Tensor h, int64_t n, torch::Tensor bases, int64_t me, int64_t n_max, int64_t G,
+            torch::Tensor epoch, torch::Tensor err, int64_t timeout_ns) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kFloat && x.is_contiguous() && x.numel() >= n);
+  TORCH_CHECK(h.is_cuda() && h.scalar_type() == torch::kFloat && h.is_contiguous() && h.numel() >= n);
+  TORCH_CHECK(n <= n_max, "all-reduce larger than its area");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(h.data_ptr()) % 16 == 0);
+  const int W = bases.numel();
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  TORCH_CHECK(G >= 1 && G <= sms && W <= 128, "grid must be co-resident (at most one CTA per SM)");
+  const QArLayout L = qar_layout(n_max, W, (int)G);
+  tp_qar_kernel<<<(int)G, 128, 0, STREAM>>>(x.data_ptr<float>(), h.data_ptr<float>(), n,
+                                            reinterpret_cast<const uint64_t*>(bases.data_ptr<int64_t>()), (int)me, W,
+                                            L, epoch.data_ptr<int64_t>(), err.data_ptr<int32_t>(),
+                                            (uint64_t)timeout_ns);
+}
+
 }  // namespace
 
 void register_tp(pybind11::module& m) {
@@ -147,4 +334,6 @@ void register_tp(pybind11::module& m) {
   m.def("tp_push", &tp_push);
   m.def("tp_signal", &tp_signal);
   m.def("tp_reduce", &tp_reduce);
+  m.def("tp_qar", &tp_qar);
+  m.def("tp_qar_bytes", &tp_qar_bytes);
 }

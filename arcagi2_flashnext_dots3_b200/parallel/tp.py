@@ -6,7 +6,10 @@ The reference runs D3 with TP4 and replaces NCCL's all-reduce by a host-staged q
 (dotsnote/engine/arcstats_pkg/arcstats/host_ar.py; routed in arcstats/__init__.py:383-410). Here
 ``comm="fused"``: the o-projection GEMM stores its fp32 partial directly into every rank's symmetric buffer
 (wgemm fan-out epilogue), then csrc/k_tp.cu signals and reduces (bounded waits, deterministic rank order, the
-residual add fused into the reduce); the MoE partial is pushed the same way. ``comm="nccl"``: all_reduce.
+residual add fused into the reduce); the MoE partial is pushed the same way. ``comm="q8"``: one kernel
+(csrc/k_tp.cu ``tp_qar``) quantizes the partial to int8 per 128 elements, reduce-scatters it over peer memory,
+re-quantizes each owner's sum and all-gathers it into the residual (2 (W-1)/W bytes per element per rank instead
+of 4 (W-1)). ``comm="nccl"``: all_reduce.
 """
 from __future__ import annotations
 
@@ -51,12 +54,26 @@ class TPGroup:
             self.flags, self.flag_ptrs = alloc((2, W), torch.int64)
             torch.cuda.synchronize(self.device)
             dist.barrier(group=self.group)
+        elif comm == "q8":
+            if self.device.type == "cuda":
+                import torch.distributed._symmetric_memory as symm
+                sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+                groups = -(-self.slot // (world * 128))
+                self.qar_grid = max(1, min(sms, groups))
+                nbytes = native.C().tp_qar_bytes(self.slot, world, self.qar_grid)
+                self.qbuf = symm.empty(nbytes, dtype=torch.uint8, device=self.device)
+                self.qbuf.zero_()
+                hd = symm.rendezvous(self.qbuf, self.group)
+                self.qbases = torch.tensor([hd.get_buffer(r, (nbytes,), torch.uint8).data_ptr() for r in range(world)],
+                                           dtype=torch.int64, device=self.device)
+                torch.cuda.synchronize(self.device)
+                dist.barrier(group=self.group)
         elif comm != "nccl":
             raise ValueError(comm)
 
     # ------------------------------------------------------------------------------------ fused GEMM path
     def begin(self):
-        if self.comm == "fused":
+        if self.comm in ("fused", "q8"):
             native.C().tp_epoch(self.epoch)
 
     def fan(self):
@@ -76,6 +93,16 @@ class TPGroup:
         T = partial.shape[0]
         if T > self.max_tokens:
             raise ValueError(f"{T} rows > TP buffer capacity {self.max_tokens}")
+        if self.comm == "q8":
+            if not partial.is_cuda:   # CPU ranks: the same quantized arithmetic through gathered partials
+                parts = [torch.empty_like(partial) for _ in range(self.world)]
+                dist.all_gather(parts, partial.contiguous(), group=self.group)
+                h += qar_reference(parts)
+                return
+            self.begin()
+            native.C().tp_qar(partial.contiguous(), h, T * self.H, self.qbases, self.rank, self.slot, self.qar_grid,
+                              self.epoch, native.err_word(self.device), self.timeout_ns)
+            return
         if self.comm == "nccl" or not partial.is_cuda:
             dist.all_reduce(partial, group=self.group)
             h += partial
@@ -88,7 +115,7 @@ class TPGroup:
         """h += all-reduce(x16 @ W_rank^T) with the GEMM epilogue writing into the peers (fused path)."""
         from ..ops import wgemm
         T = x16.shape[0]
-        if self.comm == "nccl" or not x16.is_cuda:
+        if self.comm in ("nccl", "q8") or not x16.is_cuda:
             self.allreduce_add(h, model._mm(x16, ws))
             return
         if T > self.max_tokens:
@@ -97,6 +124,31 @@ class TPGroup:
         dummy = torch.empty(T, ws.rows, dtype=torch.float32, device=x16.device)
         wgemm.matmul(x16, ws, out=dummy, fan=self.fan())
         self.finish_into(h, T)
+
+
+def _q8(x: torch.Tensor):
+    """Per 128-element group: (codes, scale) with scale = absmax / 127 (1 for an all-zero group) and codes =
+    round-half-even(x * (1 / scale)); x is [groups, 128]."""
+    amax = x.abs().amax(-1, keepdim=True)
+    s = torch.where(amax > 0, amax / 127.0, torch.ones_like(amax))
+    return torch.round(x * (1.0 / s)), s
+
+
+def qar_reference(partials: list) -> torch.Tensor:
+    """The quantized two-shot all-reduce of csrc/k_tp.cu in torch (same chunking, rounding and summation order):
+    every rank's partial quantized per 128-element group, dequantized and summed in rank order per owner chunk,
+    the sum quantized again. Returns the fp32 sum every rank adds."""
+    W = len(partials)
+    shape, n = partials[0].shape, partials[0].numel()
+    chunk = ((n + W - 1) // W + 127) // 128 * 128
+    pad = W * chunk - n
+    xs = [torch.nn.functional.pad(p.reshape(-1).float(), (0, pad)).view(-1, 128) for p in partials]
+    acc = torch.zeros_like(xs[0])
+    for x in xs:                                  # rank order, as every owner sums its sources
+        q, s = _q8(x)
+        acc = acc + q * s
+    q, s = _q8(acc)
+    return (q * s).reshape(-1)[:n].view(shape)
 
 
 def vocab_range(V: int, rank: int, world: int):

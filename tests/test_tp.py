@@ -23,12 +23,17 @@ def test_tp_cpu_two_ranks():
     _run(2, "nccl", 29681, {"CUDA_VISIBLE_DEVICES": ""})
 
 
+def test_tp_cpu_two_ranks_quantized_allreduce():
+    """int8 two-shot all-reduce semantics on gloo ranks (the torch statement the GPU kernel is checked against)."""
+    _run(2, "q8", 29687, {"CUDA_VISIBLE_DEVICES": "", "TP_DEVICE": "cpu"})
+
+
 @pytest.mark.gpu
-@pytest.mark.parametrize("comm", ["fused", "nccl"])
+@pytest.mark.parametrize("comm", ["fused", "nccl", "q8"])
 def test_tp_two_gpus(comm):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    _run(2, comm, 29683 if comm == "fused" else 29685, {"NCCL_NVLS_ENABLE": "0", "TP_DEVICE": "cuda"})
+    _run(2, comm, {"fused": 29683, "nccl": 29685, "q8": 29689}[comm], {"NCCL_NVLS_ENABLE": "0", "TP_DEVICE": "cuda"})
 
 
 @pytest.mark.gpu
@@ -50,6 +55,28 @@ def test_tp_reduce_wait_times_out_with_error_code():
         native.check_error(dev)
     assert bool((h == 1).all())                    # nothing was added
     assert float(torch.ones(3, device=dev).sum()) == 3.0   # the context still works
+
+
+@pytest.mark.gpu
+def test_quantized_allreduce_wait_times_out_with_error_code():
+    """One launch of the int8 all-reduce as rank 0 of two, both ranks' areas on this GPU, rank 1 never running:
+    its reduce-scatter wait gives up, records 6410 + 1 and leaves the context usable."""
+    from arcagi2_flashnext_dots3_b200.ops import native
+    dev = torch.device("cuda")
+    W, n, G = 2, 4 * 256, 4
+    nbytes = native.C().tp_qar_bytes(n, W, G)
+    areas = [torch.zeros(nbytes, dtype=torch.uint8, device=dev) for _ in range(W)]
+    bases = torch.tensor([a.data_ptr() for a in areas], dtype=torch.int64, device=dev)
+    epoch = torch.ones(1, dtype=torch.int64, device=dev)
+    x = torch.randn(n, device=dev)
+    h = torch.ones(n, device=dev)
+    native.err_word(dev).zero_()
+    native.C().tp_qar(x, h, n, bases, 0, n, G, epoch, native.err_word(dev), 50_000_000)
+    torch.cuda.synchronize()
+    with pytest.raises(native.DeviceWaitTimeout, match="6411"):
+        native.check_error(dev)
+    assert bool((h == 1).all())
+    assert float(torch.ones(3, device=dev).sum()) == 3.0
 
 
 @pytest.mark.parametrize("nproc", [2, 3])

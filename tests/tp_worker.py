@@ -30,7 +30,7 @@ def run(model, ids, dev, hidden=False):
 def main():
     comm = sys.argv[1]
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
-    cuda = comm == "fused" or os.environ.get("TP_DEVICE") == "cuda"
+    cuda = comm in ("fused", "q8") and os.environ.get("TP_DEVICE") != "cpu" or os.environ.get("TP_DEVICE") == "cuda"
     if cuda:
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
     dev = torch.device("cuda", torch.cuda.current_device()) if cuda else torch.device("cpu")
@@ -49,7 +49,24 @@ def main():
         torch.cuda.synchronize()
         native.check_error(dev)
     err = (got - ref).abs().max() / ref.abs().max()
-    tol = 2e-2 if cuda else 1e-4
+    tol = 2e-2 if (cuda or comm == "q8") else 1e-4
+    if comm == "q8":
+        # the kernel's quantized all-reduce equals its torch statement on the gathered partials
+        from arcagi2_flashnext_dots3_b200.parallel.tp import qar_reference
+        g = torch.Generator().manual_seed(100 + rank)
+        part = (torch.randn(13, cfg.hidden_size, generator=g) * (1 + rank)).to(dev)
+        parts = [torch.empty_like(part) for _ in range(world)]
+        dist.all_gather(parts, part)
+        h = torch.full_like(part, 0.5)
+        tp.allreduce_add(h, part)
+        if cuda:
+            torch.cuda.synchronize()
+            native.check_error(dev)
+        want = qar_reference([p.cpu() for p in parts]) + 0.5
+        qerr = float((h.cpu() - want).abs().max() / want.abs().max())
+        exact_sum = sum(p.cpu() for p in parts) + 0.5
+        assert qerr < 1e-6, (rank, qerr)
+        assert float((h.cpu() - exact_sum).abs().max() / exact_sum.abs().max()) < 2e-2
     assert err < tol, (rank, float(err))
     if not cuda:
         # LM head split across the ranks too: the sharded greedy pick equals the argmax of the full logits
