@@ -191,11 +191,11 @@ class SpecDecoder:
                 drafter.head.caches.block_table.shape[0] <= llm.scratch:
             raise ValueError("the MTP head needs a cache slot for the engine's scratch slot (n_slots > max_seqs)")
 
-    def add(self, prompt, max_new_tokens: int = 64):
+    def add(self, prompt, max_new_tokens: int = 64, sp=None):
         llm = self.llm
         if isinstance(self.drafter, MTPDrafter):
             llm._keep_prefill_rows = True
-        seq = llm.add(prompt, max_new_tokens)
+        seq = llm.add(prompt, max_new_tokens, sp=sp)
         if isinstance(self.drafter, MTPDrafter):
             self.drafter.prefill(llm, seq, llm._prefill_rows, self.k)
             llm._keep_prefill_rows = False
@@ -239,11 +239,12 @@ class SpecDecoder:
         seqs = [s for s in llm.running.values() if not s.done]
         if not seqs:
             return {}
-        if any(s.sp.temperature > 0 for s in seqs):
-            raise ValueError("speculative decoding verifies greedy sequences only")
+        sampled = any(s.sp.temperature > 0 for s in seqs)
+        if any(s.sp.top_k or s.sp.top_p < 1.0 for s in seqs if s.sp.temperature > 0):
+            raise ValueError("speculative sampling supports full-vocabulary temperature sampling (no top-k / top-p)")
         dev = llm.device
         drafts = self.drafter.propose(llm, seqs, k)
-        if self.use_graph:
+        if self.use_graph and not sampled:
             y, accepted = self._graph_step(seqs, drafts)
             return self._advance(seqs, drafts, y, accepted)
         ids = [[s.out[-1]] + list(d) for s, d in zip(seqs, drafts)]
@@ -252,17 +253,38 @@ class SpecDecoder:
         sl = torch.tensor([s.slot for s in seqs], dtype=torch.int32, device=dev)
         pos = torch.tensor([s.pos for s in seqs], dtype=torch.int32, device=dev)
         x = llm.model.step(torch.tensor(ids, dtype=torch.int32, device=dev).view(-1), sl, pos, k1, verify=True)
-        y = greedy_ids(llm.model, x).view(len(seqs), k1).tolist()
-        accepted = []
-        for d, yy in zip(drafts, y):
-            a = 0
-            while a < k and d[a] == yy[a]:
-                a += 1
-            accepted.append(a)
+        if sampled:
+            accepted, nxt = self._sample_verify(seqs, x, drafts)
+            y = [list(d[:a]) + [t] + [0] * (k1 - a - 1) for d, a, t in zip(drafts, accepted, nxt)]
+        else:
+            y = greedy_ids(llm.model, x).view(len(seqs), k1).tolist()
+            accepted = []
+            for d, yy in zip(drafts, y):
+                a = 0
+                while a < k and d[a] == yy[a]:
+                    a += 1
+                accepted.append(a)
         llm.model.commit(torch.tensor([a + 1 for a in accepted], dtype=torch.int32, device=dev))
         res = self._advance(seqs, drafts, y, accepted)
         self.drafter.observe(llm, seqs, x, ids, accepted, k)
         return res
+
+    def _sample_verify(self, seqs, x, drafts):
+        """Rejection-sampling verification (ops.sampling.speculative_accept; the sharded form when the LM head is
+        split over a TP group). Emitted tokens follow the model's sampling distribution; greedy rows in the batch
+        verify by argmax as before."""
+        from ..ops import sampling
+        m, k1 = self.llm.model, self.k + 1
+        dr = torch.tensor([list(d) for d in drafts], dtype=torch.long).view(len(seqs), self.k)
+        temps = [s.sp.temperature for s in seqs]
+        seeds = [s.sp.seed for s in seqs]
+        steps = [len(s.out) for s in seqs]        # index of the first token this verify emits
+        if getattr(m, "vocab_sharded", False):
+            from ..parallel.tp import sharded_speculative_accept
+            lg = m._mm(x, m.W["lm_head"]).float().view(len(seqs), k1, -1)
+            return sharded_speculative_accept(lg, m.W["vocab_range"][0], dr, temps, seeds, steps, m.tp.group)
+        lg = m.logits(x).float().view(len(seqs), k1, -1)
+        return sampling.speculative_accept(lg, dr, temps, seeds, steps)
 
     def _advance(self, seqs, drafts, y, accepted) -> dict:
         llm, k = self.llm, self.k
@@ -282,8 +304,8 @@ class SpecDecoder:
         self.stats["accepted"] += sum(accepted)
         return res
 
-    def generate(self, prompts, max_new_tokens: int = 64) -> list:
-        seqs = [self.add(p, max_new_tokens) for p in prompts]
+    def generate(self, prompts, max_new_tokens: int = 64, sp=None) -> list:
+        seqs = [self.add(p, max_new_tokens, sp=sp) for p in prompts]
         while any(not s.done for s in seqs):
             self.step()
         outs = [s.out[: s.max_new] for s in seqs]

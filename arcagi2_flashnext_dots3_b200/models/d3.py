@@ -196,9 +196,19 @@ class D3Model:
         ones = torch.ones(T, 1, dtype=torch.float32, device=x.device)
         ops.moe_combine(h, ypair, pair_pos, w, ysh, torch.full((T,), float("inf"), device=x.device), ones)
 
-    def step(self, ids: torch.Tensor, slots: torch.Tensor, positions: torch.Tensor, n_tok: int = 1):
+    def step(self, ids: torch.Tensor, slots: torch.Tensor, positions: torch.Tensor, n_tok: int = 1,
+             verify: bool = False):
+        """Hidden states [T, H] after the final norm. ``verify`` (speculative verification) needs no special
+        handling: every cache of this model is position-indexed, so rejected positions are simply rewritten
+        when real tokens reach them, and :meth:`commit` has nothing to do."""
+        return self.step_from_h(self.W["embed"][ids.long()].float(), slots, positions, n_tok)
+
+    def commit(self, n_commit: torch.Tensor):
+        """Speculative commit: nothing to roll forward (no recurrent state)."""
+
+    def step_from_h(self, h: torch.Tensor, slots: torch.Tensor, positions: torch.Tensor, n_tok: int = 1):
         cfg, W = self.cfg, self.W
-        h = W["embed"][ids.long()].float()
+        h = h.float().contiguous()
         self._h = h
         y = None
         for l, L in enumerate(W["layers"]):

@@ -128,3 +128,85 @@ def params_tensors(sps: list, steps: list, device):
     st = torch.tensor(steps, dtype=torch.int64)
     out = [t, k, p, sd, st]
     return [x.pin_memory() for x in out] if pin else out
+
+
+# ------------------------------------------------------------------------------------ speculative verify
+ACCEPT_INDEX = -1     # RNG index of the acceptance draw (vocabulary indices are >= 0)
+
+
+def _row_candidates(lg: torch.Tensor, drafts: torch.Tensor, T: float, seed: int, step: int, v0: int = 0):
+    """Per verify position j of one sequence (lg [k1, Vl] logits of a vocabulary slice starting at global index
+    v0, drafts [k]): (max, sum of exp(l/T - max), logit of draft j or -inf, best Gumbel-max value, its global
+    index); position j's candidate excludes draft j, the last position excludes nothing. Greedy (T <= 0) uses
+    the raw logits with no noise and no probabilities."""
+    k1, Vl = lg.shape
+    k = k1 - 1
+    idx = torch.arange(v0, v0 + Vl, device=lg.device)
+    x = lg.float()
+    out = torch.empty(k1, 5, dtype=torch.float64, device=lg.device)
+    for j in range(k1):
+        d = int(drafts[j]) if j < k else -1
+        local_d = d - v0
+        own = 0 <= local_d < Vl
+        if T > 0:
+            z = x[j] / T
+            m = z.max()
+            out[j, 0] = m
+            out[j, 1] = torch.exp(z - m).sum()
+            out[j, 2] = z[local_d] if own else float("-inf")
+            key = z - torch.log(-torch.log(uniform_torch(seed, step + j, idx)))
+        else:
+            out[j, 0], out[j, 1] = 0.0, 1.0
+            out[j, 2] = x[j, local_d] if own else float("-inf")
+            key = x[j].clone()
+        if own:
+            key[local_d] = float("-inf")
+        best = int(key.argmax())
+        out[j, 3] = key[best]
+        out[j, 4] = v0 + best
+    return out
+
+
+def _decide(cands: torch.Tensor, drafts, T: float, seed: int, step: int, k: int):
+    """cands [shards, k1, 5] (shards in vocabulary order) -> (accepted drafts, next token)."""
+    m, s, ld = cands[..., 0], cands[..., 1], cands[..., 2]
+    for j in range(k):
+        if T > 0:
+            gm = m.max(0).values[j]
+            logz = gm + torch.log((s[:, j] * torch.exp(m[:, j] - gm)).sum())
+            p_d = float(torch.exp(ld.max(0).values[j] - logz))
+            u = float(uniform_torch(seed, step + j, torch.tensor([ACCEPT_INDEX]))[0])
+            ok = u < p_d
+        else:   # greedy: the draft must be the argmax (lowest index on ties)
+            best_other = cands[:, j, 3].max()
+            dl = float(ld[:, j].max())
+            ok = dl > best_other or (dl == best_other and int(drafts[j]) < _first_index(cands[:, j]))
+        if not ok:
+            return j, _first_index(cands[:, j])
+    return k, _first_index(cands[:, k])
+
+
+def _first_index(c: torch.Tensor) -> int:
+    """Global index of the largest candidate value over shards, lowest index among equal values."""
+    vals, ids = c[:, 3], c[:, 4]
+    top = vals.max()
+    return int(ids[vals == top].min())
+
+
+def speculative_accept(logits: torch.Tensor, drafts: torch.Tensor, temps, seeds, steps):
+    """Speculative verification of point-mass drafts, per sequence b: logits [B, k + 1, V], drafts [B, k],
+    temps / seeds / steps per sequence (step = index of the first token this verify emits). Draft j is accepted
+    with probability p_j(d_j) (p_j = softmax(logits[b, j] / T)), drawn from the counter RNG at (seed, step + j,
+    index -1); at the first rejection the token comes from p_j with d_j removed (renormalized), by Gumbel-max
+    with the noise at (seed, step + j, token index); with every draft accepted a bonus token comes from p_k. The
+    emitted tokens are distributed as sampling from the model. Greedy rows (T <= 0): accept while the draft is
+    the argmax; the next token is the argmax. Returns (accepted [B] int, next [B] int) as lists."""
+    B, k1, V = logits.shape
+    acc, nxt = [], []
+    for b in range(B):
+        T, sd, st = float(temps[b]), int(seeds[b]), int(steps[b])
+        c = _row_candidates(logits[b], drafts[b], T, sd, st)
+        a, t = _decide(c[None], drafts[b], T, sd, st, k1 - 1)
+        acc.append(a)
+        nxt.append(t)
+    return acc, nxt

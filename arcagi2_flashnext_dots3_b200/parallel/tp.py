@@ -151,6 +151,29 @@ def qar_reference(partials: list) -> torch.Tensor:
     return (q * s).reshape(-1)[:n].view(shape)
 
 
+def sharded_speculative_accept(local_logits: torch.Tensor, v0: int, drafts, temps, seeds, steps, group=None):
+    """:func:`..ops.sampling.speculative_accept` with the LM head split over the TP group: every rank reduces
+    its vocabulary slice to five numbers per (sequence, verify position): its max and exp-sum at the temperature,
+    the draft's logit when it owns the draft, and its best Gumbel-max candidate (value, global index) excluding
+    the draft. One all-gather of [world, B, k + 1, 5] replaces gathering the logits (the reference's
+    shard_sample.py:67-119 likewise exchanges a few floats per row); every rank then decides the same accepted
+    count and next token, equal to the unsharded result."""
+    from ..ops.sampling import _decide, _row_candidates
+    B, k1, _ = local_logits.shape
+    mine = torch.stack([_row_candidates(local_logits[b], drafts[b], float(temps[b]), int(seeds[b]), int(steps[b]),
+                                        v0) for b in range(B)])          # [B, k1, 5]
+    world = dist.get_world_size(group)
+    parts = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(parts, mine.contiguous(), group=group)
+    allc = torch.stack(parts)                                           # [W, B, k1, 5], ranks in vocab order
+    acc, nxt = [], []
+    for b in range(B):
+        a, t = _decide(allc[:, b].cpu(), drafts[b], float(temps[b]), int(seeds[b]), int(steps[b]), k1 - 1)
+        acc.append(a)
+        nxt.append(t)
+    return acc, nxt
+
+
 def vocab_range(V: int, rank: int, world: int):
     """[v0, v1) of the vocabulary whose LM-head rows this rank holds when the head is split over the TP group."""
     return rank * V // world, (rank + 1) * V // world

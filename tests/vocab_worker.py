@@ -24,6 +24,20 @@ def main():
         got = sharded_pick(logits[:, v0:v1], v0, temperature=temp, seed=seed, step=step)
         want = [sampling._sample_row(logits[r], temp, 0, 1.0, seed, step) for r in range(T)]
         assert got.tolist() == want, (got.tolist(), want)
+    # speculative verification over the split head: same accepted counts and next tokens as unsharded
+    from arcagi2_flashnext_dots3_b200.parallel.tp import sharded_speculative_accept
+    B, k = 5, 3
+    lg = torch.randn(B, k + 1, V, generator=torch.Generator().manual_seed(2)) * 2
+    drafts = lg[:, :k].argmax(-1)
+    drafts[1, 1] = (drafts[1, 1] + 7) % V            # a greedy row rejected at position 1
+    drafts[3, 0] = 900                               # a draft owned by the last rank
+    temps, seeds, steps = [0.0, 0.0, 0.9, 1.2, 0.5], [1, 2, 3, 4, 5], [0, 4, 9, 2, 30]
+    want = sampling.speculative_accept(lg, drafts, temps, seeds, steps)
+    got = sharded_speculative_accept(lg[..., v0:v1].contiguous(), v0, drafts, temps, seeds, steps)
+    assert got == want, (got, want)
+    acc, nxt = want
+    assert acc[0] == k and nxt[0] == int(lg[0, k].argmax())        # greedy row, every draft accepted + bonus
+    assert acc[1] == 1 and nxt[1] == int(lg[1, 1].argmax())        # greedy row, rejected at position 1
     dist.barrier()
     if rank == 0:
         print("VOCAB_OK", world)
