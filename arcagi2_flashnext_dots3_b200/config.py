@@ -143,6 +143,7 @@ class D3Config:
     eos_token_id: int = 1
     dsa_pattern: str = "FFSFSFSFSFFSF"   # index-share pattern over the DSA layers (used when index_share is on)
     index_share: bool = False            # DSA layers marked 'S' reuse the top-k of the latest 'F' layer
+    shard_index: bool = False            # under TP: rank r keeps the index keys of positions = r (mod TP size)
     dsa_every: int = 0                   # 0: DSA layers spread evenly (13 of 46)
     n_dsa_layers: int = 13
     index_heads: int = 64

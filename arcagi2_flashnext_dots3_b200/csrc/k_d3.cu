@@ -143,8 +143,9 @@ struct PrepArgs {
   __nv_fp8_e4m3* cache;             // [n_blocks, bs, kvr + dr]
   const int* block_table;
   int max_blocks, bs;
-  void* idx_cache;                  // [S, max_len, iD] (bf16 or fp32)
+  void* idx_cache;                  // [S, max_len / idx_stride, iD] (bf16 or fp32)
   int idx_bf16, idx_max_len;
+  int idx_stride, idx_off;          // sharded index: this rank stores positions p = idx_off (mod idx_stride)
   const int *slots, *positions;
   int n_tok;
   __half* qc_out;                   // [T, qr]
@@ -198,8 +199,9 @@ __global__ void __launch_bounds__(256) mla_prep_kernel(PrepArgs a) {
   const float inv = rsqrtf(bsum(s2, red) / a.iD + 1e-6f);
   for (int i = threadIdx.x; i < a.iD; i += blockDim.x) ikb[i] = (ik[i] - mean) * inv * a.ik_w[i] + a.ik_b[i];
   __syncthreads();
-  const int64_t ibase = ((int64_t)slot * a.idx_max_len + pos) * a.iD;
-  for (int i = threadIdx.x; i < a.iD; i += blockDim.x) {
+  const bool keep_key = pos >= a.idx_off && (pos - a.idx_off) % a.idx_stride == 0;
+  const int64_t ibase = ((int64_t)slot * a.idx_max_len + (pos - a.idx_off) / a.idx_stride) * a.iD;
+  for (int i = threadIdx.x; i < a.iD && keep_key; i += blockDim.x) {
     float v = ikb[i];
     if (i < a.dr) {
       const int p2 = i >> 1;
@@ -570,12 +572,15 @@ void d3_mla_prep(torch::Tensor P, std::vector<int64_t> dims, std::vector<int64_t
                  torch::Tensor block_table, c10::optional<torch::Tensor> idx_cache, torch::Tensor slots,
                  torch::Tensor positions, int64_t n_tok, torch::Tensor qc_out, torch::Tensor gate_out,
                  c10::optional<torch::Tensor> iw_out) {
-  CK(dims.size() == 6 && offs.size() == 3 && scal.size() == 3);
+  CK(dims.size() == 6 && (offs.size() == 3 || offs.size() == 5) && scal.size() == 3);
   PrepArgs a{};
   a.P = P.data_ptr<float>();
   a.ldP = P.size(1);
   a.qr = dims[0]; a.kvr = dims[1]; a.dr = dims[2]; a.H = dims[3]; a.iD = dims[4]; a.iH = dims[5];
   a.off_g = offs[0]; a.off_ik = offs[1]; a.off_iw = offs[2];
+  a.idx_stride = offs.size() == 5 ? (int)offs[3] : 1;
+  a.idx_off = offs.size() == 5 ? (int)offs[4] : 0;
+  CK(a.idx_stride >= 1 && a.idx_off >= 0 && a.idx_off < a.idx_stride);
   CK(a.dr <= 256 && a.dr % 2 == 0 && a.iD <= 512);
   CK(cache.scalar_type() == at::kFloat8_e4m3fn && cache.size(2) == a.kvr + a.dr);
   CK(rope.size(1) == a.dr / 2 && rope.size(2) == 2);

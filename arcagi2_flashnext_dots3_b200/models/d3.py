@@ -38,19 +38,24 @@ class D3Caches:
     max_len: int
 
 
+INDEX_SLACK = 4096   # rows past a sharded index cache's end that prefill chunks of up to this many tokens may read
+
+
 def allocate_caches(cfg, device, n_slots: int, max_len: int, block_size: int = 64, n_blocks: int = None,
-                    kv_dtype: str = "fp8", state_dtype: str = "bf16") -> D3Caches:
+                    kv_dtype: str = "fp8", state_dtype: str = "bf16", index_shards: int = 1) -> D3Caches:
+    """``index_shards`` > 1: the DSA index caches hold one TP rank's share of the positions (p = rank mod W)."""
     dev = torch.device(device)
     cpu = dev.type == "cpu"
     max_blocks = (max_len + block_size - 1) // block_size
     n_blocks = n_blocks or n_slots * max_blocks
+    idx_len = max_len if index_shards == 1 else -(-max_len // index_shards) + INDEX_SLACK
     latent, idx = [], []
     for l in range(cfg.num_layers):
         D = cfg.latent_of(l) + cfg.qk_rope_dim
         latent.append(torch.zeros(n_blocks, block_size, D, dtype=torch.float32 if cpu else torch.float8_e4m3fn,
                                   device=dev))
         own_index = cfg.layer_kind(l) == "dsa" and l not in cfg.shared_index_layers()
-        idx.append(torch.zeros(n_slots, max_len, cfg.index_dim, dtype=torch.float32 if cpu else torch.bfloat16,
+        idx.append(torch.zeros(n_slots, idx_len, cfg.index_dim, dtype=torch.float32 if cpu else torch.bfloat16,
                                device=dev) if own_index else None)
     return D3Caches(latent, idx, torch.zeros(n_slots, max_blocks, dtype=torch.int32, device=dev), block_size,
                     n_blocks, max_len)
@@ -70,6 +75,7 @@ class D3Model:
         self.rope = d3.rope_table(caches.max_len + 8, cfg.qk_rope_dim, cfg.rope_theta, self.device)
         self.scale = (cfg.qk_nope_dim + cfg.qk_rope_dim) ** -0.5
         self.shared_index = cfg.shared_index_layers()
+        self.index_shard = (tp.world, tp.rank) if (tp is not None and cfg.shard_index) else (1, 0)
         self.overlap = None     # utils.observe.TopkOverlap: per-step top-k overlap between DSA layers (eval only)
 
     def _mm(self, x, ws, epi=wgemm.EPI_STORE, out_dtype=torch.float32):
@@ -110,13 +116,17 @@ class D3Model:
         P = self._mm(x, p["a"])
         shared = l in self.shared_index
         qc, gate, iw = d3.mla_prep(P, cfg, l, p, self.rope, c.latent[l], c.block_table, c.idx[l], slots, positions,
-                                   n_tok, index=not shared)
+                                   n_tok, index=not shared, index_shard=self.index_shard)
         Q = self._mm(qc, p["qb"])
         q_nope, q_pe, iq = d3.mla_qsplit(Q, cfg, l, self.rope, positions, n_tok)
         q_lat = self._absorb(q_nope, p, "uk")                   # [H, T, kvr]
         if cfg.layer_kind(l) == "dsa":
             if shared:     # index sharing: the latest indexing layer's selection, no scoring of our own
                 sel = self._sel
+            elif self.index_shard[0] > 1:
+                sel = d3.dsa_select_sharded(iq, iw, c.idx[l], slots, positions, n_tok, cfg.index_topk,
+                                            self.index_shard[1], self.index_shard[0], self.tp.group)
+                self._sel = sel
             else:
                 sel = d3.dsa_select(iq, iw, c.idx[l], slots, positions, n_tok, cfg.index_topk, c.max_len)
                 self._sel = sel

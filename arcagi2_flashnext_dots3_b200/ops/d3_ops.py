@@ -54,9 +54,11 @@ def add_rms(h, y, w, eps, out_dtype=torch.float16):
     return out
 
 
-def mla_prep(P, cfg, l, p, rope, cache, block_table, idx_cache, slots, positions, n_tok, index: bool = True):
+def mla_prep(P, cfg, l, p, rope, cache, block_table, idx_cache, slots, positions, n_tok, index: bool = True,
+             index_shard=(1, 0)):
     """Returns (qc [T, qr] act, gate logits [T, H], index weights [T, iH] or None); writes the cache rows.
-    ``index=False`` (a DSA layer that shares another layer's top-k) skips the index key and weights."""
+    ``index=False`` (a DSA layer that shares another layer's top-k) skips the index key and weights.
+    ``index_shard=(W, r)``: the index cache holds only positions p = r (mod W), position p at row (p - r) / W."""
     T = P.shape[0]
     qr, kvr, dr, H = cfg.q_lora_rank, cfg.latent_of(l), cfg.qk_rope_dim, cfg.heads_of(l)
     dsa = cfg.layer_kind(l) == "dsa" and index
@@ -70,7 +72,8 @@ def mla_prep(P, cfg, l, p, rope, cache, block_table, idx_cache, slots, positions
         qc = torch.empty(T, qr, dtype=torch.float16, device=dev)
         gate = torch.empty(T, H, dtype=torch.float32, device=dev)
         iw = torch.empty(T, iH, dtype=torch.float32, device=dev) if dsa else None
-        native.C().d3_mla_prep(P, [qr, kvr, dr, H, iD, iH], [off_g, off_ik, off_iw], p["q_ln"], p["kv_ln"], p["kr_ln"],
+        offs = [off_g, off_ik, off_iw] + ([index_shard[0], index_shard[1]] if index_shard[0] > 1 else [])
+        native.C().d3_mla_prep(P, [qr, kvr, dr, H, iD, iH], offs, p["q_ln"], p["kv_ln"], p["kr_ln"],
                                p.get("ik_w"), p.get("ik_b"), [qs, kvs, cfg.rms_eps], rope, cache, block_table,
                                idx_cache, slots, positions, n_tok, qc, gate, iw)
         return qc, gate, iw
@@ -89,7 +92,9 @@ def mla_prep(P, cfg, l, p, rope, cache, block_table, idx_cache, slots, positions
     if dsa:
         ik = F.layer_norm(P[:, off_ik:off_ik + iD], (iD,), p["ik_w"], p["ik_b"], 1e-6)
         ik = torch.cat([_rope_inter(ik[:, None, :dr], cs)[:, 0], ik[:, dr:]], -1)
-        idx_cache[sl, pos] = ik.to(idx_cache.dtype)
+        Wsh, r = index_shard
+        keep = ((pos - r) % Wsh == 0) & (pos >= r)
+        idx_cache[sl[keep], (pos[keep] - r) // Wsh] = ik[keep].to(idx_cache.dtype)
         iw = P[:, off_iw:off_iw + iH] * iD ** -0.5 * iH ** -0.5
     return qc, gate, iw
 
@@ -149,6 +154,71 @@ def dsa_select(iq, iw, idx_cache, slots, positions, n_tok, topk: int, max_len: i
         s = (torch.relu(torch.einsum("hd,kd->hk", iq[t], k)) * iw[t][:, None]).sum(0)
         sel[t] = torch.sort(s, descending=True, stable=True).indices[:topk].to(torch.int32)
     return sel
+
+
+def dsa_select_sharded(iq, iw, idx_cache, slots, positions, n_tok, topk: int, rank: int, world: int, group=None):
+    """:func:`dsa_select` with the index keys sharded over a TP group by position mod world (the reference's
+    shard_indexer.py:1-15, 42-145 with the local select / all-gather / merge of topk_select.cu:77, 204): this rank
+    scores only its own keys (position p = rank + world * i at row i), takes its local top-k (lowest position
+    first among equal scores), all-gathers (score, position) candidates and merges them into the global top-k by
+    (score descending, position ascending). Each rank's share of the global top-k is inside its local top-k, so
+    the merge selects the same key set as the unsharded indexer."""
+    import torch.distributed as dist
+    T = iq.shape[0]
+    dev = iq.device
+    pos = _pos(positions, n_tok).long()
+    n_loc = torch.where(pos >= rank, (pos - rank) // world + 1, torch.zeros_like(pos))
+    if _cuda(iq):
+        L = idx_cache.shape[1]
+        ld = (L + 255) // 256 * 256
+        scores = torch.full((T, ld), float("-inf"), dtype=torch.float32, device=dev)
+        # every row of a sequence scores up to the sequence's last local key plus its row offset (masked below);
+        # the local cache keeps n_tok rows of slack past max_len / world for these reads
+        last = n_loc.view(-1, n_tok)[:, -1] - 1                 # last local key of each sequence
+        p_kern = last.clamp_min(0).to(torch.int32)              # row j scores local keys <= last + j
+        C = native.C()
+        if (not _DSA_CUDA_CORE and idx_cache.dtype == torch.bfloat16
+                and C.d3_dsa_tc_supported(iq.shape[1], iq.shape[2])):
+            C.d3_dsa_scores_tc(iq, iw, idx_cache, slots, p_kern, n_tok, scores, native.err_word(dev),
+                               native.DEFAULT_TIMEOUT_NS)
+        else:
+            C.d3_dsa_scores(iq, iw, idx_cache, slots, p_kern, n_tok, scores)
+        loc = torch.empty(T, topk, dtype=torch.int32, device=dev)
+        C.topk_rows(scores, n_loc.to(torch.int32), topk, loc)
+    else:
+        sl = slots.long().repeat_interleave(n_tok)
+        scores = torch.full((T, max(1, int(n_loc.max()))), float("-inf"))
+        for t in range(T):
+            n = int(n_loc[t])
+            if n:
+                k = idx_cache[sl[t], :n].float()
+                scores[t, :n] = (torch.relu(torch.einsum("hd,kd->hk", iq[t], k)) * iw[t][:, None]).sum(0)
+        loc = torch.full((T, topk), -1, dtype=torch.int32)
+        for t in range(T):
+            n = int(n_loc[t])
+            if n > topk:
+                loc[t] = torch.sort(scores[t, :n], descending=True, stable=True).indices[:topk].to(torch.int32)
+    # rows with at most topk local keys: every local key is a candidate
+    ar = torch.arange(topk, device=dev)[None, :]
+    all_local = (loc[:, :1] < 0)
+    loc = torch.where(all_local, torch.where(ar < n_loc[:, None], ar, -1).to(torch.int32), loc)
+    valid = loc >= 0
+    cand_s = torch.where(valid, scores.gather(1, loc.clamp_min(0).long()), torch.full_like(loc, float("-inf"),
+                                                                                          dtype=torch.float32))
+    cand_p = torch.where(valid, rank + world * loc.long(), torch.full_like(loc, -1, dtype=torch.long))
+    pack = torch.stack([cand_s, cand_p.float()], -1).contiguous()            # positions < 2^24: exact in fp32
+    parts = [torch.empty_like(pack) for _ in range(world)]
+    dist.all_gather(parts, pack, group=group)
+    allc = torch.cat(parts, 1)                                               # [T, world * topk, 2]
+    s_all, p_all = allc[..., 0], allc[..., 1]
+    p_key = torch.where(p_all < 0, torch.full_like(p_all, float(1 << 30)), p_all)
+    o1 = torch.sort(p_key, dim=1, stable=True).indices                       # position ascending
+    s1 = s_all.gather(1, o1)
+    o2 = torch.sort(s1, dim=1, descending=True, stable=True).indices         # then score descending
+    order = o1.gather(1, o2)
+    sel = p_all.gather(1, order[:, :topk]).to(torch.int32)
+    dense = (pos + 1 <= topk)[:, None]                                       # short rows attend to every key
+    return torch.where(dense, torch.full_like(sel, -1), sel)
 
 
 _MLA_CUDA_CORE = os.environ.get("FW_MLA_CUDA_CORE", "0") == "1"   # force the CUDA-core latent attention

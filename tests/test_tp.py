@@ -23,6 +23,11 @@ def test_tp_cpu_two_ranks():
     _run(2, "nccl", 29681, {"CUDA_VISIBLE_DEVICES": ""})
 
 
+def test_tp_cpu_two_ranks_sharded_index():
+    """DSA index keys sharded by position mod 2: local select, all-gather, merge equals the replicated indexer."""
+    _run(2, "nccl", 29695, {"CUDA_VISIBLE_DEVICES": "", "TP_SHARD_INDEX": "1"})
+
+
 def test_tp_cpu_two_ranks_quantized_allreduce():
     """int8 two-shot all-reduce semantics on gloo ranks (the torch statement the GPU kernel is checked against)."""
     _run(2, "q8", 29687, {"CUDA_VISIBLE_DEVICES": "", "TP_DEVICE": "cpu"})
@@ -33,7 +38,8 @@ def test_tp_cpu_two_ranks_quantized_allreduce():
 def test_tp_two_gpus(comm):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    _run(2, comm, {"fused": 29683, "nccl": 29685, "q8": 29689}[comm], {"NCCL_NVLS_ENABLE": "0", "TP_DEVICE": "cuda"})
+    _run(2, comm, {"fused": 29683, "nccl": 29685, "q8": 29689}[comm],
+         {"NCCL_NVLS_ENABLE": "0", "TP_DEVICE": "cuda", "TP_SHARD_INDEX": "1" if comm == "fused" else "0"})
 
 
 @pytest.mark.gpu

@@ -68,6 +68,18 @@ def main():
         assert qerr < 1e-6, (rank, qerr)
         assert float((h.cpu() - exact_sum).abs().max() / exact_sum.abs().max()) < 2e-2
     assert err < tol, (rank, float(err))
+    if os.environ.get("TP_SHARD_INDEX") == "1":
+        # index keys sharded by position mod world: same selection, same logits as the unsharded TP model
+        import dataclasses
+        lcs = dataclasses.replace(lc, shard_index=True)
+        m3 = D3Model(lcs, to_engine(shard_d3_weights(W, cfg, rank, world), lcs, dev),
+                     allocate_caches(lcs, dev, 2, 64, block_size=16, index_shards=world), dev, tp=tp)
+        got3 = run(m3, ids, dev)
+        if cuda:
+            torch.cuda.synchronize()
+            native.check_error(dev)
+        err3 = float((got3 - got).abs().max() / got.abs().max())
+        assert err3 < (2e-2 if cuda else 1e-5), (rank, err3)
     if not cuda:
         # LM head split across the ranks too: the sharded greedy pick equals the argmax of the full logits
         m2 = D3Model(lc, to_engine(shard_d3_weights(W, cfg, rank, world, shard_vocab=True), lc, dev),
