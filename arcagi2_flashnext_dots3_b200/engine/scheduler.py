@@ -52,6 +52,7 @@ class Request:
     resumed: bool = False      # rebuilt after preemption: its newest token is pending, nothing to sample
     holds_slot: bool = False   # slot and blocks still allocated (a kept session being pushed)
     evicted: bool = False      # an idle session whose KV was dropped
+    offloaded: bool = False    # an idle session whose KV waits in the host tier
     closed: bool = False
     done: bool = False
     t_submit: float = 0.0
@@ -70,6 +71,8 @@ class SchedulerStats:
     admitted: int = 0
     preempted: int = 0
     evicted_sessions: int = 0
+    offloaded_sessions: int = 0
+    restored_sessions: int = 0
     prefill_tokens: int = 0
     decode_steps: int = 0
     generated: int = 0
@@ -79,8 +82,10 @@ class SchedulerStats:
 
 class Scheduler:
     def __init__(self, llm, prefill_budget: int = 4096, chunk: int = 2048, watermark: int = None,
-                 evict_idle=None):
+                 evict_idle=None, host_tier=None):
+        """``host_tier``: an :class:`.kv_tier.HostKVTier`; idle sessions are offloaded there before being dropped."""
         self.llm = llm
+        self.host_tier = host_tier
         self.prefill_budget, self.chunk = prefill_budget, chunk
         self.bs = llm.ec.block_size
         # free blocks kept for the running sequences' next decode blocks
@@ -136,7 +141,9 @@ class Scheduler:
         r.done, r.resumed = False, False
         if r in self.idle:
             self.idle.remove(r)
-        if r.evicted:
+        if r.offloaded:
+            r.fed, r.base, r.holds_slot = tokens, held, False
+        elif r.evicted:
             r.fed, r.base, r.holds_slot = r.history + tokens, 0, False
         else:
             r.fed, r.base, r.holds_slot = tokens, held, True
@@ -157,6 +164,9 @@ class Scheduler:
             self.waiting.remove(r)
         if r.seq is not None and r.holds_slot:
             self._release(r)
+        if r.offloaded and self.host_tier is not None:
+            self.host_tier.drop(r.rid)
+            r.offloaded = False
 
     def _release(self, r: Request):
         llm = self.llm
@@ -170,6 +180,15 @@ class Scheduler:
         if not self.idle:
             return False
         r = self.idle.pop(0)
+        if self.host_tier is not None and self.host_tier.offload(r.rid, r.seq.slot):
+            llm = self.llm                   # blocks went to the host tier; the slot is free for others
+            llm.running.pop(r.seq.slot, None)
+            llm.model.reset_slot(r.seq.slot)
+            llm.free_slots.append(r.seq.slot)
+            r.holds_slot = False
+            r.offloaded = True
+            self.stats.offloaded_sessions += 1
+            return True
         self._release(r)
         r.evicted = True
         self.stats.evicted_sessions += 1
@@ -202,7 +221,12 @@ class Scheduler:
                     r.seq = Sequence(slot, list(r.prompt), r.max_new, sp=r.sp)
                 else:
                     r.seq.slot = slot
-                r.base = 0
+                if r.offloaded:              # KV and state come back from the host tier; prefill only the push
+                    self.host_tier.restore(r.rid, slot)
+                    r.offloaded = False
+                    self.stats.restored_sessions += 1
+                else:
+                    r.base = 0
                 r.holds_slot = True
                 r.evicted = False
             llm.model.assign_blocks(r.seq.slot, r.base + len(r.fed) + 1, llm.alloc)

@@ -97,3 +97,27 @@ def test_sessions_keep_kv_extend_and_exact_eviction_resume():
     assert st_ev.evicted_sessions >= 1 and st_kept.evicted_sessions == 0
     assert out_ev == out_kept and hist_ev == hist_kept
     assert pf_kept == len(PROMPTS[1]) + 6        # the push prefilled only the pushed tokens
+
+
+def test_idle_session_offload_to_host_tier_resumes_without_recompute():
+    """With a host tier, the idle session squeezed out of the KV pool is offloaded instead of dropped: its next
+    push restores blocks and recurrent state and prefills only the pushed tokens, with the same output."""
+    from arcagi2_flashnext_dots3_b200.engine.kv_tier import HostKVTier
+
+    def run(kv_blocks, squeeze, tier_blocks):
+        llm = _llm(kv_blocks=kv_blocks)
+        sch = Scheduler(llm, prefill_budget=64, chunk=16, watermark=0,
+                        host_tier=HostKVTier(llm, tier_blocks) if tier_blocks else None)
+        a = sch.submit(PROMPTS[1], 6, keep_kv=True)
+        sch.run([a])
+        if squeeze:
+            sch.generate([PROMPTS[3]], max_new_tokens=30)
+        pf0 = sch.stats.prefill_tokens
+        sch.extend(a, [a.out[-1]] + PROMPTS[0][:5], 6)
+        sch.run([a])
+        return list(a.seq.out), sch.stats, sch.stats.prefill_tokens - pf0
+    out_kept, st_kept, pf_kept = run(0, False, 0)
+    out_tier, st_tier, pf_tier = run(12, True, 16)
+    assert st_tier.offloaded_sessions >= 1 and st_tier.restored_sessions >= 1 and st_tier.evicted_sessions == 0
+    assert out_tier == out_kept
+    assert pf_tier == pf_kept == 6            # the push only: no recompute of the context
