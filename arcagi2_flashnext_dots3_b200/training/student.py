@@ -150,9 +150,11 @@ class MoETrain(nn.Module):
 
 
 class FNStudent(nn.Module):
-    def __init__(self, cfg, W: dict, device, train_norms: bool = False):
+    def __init__(self, cfg, W: dict, device, train_norms: bool = False, layer_offset: int = 0):
+        """``layer_offset``: W["layers"] holds layers layer_offset.. of the model (a pipeline stage)."""
         super().__init__()
         self.cfg = cfg
+        self.l0 = layer_offset
         self.device = torch.device(device)
         Wd = _to({k: v for k, v in W.items() if k != "layers"}, self.device)
         Wd["layers"] = [_to({k: v for k, v in L.items() if k != "moe"}, self.device) for L in W["layers"]]
@@ -172,7 +174,7 @@ class FNStudent(nn.Module):
         if "ple" in L:
             h = h + R.ple(h, emb, L["ple"], cfg)
         x, inj = R.gated_residual(h, L["ahc"], hc, H, cfg.rms_eps)
-        if cfg.layer_kind(l) == "linear":
+        if cfg.layer_kind(l + self.l0) == "linear":
             y = gdn_train(x, L["mix"], cfg)
         else:
             y = qsa_train(x, L["mix"], cfg, cos, sin)

@@ -175,3 +175,12 @@ def test_flag_report_and_reclaim():
     llm.generate([[1, 2, 3]], max_new_tokens=2)          # CPU matmuls fill the dense-copy caches
     freed = observe.reclaim(llm)
     assert freed["dense_caches"] > 0
+
+
+def test_pipeline_parallel_two_stages_match_single_process():
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29711", os.path.join(here, "pp_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "PP_OK" in r.stdout, (r.stdout[-2000:], r.stderr[-3000:])
