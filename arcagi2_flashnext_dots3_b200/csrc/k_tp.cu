@@ -180,6 +180,65 @@ __device__ __forceinline__ float4 unpack_q8(uint32_t q, float s) {
                      (float)(int8_t)((q >> 16) & 0xff) * s, (float)(int8_t)(q >> 24) * s);
 }
 
+// 4-bit codes -7..7 of four values, two per byte, as 16 bits.
+__device__ __forceinline__ uint32_t pack_q4(float4 v, float inv) {
+  auto c = [&](float x) { return (uint32_t)(max(-7, min(7, __float2int_rn(x * inv))) & 0xf); };
+  return c(v.x) | (c(v.y) << 4) | (c(v.z) << 8) | (c(v.w) << 12);
+}
+
+__device__ __forceinline__ float4 unpack_q4(uint32_t q, float s) {
+  auto d = [&](int sh) { int c = (int)((q >> sh) & 0xf); return (float)(c >= 8 ? c - 16 : c) * s; };
+  return make_float4(d(0), d(4), d(8), d(12));
+}
+
+// Orthonormal 128-point Walsh-Hadamard transform of a warp's 128 values (lane l holds elements 4l .. 4l + 3):
+// butterflies of stride 1 and 2 in registers, 4 .. 64 across lanes. Symmetric and orthogonal: its own inverse.
+__device__ __forceinline__ float4 wht128(float4 v) {
+  float a = v.x + v.y, b = v.x - v.y, c = v.z + v.w, d = v.z - v.w;
+  v = make_float4(a + c, b + d, a - c, b - d);
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    const float px = __shfl_xor_sync(0xffffffffu, v.x, m), py = __shfl_xor_sync(0xffffffffu, v.y, m),
+                pz = __shfl_xor_sync(0xffffffffu, v.z, m), pw = __shfl_xor_sync(0xffffffffu, v.w, m);
+    if (lane & m) v = make_float4(px - v.x, py - v.y, pz - v.z, pw - v.w);
+    else v = make_float4(v.x + px, v.y + py, v.z + pz, v.w + pw);
+  }
+  const float r = 0.08838834764831845f;   // 1 / sqrt(128)
+  return make_float4(v.x * r, v.y * r, v.z * r, v.w * r);
+}
+
+struct QArOpts {
+  int bits;          // 8 or 4
+  int had;           // rotate each 128-group by the Walsh-Hadamard transform before quantizing
+  float* carry;      // error feedback: [n_max] this rank's carried error (nullptr: off)
+};
+
+// Quantize one warp-group of four values per lane; returns the packed codes and the scale, and (when ef) the
+// quantization error in the original domain.
+__device__ __forceinline__ uint32_t quant_group(float4 v, const QArOpts& o, float& scale, float4* err) {
+  const float qmax = o.bits == 8 ? 127.f : 7.f;
+  const float amax = warp_absmax(fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  scale = amax > 0.f ? amax / qmax : 1.f;
+  const uint32_t q = o.bits == 8 ? pack_q8(v, 1.f / scale) : pack_q4(v, 1.f / scale);
+  if (err) {
+    const float4 d = o.bits == 8 ? unpack_q8(q, scale) : unpack_q4(q, scale);
+    float4 e = make_float4(v.x - d.x, v.y - d.y, v.z - d.z, v.w - d.w);
+    *err = o.had ? wht128(e) : e;
+  }
+  return q;
+}
+
+__device__ __forceinline__ void store_codes(int8_t* base, int64_t g, int lane, uint32_t q, int bits) {
+  if (bits == 8) reinterpret_cast<uint32_t*>(base + g * 128)[lane] = q;
+  else reinterpret_cast<uint16_t*>(base + g * 128)[lane] = (uint16_t)q;
+}
+
+__device__ __forceinline__ float4 load_codes(const int8_t* base, int64_t g, int lane, float s, int bits) {
+  if (bits == 8) return unpack_q8(reinterpret_cast<const uint32_t*>(base + g * 128)[lane], s);
+  return unpack_q4(reinterpret_cast<const uint16_t*>(base + g * 128)[lane], s);
+}
+
 // Bounded wait of one thread for flag >= e; false on timeout (error 6410 + peer) or abort.
 __device__ bool wait_epoch(const int64_t* flag, int64_t e, int peer, int* err, int* abort_word, uint64_t limit_ns) {
   uint64_t t0 = 0;
@@ -201,7 +260,7 @@ __device__ bool wait_epoch(const int64_t* flag, int64_t e, int peer, int* err, i
 
 __global__ void __launch_bounds__(128) tp_qar_kernel(const float* __restrict__ x, float* __restrict__ h, int64_t n,
                                                      const uint64_t* bases, int me, int W, QArLayout L,
-                                                     const int64_t* epoch, int* err, uint64_t limit_ns) {
+                                                     const int64_t* epoch, int* err, uint64_t limit_ns, QArOpts o) {
   __shared__ int ok;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = gridDim.x, b = blockIdx.x;
   const int64_t e = epoch[0];
@@ -222,10 +281,17 @@ __global__ void __launch_bounds__(128) tp_qar_kernel(const float* __restrict__ x
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (i0 + 3 < n) v = *reinterpret_cast<const float4*>(x + i0);
       else if (i0 < n) { v.x = x[i0]; if (i0 + 1 < n) v.y = x[i0 + 1]; if (i0 + 2 < n) v.z = x[i0 + 2]; }
-      const float amax = warp_absmax(fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-      const float s = amax > 0.f ? amax / 127.f : 1.f;
-      reinterpret_cast<uint32_t*>(q + g * 128)[lane] = pack_q8(v, 1.f / s);
+      if (o.carry && i0 < n) {   // error feedback: add the error carried from the previous all-reduce
+        const float4 cv = *reinterpret_cast<const float4*>(o.carry + i0);
+        v.x += cv.x; v.y += cv.y; v.z += cv.z; v.w += cv.w;
+      }
+      if (o.had) v = wht128(v);
+      float s;
+      float4 e;
+      const uint32_t qq = quant_group(v, o, s, o.carry ? &e : nullptr);
+      store_codes(q, g, lane, qq, o.bits);
       if (lane == 0) sc[g] = s;
+      if (o.carry && i0 < n) *reinterpret_cast<float4*>(o.carry + i0) = e;   // this rank's share of the error
     }
   }
   __threadfence_system();
@@ -244,17 +310,23 @@ __global__ void __launch_bounds__(128) tp_qar_kernel(const float* __restrict__ x
     for (int64_t g = b + (int64_t)warp * G; g < L.groups; g += 4LL * G) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int s2 = 0; s2 < W; ++s2) {
-        const uint32_t qq = reinterpret_cast<const uint32_t*>(rq + (int64_t)s2 * L.chunk + g * 128)[lane];
-        const float4 d = unpack_q8(qq, rs[(int64_t)s2 * L.groups + g]);
+        const float4 d = load_codes(rq + (int64_t)s2 * L.chunk, g, lane, rs[(int64_t)s2 * L.groups + g], o.bits);
         acc.x += d.x; acc.y += d.y; acc.z += d.z; acc.w += d.w;
       }
-      const float amax = warp_absmax(fmaxf(fmaxf(fabsf(acc.x), fabsf(acc.y)), fmaxf(fabsf(acc.z), fabsf(acc.w))));
-      const float s = amax > 0.f ? amax / 127.f : 1.f;
-      const uint32_t packed = pack_q8(acc, 1.f / s);
-      for (int o = 0; o < W; ++o) {
-        char* peer = reinterpret_cast<char*>(bases[o]);
-        reinterpret_cast<uint32_t*>(reinterpret_cast<int8_t*>(peer + L.ag_q) + ((int64_t)par * W + me) * L.chunk +
-                                    g * 128)[lane] = packed;
+      float s;
+      float4 e;
+      const int64_t i0 = (int64_t)me * L.chunk + g * 128 + lane * 4;
+      // the error pointer must be warp-uniform (the Hadamard transform shuffles); only the store is per lane
+      const uint32_t packed = quant_group(acc, o, s, o.carry ? &e : nullptr);
+      if (o.carry && i0 < n) {   // the owner also carries the re-quantization error of its chunk's sum
+        float4 cv = *reinterpret_cast<float4*>(o.carry + i0);
+        cv.x += e.x; cv.y += e.y; cv.z += e.z; cv.w += e.w;
+        *reinterpret_cast<float4*>(o.carry + i0) = cv;
+      }
+      for (int r = 0; r < W; ++r) {
+        char* peer = reinterpret_cast<char*>(bases[r]);
+        store_codes(reinterpret_cast<int8_t*>(peer + L.ag_q) + ((int64_t)par * W + me) * L.chunk, g, lane, packed,
+                    o.bits);
         if (lane == 0) reinterpret_cast<float*>(peer + L.ag_s)[((int64_t)par * W + me) * L.groups + g] = s;
       }
     }
@@ -265,18 +337,18 @@ __global__ void __launch_bounds__(128) tp_qar_kernel(const float* __restrict__ x
   // ---- phase 3: gather every owner's reduced chunk into h
   if (threadIdx.x == 0) {
     ok = 1;
-    for (int o = 0; o < W && ok; ++o) ok = wait_epoch(flag_at(mine, 1, o), e, o, err, abort_word, limit_ns);
+    for (int ow = 0; ow < W && ok; ++ow) ok = wait_epoch(flag_at(mine, 1, ow), e, ow, err, abort_word, limit_ns);
   }
   __syncthreads();
   if (!ok) return;
   const int8_t* aq = reinterpret_cast<const int8_t*>(mine + L.ag_q) + (int64_t)par * W * L.chunk;
   const float* as = reinterpret_cast<const float*>(mine + L.ag_s) + (int64_t)par * W * L.groups;
-  for (int o = 0; o < W; ++o) {
+  for (int ow = 0; ow < W; ++ow) {
     for (int64_t g = b + (int64_t)warp * G; g < L.groups; g += 4LL * G) {
-      const int64_t i0 = (int64_t)o * L.chunk + g * 128 + lane * 4;
+      const int64_t i0 = (int64_t)ow * L.chunk + g * 128 + lane * 4;
+      float4 d = load_codes(aq + (int64_t)ow * L.chunk, g, lane, as[(int64_t)ow * L.groups + g], o.bits);
+      if (o.had) d = wht128(d);      // all lanes take part in the shuffles before any of them leaves
       if (i0 >= n) continue;
-      const float4 d = unpack_q8(reinterpret_cast<const uint32_t*>(aq + (int64_t)o * L.chunk + g * 128)[lane],
-                                 as[(int64_t)o * L.groups + g]);
       if (i0 + 3 < n) {
         float4 t = *reinterpret_cast<float4*>(h + i0);
         t.x += d.x; t.y += d.y; t.z += d.z; t.w += d.w;
@@ -310,7 +382,15 @@ int64_t tp_qar_bytes(int64_t n_max, int64_t W, int64_t G) {
 }
 
 void tp_qar(torch::Tensor x, torch::Tensor h, int64_t n, torch::Tensor bases, int64_t me, int64_t n_max, int64_t G,
-            torch::Tensor epoch, torch::Tensor err, int64_t timeout_ns) {
+            torch::Tensor epoch, torch::Tensor err, int64_t timeout_ns, int64_t bits, bool had,
+            c10::optional<torch::Tensor> carry) {
+  TORCH_CHECK(bits == 8 || bits == 4, "payload bits must be 8 or 4");
+  QArOpts o{(int)bits, had ? 1 : 0, nullptr};
+  if (carry) {
+    TORCH_CHECK(carry->is_cuda() && carry->scalar_type() == torch::kFloat && carry->numel() >= n &&
+                reinterpret_cast<uintptr_t>(carry->data_ptr()) % 16 == 0);
+    o.carry = carry->data_ptr<float>();
+  }
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kFloat && x.is_contiguous() && x.numel() >= n);
   TORCH_CHECK(h.is_cuda() && h.scalar_type() == torch::kFloat && h.is_contiguous() && h.numel() >= n);
   TORCH_CHECK(n <= n_max, "all-reduce larger than its area");
@@ -324,7 +404,7 @@ void tp_qar(torch::Tensor x, torch::Tensor h, int64_t n, torch::Tensor bases, in
   tp_qar_kernel<<<(int)G, 128, 0, STREAM>>>(x.data_ptr<float>(), h.data_ptr<float>(), n,
                                             reinterpret_cast<const uint64_t*>(bases.data_ptr<int64_t>()), (int)me, W,
                                             L, epoch.data_ptr<int64_t>(), err.data_ptr<int32_t>(),
-                                            (uint64_t)timeout_ns);
+                                            (uint64_t)timeout_ns, o);
 }
 
 }  // namespace

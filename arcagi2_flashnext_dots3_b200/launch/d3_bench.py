@@ -37,7 +37,7 @@ def main():
     ap.add_argument("--ctx", type=int, default=32768)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--comm", default="fused", choices=["fused", "nccl", "q8"])
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl", "q8", "q4"])
     ap.add_argument("--eager", action="store_true", help="no CUDA graph (for launch lists)")
     ap.add_argument("--shard-vocab", action="store_true",
                     help="with TP: each rank holds its slice of the LM head; tokens via the sharded pick")

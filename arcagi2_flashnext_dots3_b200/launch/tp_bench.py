@@ -46,7 +46,7 @@ def _time(fn, steps, warmup):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--comm", default="fused", choices=["fused", "nccl", "q8"])
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl", "q8", "q4"])
     ap.add_argument("--layers", type=int, default=3)
     ap.add_argument("--experts", type=int, default=16)
     ap.add_argument("--vocab", type=int, default=32768)

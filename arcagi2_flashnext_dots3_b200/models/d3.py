@@ -220,6 +220,8 @@ class D3Model:
         cfg, W = self.cfg, self.W
         h = h.float().contiguous()
         self._h = h
+        if self.tp is not None and hasattr(self.tp, "begin_forward"):
+            self.tp.begin_forward()
         y = None
         for l, L in enumerate(W["layers"]):
             x = d3.add_rms(h, y, L["ln1"], cfg.rms_eps, self.act)

@@ -30,8 +30,15 @@ def tp_config(cfg, world: int):
 
 class TPGroup:
     def __init__(self, rank: int, world: int, device, max_tokens: int, hidden: int, group=None, comm: str = "fused",
-                 timeout_ns: int = None):
+                 timeout_ns: int = None, q_bits: int = 8, hadamard: bool = False, error_feedback: bool = False):
+        """``comm="q8"`` options: ``q_bits`` 8 or 4 (codes -7..7), ``hadamard`` (128-point Walsh-Hadamard rotation
+        of every scale group before quantizing), ``error_feedback`` (within one forward pass each rank adds the
+        quantization error it carried out of the previous all-reduce to its next input; :meth:`begin_forward`
+        clears the carry)."""
+        if comm == "q4":     # shorthand: 4-bit payload with rotation and error feedback
+            comm, q_bits, hadamard, error_feedback = "q8", 4, True, True
         self.rank, self.world, self.comm = rank, world, comm
+        self.q_bits, self.hadamard, self.error_feedback = q_bits, hadamard, error_feedback
         self.device = torch.device(device)
         self.group = group or dist.group.WORLD
         self.H = hidden
@@ -68,6 +75,7 @@ class TPGroup:
                                            dtype=torch.int64, device=self.device)
                 torch.cuda.synchronize(self.device)
                 dist.barrier(group=self.group)
+            self.carry = torch.zeros(self.slot, dtype=torch.float32, device=self.device) if error_feedback else None
         elif comm != "nccl":
             raise ValueError(comm)
 
@@ -75,6 +83,11 @@ class TPGroup:
     def begin(self):
         if self.comm in ("fused", "q8"):
             native.C().tp_epoch(self.epoch)
+
+    def begin_forward(self):
+        """Start of a forward pass: the error-feedback chain restarts (errors never cross forward passes)."""
+        if getattr(self, "carry", None) is not None:
+            self.carry.zero_()
 
     def fan(self):
         """wgemm fan-out arguments: write the GEMM output into slot [rank] of every rank's buffer."""
@@ -94,14 +107,22 @@ class TPGroup:
         if T > self.max_tokens:
             raise ValueError(f"{T} rows > TP buffer capacity {self.max_tokens}")
         if self.comm == "q8":
+            n = T * self.H
             if not partial.is_cuda:   # CPU ranks: the same quantized arithmetic through gathered partials
-                parts = [torch.empty_like(partial) for _ in range(self.world)]
-                dist.all_gather(parts, partial.contiguous(), group=self.group)
-                h += qar_reference(parts)
+                x = partial.reshape(-1).float()
+                if self.carry is not None:
+                    x = x + self.carry[:n]
+                parts = [torch.empty_like(x) for _ in range(self.world)]
+                dist.all_gather(parts, x.contiguous(), group=self.group)
+                out, carry = qar_reference(parts, self.q_bits, self.hadamard, rank=self.rank)
+                if self.carry is not None:
+                    self.carry[:n] = carry
+                h += out.view_as(h)
                 return
             self.begin()
-            native.C().tp_qar(partial.contiguous(), h, T * self.H, self.qbases, self.rank, self.slot, self.qar_grid,
-                              self.epoch, native.err_word(self.device), self.timeout_ns)
+            native.C().tp_qar(partial.contiguous(), h, n, self.qbases, self.rank, self.slot, self.qar_grid,
+                              self.epoch, native.err_word(self.device), self.timeout_ns, self.q_bits, self.hadamard,
+                              self.carry)
             return
         if self.comm == "nccl" or not partial.is_cuda:
             dist.all_reduce(partial, group=self.group)
@@ -126,29 +147,50 @@ class TPGroup:
         self.finish_into(h, T)
 
 
-def _q8(x: torch.Tensor):
-    """Per 128-element group: (codes, scale) with scale = absmax / 127 (1 for an all-zero group) and codes =
-    round-half-even(x * (1 / scale)); x is [groups, 128]."""
+def _quant(x: torch.Tensor, bits: int = 8):
+    """Per 128-element group: (codes, scale) with scale = absmax / qmax (1 for an all-zero group), qmax 127 or 7,
+    and codes = round-half-even(x * (1 / scale)) clamped to +-qmax; x is [groups, 128]."""
+    qmax = 127.0 if bits == 8 else 7.0
     amax = x.abs().amax(-1, keepdim=True)
-    s = torch.where(amax > 0, amax / 127.0, torch.ones_like(amax))
-    return torch.round(x * (1.0 / s)), s
+    s = torch.where(amax > 0, amax / qmax, torch.ones_like(amax))
+    return torch.round(x * (1.0 / s)).clamp(-qmax, qmax), s
 
 
-def qar_reference(partials: list) -> torch.Tensor:
+def hadamard128(device=None) -> torch.Tensor:
+    """Orthonormal Sylvester Walsh-Hadamard matrix of order 128 (symmetric: its own inverse)."""
+    h = torch.ones(1, 1)
+    while h.shape[0] < 128:
+        h = torch.cat([torch.cat([h, h], 1), torch.cat([h, -h], 1)], 0)
+    return (h / 128 ** 0.5).to(device)
+
+
+def qar_reference(partials: list, bits: int = 8, had: bool = False, rank: int = None):
     """The quantized two-shot all-reduce of csrc/k_tp.cu in torch (same chunking, rounding and summation order):
-    every rank's partial quantized per 128-element group, dequantized and summed in rank order per owner chunk,
-    the sum quantized again. Returns the fp32 sum every rank adds."""
+    every rank's partial (optionally rotated by the 128-point Walsh-Hadamard transform) quantized per 128-element
+    group, dequantized and summed in rank order per owner chunk, the sum quantized again, rotated back. Returns the
+    fp32 sum every rank adds, or with ``rank`` given (sum, that rank's error-feedback carry: its quantization error
+    everywhere plus, on its own chunk, the re-quantization error of the sum)."""
     W = len(partials)
     shape, n = partials[0].shape, partials[0].numel()
     chunk = ((n + W - 1) // W + 127) // 128 * 128
     pad = W * chunk - n
-    xs = [torch.nn.functional.pad(p.reshape(-1).float(), (0, pad)).view(-1, 128) for p in partials]
+    Hm = hadamard128(partials[0].device) if had else None
+    rot = (lambda v: v @ Hm) if had else (lambda v: v)
+    xs = [rot(torch.nn.functional.pad(p.reshape(-1).float(), (0, pad)).view(-1, 128)) for p in partials]
     acc = torch.zeros_like(xs[0])
+    errs = []
     for x in xs:                                  # rank order, as every owner sums its sources
-        q, s = _q8(x)
+        q, s = _quant(x, bits)
         acc = acc + q * s
-    q, s = _q8(acc)
-    return (q * s).reshape(-1)[:n].view(shape)
+        errs.append(x - q * s)
+    q, s = _quant(acc, bits)
+    out = rot(q * s).reshape(-1)[:n].view(shape)
+    if rank is None:
+        return out
+    carry = rot(errs[rank]).reshape(-1)
+    g0, g1 = rank * chunk // 128, (rank + 1) * chunk // 128
+    carry.view(-1, 128)[g0:g1] += rot(acc - q * s)[g0:g1]
+    return out, carry[:n]
 
 
 def sharded_speculative_accept(local_logits: torch.Tensor, v0: int, drafts, temps, seeds, steps, group=None):

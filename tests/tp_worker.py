@@ -67,6 +67,25 @@ def main():
         exact_sum = sum(p.cpu() for p in parts) + 0.5
         assert qerr < 1e-6, (rank, qerr)
         assert float((h.cpu() - exact_sum).abs().max() / exact_sum.abs().max()) < 2e-2
+        # 4-bit payloads over a chain of all-reduces into one residual (one forward pass): with Hadamard rotation
+        # and error feedback the residual keeps only about the last all-reduce's error
+        errs = {}
+        for name, kw in (("q4_ef", dict(comm="q4")),
+                         ("q4_noef", dict(comm="q8", q_bits=4, hadamard=True, error_feedback=False))):
+            tq = TPGroup(rank, world, dev, max_tokens=32, hidden=cfg.hidden_size, **kw)
+            tq.begin_forward()
+            hh = torch.zeros(13, cfg.hidden_size, device=dev)
+            exact = torch.zeros(13, cfg.hidden_size)
+            for l in range(6):
+                gl = torch.Generator().manual_seed(1000 * l + 7)
+                allp = [torch.randn(13, cfg.hidden_size, generator=gl) * (1 + r) for r in range(world)]
+                tq.allreduce_add(hh, allp[rank].to(dev))
+                exact += sum(allp)
+            if cuda:
+                torch.cuda.synchronize()
+                native.check_error(dev)
+            errs[name] = float((hh.cpu() - exact).abs().pow(2).mean().sqrt() / exact.abs().pow(2).mean().sqrt())
+        assert errs["q4_ef"] < 0.6 * errs["q4_noef"] and errs["q4_ef"] < 0.08, (rank, errs)
     assert err < tol, (rank, float(err))
     if os.environ.get("TP_SHARD_INDEX") == "1":
         # index keys sharded by position mod world: same selection, same logits as the unsharded TP model
