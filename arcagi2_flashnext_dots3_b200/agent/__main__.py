@@ -13,7 +13,26 @@ import asyncio
 import json
 
 from .client import SessionClient
-from .solver import Solver, ensure_submission, write_submission
+from .solver import Solver, ServerRoom, ensure_submission, write_submission
+
+
+def stats_poller(server: str, every_s: float = 1.0):
+    """A cached synchronous read of the server's session stats (free KV blocks, block size)."""
+    import time
+
+    import requests
+    last = {"t": 0.0, "v": None}
+
+    def get():
+        now = time.time()
+        if now - last["t"] >= every_s:
+            try:
+                last["v"] = requests.get(f"{server}/arc/session/stats", timeout=2.0).json()
+            except (requests.RequestException, ValueError):
+                pass              # keep the last reading; no reading at all means no room limit
+            last["t"] = now
+        return last["v"] or {"kv_blocks_free": 1 << 40, "block_size": 1}
+    return get
 
 
 def main(argv=None):
@@ -39,8 +58,10 @@ def main(argv=None):
     def factory(tid, idx):
         return SessionClient(a.server, tok, f"{tid}_{idx}", a.max_model_len, temperature=a.temperature,
                              seed=hash((tid, idx)) & 0x7FFFFFFF)
+    def est_ctx(task):   # prompt (about 3.5 characters per token) plus every turn's generation
+        return int(len(json.dumps(task)) / 3.5) + a.max_turns * (a.max_tokens + 256)
     s = Solver(tasks, factory, a.samples, a.concurrency, a.deadline_s, a.endgame_s, max_turns=a.max_turns,
-               max_tokens=a.max_tokens)
+               max_tokens=a.max_tokens, ctx_room=ServerRoom(stats_poller(a.server)), est_ctx=est_ctx)
     write_submission(a.out, asyncio.run(s.run()))
     ensure_submission(a.out, tasks)
     print(json.dumps({"tasks": len(tasks), "samples": len(s.log), "verified": sum(bool(x.get("verified")) for x in s.log)}))

@@ -87,6 +87,11 @@ if res["has_transform"]:
             res["flags"] = ak.flag(train, test_inputs, [t["out"] for t in res["tests"]])
         except Exception as e:
             res["flags_err"] = repr(e)[:200]
+    try:   # the helper library's full report: masked diffs, leave-one-out, size / invariant / equivariance notes
+        with contextlib.redirect_stdout(io.StringIO()), contextlib.redirect_stderr(io.StringIO()):
+            res["check_text"] = ak.check(f, train, test_inputs, verbose=False)["text"][:4000]
+    except BaseException as e:
+        res["check_err"] = repr(e)[:200]
 with open("result.json", "w") as fh:
     json.dump(res, fh)
 '''
@@ -144,6 +149,12 @@ def feedback(res: dict, task: dict, max_cells: int = 400) -> str:
     masked ('.') against the program's output."""
     if res.get("timeout"):
         return "Your program timed out."
+    if res.get("check_text") and res.get("has_transform"):
+        parts = ["Error:\n" + res["error"]] if res.get("error") else []
+        parts.append(res["check_text"])
+        if res.get("stdout"):
+            parts.append("Printed output:\n" + res["stdout"][:1500])
+        return "\n".join(parts)
     parts = []
     if res.get("error"):
         parts.append("Error:\n" + res["error"])

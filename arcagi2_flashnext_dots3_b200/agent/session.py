@@ -42,17 +42,41 @@ def extract_code(text: str):
     return blocks[-1] if blocks else None
 
 
+FORCE = ("Time is almost up. Reply now with your final ```python``` block defining transform(grid), the best "
+         "program you have; no further feedback will follow.")
+
+
+def estimate_tokens(text: str) -> int:
+    """Rough token count of generated text (about 3.5 characters per token for code and grids)."""
+    return max(1, int(len(text) / 3.5))
+
+
 async def solve_sample(task: dict, complete, max_turns: int = 4, max_tokens: int = 2048, deadline: float = None,
-                       sandbox_timeout: float = 25.0) -> dict:
-    """Returns {"progs": [...], "answer": [...], "turns": n, "verified": bool}."""
+                       sandbox_timeout: float = 25.0, token_budget: int = None, force_at: float = None,
+                       force_tokens: int = 1024) -> dict:
+    """Returns {"progs": [...], "answer": [...], "turns": n, "verified": bool, "used": tokens}.
+
+    ``token_budget`` caps the sample's generated tokens; ``force_at`` (a time) or a budget too small for another
+    regular turn turns the next turn into a forced final answer of at most ``force_tokens`` tokens (the
+    reference's forced conclusions, repl_session.py / repl_solve.py endgame)."""
     messages = [{"role": "system", "content": SYSTEM}, {"role": "user", "content": task_prompt(task)}]
-    rec = {"progs": [], "answer": [], "turns": 0, "verified": False}
+    rec = {"progs": [], "answer": [], "turns": 0, "verified": False, "used": 0, "forced": False}
     n_train = len(task["train"])
     for turn in range(max_turns):
         if deadline is not None and time.time() > deadline:
             rec["stopped"] = "deadline"
             break
-        reply = await complete(messages, max_tokens)
+        left = None if token_budget is None else token_budget - rec["used"]
+        forced = (force_at is not None and time.time() >= force_at) or (left is not None and left < max_tokens)
+        if forced and rec["forced"]:
+            rec["stopped"] = "budget"
+            break
+        if forced and turn > 0:
+            messages.append({"role": "user", "content": FORCE})
+        n_tok = min(force_tokens if forced else max_tokens, max(1, left) if left is not None else 1 << 30)
+        reply = await complete(messages, n_tok)
+        rec["forced"] = rec["forced"] or forced
+        rec["used"] += estimate_tokens(reply)
         rec["turns"] += 1
         messages.append({"role": "assistant", "content": reply})
         code = extract_code(reply)
@@ -70,5 +94,12 @@ async def solve_sample(task: dict, complete, max_turns: int = 4, max_tokens: int
             rec["verified"] = True
             rec["answer"] = tests
             break
+        if rec["forced"]:
+            rec["answer"] = tests
+            break
         messages.append({"role": "user", "content": feedback(res, task)})
+    if not rec["answer"] and rec["progs"]:   # best partial program's test outputs as the sample's answer
+        best = max(rec["progs"], key=lambda p: (p["n_ok"], p["k"]))
+        if all(t is not None for t in best["tests"]):
+            rec["answer"] = best["tests"]
     return rec

@@ -90,7 +90,8 @@ def create_app(engine: EngineLoop, model_name: str = "arcagi2-b200"):
         if sched is not None:   # scheduler counters: admissions, preemptions, idle-session evictions, KV state
             out.update({f"sched_{k}": int(v) for k, v in vars(sched.stats).items()})
             out.update(waiting=len(sched.waiting), running=len(sched.running), idle_sessions=len(sched.idle),
-                       kv_blocks_free=int(engine.llm.alloc.n_free()))
+                       kv_blocks_free=int(engine.llm.alloc.n_free()),
+                       block_size=int(engine.llm.caches.block_size))
         return JSONResponse(out)
 
     @app.post("/v1/completions")

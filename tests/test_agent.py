@@ -96,6 +96,9 @@ def test_sandbox_runs_and_scores():
     assert r["tests"][0]["out"] == [[0, 0, 5], [7, 0, 0]]
     r = run_code_sync("def transform(g):\n    return g\n", TASK)
     assert not r["train"][0]["ok"]
+    fb = feedback(r, TASK)
+    assert "0/2 training pairs correct" in fb and "cells wrong in box" in fb
+    r.pop("check_text")                      # without the helper report: the sandbox's own masked diffs
     assert "train 0: wrong cells" in feedback(r, TASK)
 
 
@@ -203,3 +206,65 @@ def test_vote_partial_weights_and_verified_override():
     assert r["attempts"] == [g1, g3] and r["from"] == ["ver", "fb"] and r["n_verified"] == 1
     r = rank(recs[:2], 1)[0]
     assert r["attempts"] == [g3, g2] and r["votes"] == [0, 0]
+
+
+def test_rate_meter_and_sample_budget():
+    from arcagi2_flashnext_dots3_b200.agent.solver import RateMeter
+    t = [0.0]
+    m = RateMeter(window=10.0, clock=lambda: t[0])
+    assert m.rate() is None
+    for k in range(12):
+        t[0] = float(k)
+        m.add(100)
+    assert abs(m.rate() - 100.0) < 1e-6          # sliding window keeps a steady 100 tok/s
+    s = Solver({"a": TASK, "b": TASK}, lambda tid, i: None, samples_per_task=2, deadline_s=100, endgame_s=0,
+               max_turns=4, max_tokens=2048, rate=m, min_sample_tokens=64)
+    now = s.cut - 10.0                           # 10 s x 100 tok/s = 1000 tokens for 4 samples to run
+    assert s.sample_budget(now) == 250
+    assert s.sample_budget(s.cut + 1) == 64      # past the cut only the floor is left
+    m2 = RateMeter()
+    s.rate = m2
+    assert s.sample_budget(now) == 4 * 2048      # no rate yet: the turn-based cap
+
+
+def test_server_room_and_tiers():
+    from arcagi2_flashnext_dots3_b200.agent.solver import ServerRoom
+    stats = {"kv_blocks_free": 10, "block_size": 64}
+    room = ServerRoom(lambda: stats)
+    assert room() == 640
+    room.grow[("a", 0)] = 600
+    assert room() == 40
+    s = Solver({"a": TASK, "b": TASK}, lambda tid, i: None, samples_per_task=3, ctx_room=room,
+               est_ctx=lambda task: 100)
+    assert s.pick() is None                      # 40 tokens of room, 100 projected
+    room.grow.clear()
+    st = s.pick()
+    assert st.tid == "a" and st.tier(2) == 0
+    st.started = 1
+    st.recs.append({"verified": True, "answer": [[[1]]], "progs": []})
+    assert st.tier(2) == 2 and s.pick().tid == "b"   # never-started tasks first
+    s.tasks["b"].started = 1
+    s.tasks["b"].recs.append({"verified": False, "answer": [], "progs": []})
+    assert s.pick().tid == "b"                   # unverified before verified-unsettled
+
+
+def test_session_forced_conclusion_and_budget():
+    from arcagi2_flashnext_dots3_b200.agent.session import FORCE, solve_sample
+    seen = []
+
+    async def complete(messages, n_tok):
+        seen.append((messages[-1]["content"], n_tok))
+        return "```python\ndef transform(g):\n    return g\n```"
+    import time
+    rec = asyncio.run(solve_sample(TASK, complete, max_turns=5, max_tokens=512, force_at=time.time() + 3600,
+                                   token_budget=1200, force_tokens=128))
+    # turn 1 and 2 regular (1200 - 2 x ~13 > 512), then budget stays > 512: no forcing by budget here
+    assert rec["turns"] == 5 and not rec["forced"]
+    seen.clear()
+    rec = asyncio.run(solve_sample(TASK, complete, max_turns=5, max_tokens=512, force_at=0.0, force_tokens=128))
+    assert rec["turns"] == 1 and rec["forced"] and seen[0][1] == 128
+    assert rec["answer"] == [TASK["test"][0]["input"]]   # the forced program's test outputs are the answer
+    seen.clear()
+    rec = asyncio.run(solve_sample(TASK, complete, max_turns=5, max_tokens=512, token_budget=520,
+                                   force_tokens=128))
+    assert rec["turns"] == 2 and rec["forced"] and seen[1] == (FORCE, 128)
