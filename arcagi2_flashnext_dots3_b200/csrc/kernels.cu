@@ -14,6 +14,7 @@ void register_gemv(pybind11::module& m);
 void register_tp(pybind11::module& m);
 void register_mla(pybind11::module& m);
 void register_dsa(pybind11::module& m);
+void register_f8gemm(pybind11::module& m);
 
 void register_kernels(pybind11::module& m) {
   register_fn(m);
@@ -26,4 +27,5 @@ void register_kernels(pybind11::module& m) {
   register_tp(m);
   register_mla(m);
   register_dsa(m);
+  register_f8gemm(m);
 }

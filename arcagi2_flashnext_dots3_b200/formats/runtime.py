@@ -122,6 +122,16 @@ def pack_fp8(w8: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
     return torch.cat([words, sc.view(torch.uint8).reshape(T, KG, 16)], -1).contiguous()
 
 
+def fp8_rowmajor(blob: torch.Tensor, R: int, K: int):
+    """FP8 tile blocks [tiles, KG, 16400] -> (e4m3 codes as uint8 [tiles*128, K] in row-major order, rows past R
+    zero; fp32 block scales [tiles, KG]): the operand layout of the tcgen05 `kind::f8f6f4` dense GEMM, whose TMA
+    loads read 128-column groups of 128 rows straight from it."""
+    T, KG, _ = blob.shape
+    codes = blob[..., : 32 * 512].reshape(T, KG, 32, TILE, 4).permute(0, 3, 1, 2, 4).reshape(T * TILE, KG * 128)
+    scale = blob[..., 32 * 512: 32 * 512 + 4].contiguous().view(torch.float32).reshape(T, KG)
+    return codes.contiguous(), scale.contiguous()
+
+
 def pack_f16(w: torch.Tensor) -> torch.Tensor:
     """Dense fp16 [R, K] -> uint8 blocks [tiles, KG, 32768]."""
     R, K = w.shape

@@ -75,43 +75,52 @@ def bench_moe(args):
 
 
 def bench_dense(args):
+    """Dense FP8 projections at decode batch: the tcgen05 kind::f8f6f4 GEMM (per-group FP8 activations, the
+    default) against the weight-dequant kind::f16 GEMM. Each arm rotates over enough weight copies that every
+    replay streams more than the 126 MB L2 from HBM; 10 launches per CUDA graph."""
     from ..ops import native, wgemm
     dev = torch.device("cuda")
     T = args.tokens
     shapes = [("hc_down", 388, 10240), ("hc_up", 10240, 384), ("gdn_proj", 16480, 2560), ("gdn_out", 2560, 6144),
-              ("attn_proj", 11904, 2560), ("attn_o", 2560, 4096), ("router", 321, 2560), ("lm_head", 151936, 2560)]
-    for name, R, K in shapes:
-        if args.only and name not in args.only.split(","):
-            continue
-        wt = torch.randn(R, K, device=dev) * 0.02
-        ws = wgemm.dense_fp8(wt)
-        x = torch.randn(T, K, device=dev).half()
-        out = torch.empty(T, R, device=dev)
-        t = _time(lambda: wgemm.matmul(x, ws, out=out), args.reps)
-        # device time without host launch gaps: 10 launches captured in one CUDA graph
-        wgemm.matmul(x, ws, out=out)
+              ("attn_proj", 11904, 2560), ("attn_o", 2560, 4096), ("router", 321, 2560),
+              ("shared_gu", 1280, 2560), ("shared_d", 2560, 640)]
+
+    def graph_us(fn, copies):
+        fn(copies[0])
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            for _ in range(10):
-                wgemm.matmul(x, ws, out=out)
-        t_graph = _time(g.replay, args.reps) / 10
-        b = ws.nbytes()
+            for i in range(10):
+                fn(copies[i % len(copies)])
+        t = _time(g.replay, args.reps) / 10
+        del g
+        return t * 1e3
+
+    for name, R, K in shapes:
+        if args.only and name not in args.only.split(","):
+            continue
+        ws0 = wgemm.dense_fp8(torch.randn(R, K, device=dev) * 0.02)
+        n = max(1, min(10, -(-(256 << 20) // ws0.nbytes())))
+        copies = [ws0] + [wgemm.WeightSet(ws0.blob.clone(), ws0.exp_off, ws0.exp_fmt, R, K, ws0.fmts)
+                          for _ in range(n - 1)]
+        for c in copies:
+            c.f8_operands()
+        x = torch.randn(T, K, device=dev).half()
+        out = torch.empty(T, R, device=dev)
+        nt_old, ks_old = wgemm.dense_plan(T, ws0)
+        t_old = graph_us(lambda w: wgemm.matmul(x, w, out=out, n_tile=nt_old, k_splits=ks_old), copies)
+        t_f8 = graph_us(lambda w: wgemm.f8_linear(x, w, out), copies)
+        nt, s = wgemm.f8_plan(T, ws0)
+        b = R * K
         sweep = {}
         if args.sweep:
-            for nt in (16, 32, 64):
-                for ks in (1, 2, 4, 8, 16):
-                    if ks <= K // 128:
-                        gs = torch.cuda.CUDAGraph()
-                        wgemm.matmul(x, ws, out=out, n_tile=nt, k_splits=ks)
-                        with torch.cuda.graph(gs):
-                            for _ in range(10):
-                                wgemm.matmul(x, ws, out=out, n_tile=nt, k_splits=ks)
-                        sweep[f"n{nt}_k{ks}"] = round(100 * _time(gs.replay, args.reps), 1)
-                        del gs
-        print(json.dumps({"case": name, "rows": R, "K": K, "tokens": T, "ms": round(t, 4),
-                          "graph_us": round(t_graph * 1e3, 1), "MB": round(b / 1e6, 2),
-                          "GBps": round(b / t_graph / 1e6, 1), "sweep_us": sweep}))
+            for ss in range(1, 9):
+                if ss <= K // 128:
+                    sweep[f"s{ss}"] = round(graph_us(lambda w: wgemm.f8_linear(x, w, out, nt=nt, splits=ss),
+                                                     copies), 1)
+        print(json.dumps({"case": name, "rows": R, "K": K, "tokens": T, "weight_MB": round(b / 1e6, 2),
+                          "f16_dequant_us": round(t_old, 1), "f8_us": round(t_f8, 1), "f8_plan": [nt, s],
+                          "f8_GBps": round(b / t_f8 / 1e3, 1), "f8_sweep_us": sweep}))
     native.check_error()
 
 

@@ -31,6 +31,7 @@ class WeightSet:
     fmts: tuple                 # python copy of exp_fmt
     silu_pairs: bool = False    # rows are [gate; up] permuted for the silu*up epilogue
     _dense_cache: dict = None
+    _f8: tuple = None           # (e4m3 row-major codes, block scales) for the kind::f8f6f4 dense GEMM
 
     @property
     def row_tiles(self) -> int:
@@ -54,6 +55,14 @@ class WeightSet:
     def to(self, device):
         return WeightSet(self.blob.to(device), self.exp_off.to(device), self.exp_fmt.to(device), self.rows,
                          self.K, self.fmts, self.silu_pairs)
+
+    def f8_operands(self):
+        """Row-major e4m3 codes [row_tiles*128, K] and fp32 scales [row_tiles, KG] of a dense FP8 set (cached)."""
+        if self._f8 is None:
+            n = self.row_tiles * self.kg * rt.block_bytes(8)
+            blob = self.blob[:n].view(self.row_tiles, self.kg, rt.block_bytes(8))
+            self._f8 = rt.fp8_rowmajor(blob, self.rows, self.K)
+        return self._f8
 
     # ------------------------------------------------------------------ reference dequant
     def dense(self, e: int = 0) -> torch.Tensor:
@@ -132,6 +141,51 @@ def dense_plan(T: int, ws: WeightSet):
     return ns[-1], min(8, ws.kg)
 
 
+F8_DENSE = __import__("os").environ.get("FW_DENSE_F8", "1") != "0"   # dense FP8 sets on kind::f8f6f4
+F8_MAX_SPLITS = 8           # cluster size along K (portable limit)
+F8_SMS = 148
+
+
+def f8_plan(T: int, ws: WeightSet):
+    """(token tile, K splits) of the FP8 dense GEMM: the narrowest of 32/64/128 tokens that holds T (all of a
+    decode batch in one tile, so the weights stream once), then as many K splits (a cluster of CTAs per row tile,
+    reduced in distributed shared memory) as keep the grid within one wave of the SMs."""
+    nt = 32 if T <= 32 else 64 if T <= 64 else 128
+    units = ws.row_tiles * ((T + nt - 1) // nt)
+    s = max(1, min(F8_MAX_SPLITS, ws.kg, F8_SMS // max(1, units)))
+    return nt, s
+
+
+def f8_ok(ws: WeightSet, fan) -> bool:
+    return F8_DENSE and fan is None and ws.fmts == (8,)
+
+
+def f8_linear(x: torch.Tensor, ws: WeightSet, out: torch.Tensor, epi: int = EPI_STORE, accumulate=False,
+              alpha=1.0, nt: int = 0, splits: int = 0) -> torch.Tensor:
+    """Dense FP8 GEMM on tcgen05 `kind::f8f6f4` (csrc/k_f8gemm.cu): x [T, K] quantized per (token, 128-column
+    group) to e4m3, weights read as their e4m3 codes. Two launches (quantize, GEMM)."""
+    w8, sc = ws.f8_operands()
+    if not nt or not splits:
+        p_nt, p_s = f8_plan(x.shape[0], ws)
+        nt, splits = nt or p_nt, splits or p_s
+    native.C().f8_linear(x.contiguous(), w8, sc, ws.rows, out, epi, accumulate, alpha, nt, splits,
+                         native.err_word(x.device), native.DEFAULT_TIMEOUT_NS)
+    return out
+
+
+def f8_reference(x: torch.Tensor, ws: WeightSet, epi: int = EPI_STORE) -> torch.Tensor:
+    """fp32 emulation of :func:`f8_linear`: the same per-group e4m3 activation codes and scales, exact products,
+    fp32 sums (differs from the kernel only in the order of the fp32 additions)."""
+    T, K = x.shape
+    xg = x.float().view(T, K // 128, 128)
+    amax = xg.abs().amax(-1, keepdim=True)
+    inv = torch.where(amax > 0, 448.0 / amax, torch.zeros_like(amax))
+    x8 = (xg * inv).clamp(-448, 448).to(torch.float8_e4m3fn).float()
+    xq = (x8 * (amax / 448.0)).view(T, K)
+    w = ws.dense(0) if not x.is_cuda else ws.dense(0).to(x.device)
+    return _ref_apply(xq @ w.t(), epi)
+
+
 def matmul(x16: torch.Tensor, ws: WeightSet, out: torch.Tensor = None, epi: int = EPI_STORE,
            out_dtype=torch.float32, accumulate=False, alpha=1.0, n_tile=None, k_splits: int = 0,
            fan=None) -> torch.Tensor:
@@ -148,6 +202,8 @@ def matmul(x16: torch.Tensor, ws: WeightSet, out: torch.Tensor = None, epi: int 
         else:
             out.copy_(y.to(out.dtype))
         return out
+    if f8_ok(ws, fan) and n_tile is None and k_splits == 0:
+        return f8_linear(x16, ws, out, epi, accumulate, alpha)
     if n_tile is None and k_splits == 0 and not _OLD_DENSE_PLAN:
         n_tile, k_splits = dense_plan(T, ws)
     n = n_tile or dense_n_tile(T, ws)

@@ -77,7 +77,7 @@ def test_quantized_allreduce_wait_times_out_with_error_code():
     x = torch.randn(n, device=dev)
     h = torch.ones(n, device=dev)
     native.err_word(dev).zero_()
-    native.C().tp_qar(x, h, n, bases, 0, n, G, epoch, native.err_word(dev), 50_000_000)
+    native.C().tp_qar(x, h, n, bases, 0, n, G, epoch, native.err_word(dev), 50_000_000, 8, False, None)
     torch.cuda.synchronize()
     with pytest.raises(native.DeviceWaitTimeout, match="6411"):
         native.check_error(dev)
