@@ -22,8 +22,10 @@
 // contiguous range of groups; their partial tiles meet in distributed shared memory and CTA c sums token rows
 // [c*NT/S, (c+1)*NT/S) over the S partials in cluster-rank order (a fixed order: the bits do not depend on
 // timing) and runs the store or silu(gate)*up epilogue. No workspace, no second launch, no atomics.
-// Every mbarrier wait is bounded (%globaltimer); a timeout records an error code, the CTA waits (bounded) for its
-// copies and MMAs in flight, frees its TMEM and leaves without storing.
+// The GEMM is launched with programmatic stream serialization behind its activation quantizer: the CTA's prologue
+// and its first weight stages overlap the quantizer, and only the activation tiles and scales wait for it
+// (griddepcontrol.wait). Every mbarrier wait is bounded (%globaltimer); a timeout records an error code, the CTA
+// waits (bounded) for its copies and MMAs in flight, frees its TMEM and leaves without storing.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -189,7 +191,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int i = 0; i < n_kb; ++i) {
+      // The weights do not depend on the previous kernel (the activation quantizer): their first stages are in
+      // flight before the wait for its results, the activation tiles of those stages follow it.
+      const int pre = n_kb < C::kStages ? n_kb : C::kStages;
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(full(i), C::kStageBytes);
+        tma_load_2d(base + i * C::kStageBytes, &wmap, (kb0 + i) * 128, rb * 128, full(i));
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(base + i * C::kStageBytes + kWBytes, &xmap, (kb0 + i) * 128, tt * NT, full(i));
+      issued = pre;
+      for (int i = pre; i < n_kb; ++i) {
         const int s = i % C::kStages;
         const uint32_t ph = (uint32_t)(i / C::kStages) & 1u;
         if (!mbar_wait_sleepy(empty(s), ph ^ 1u, a.err, 7101, abort_flag, lim, 2000u)) break;
@@ -219,6 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
+    pdl_wait();                          // activation scales (and an accumulated output) come from earlier kernels
     const float* xs_base = a.xscale + tt * NT + h * (NT / 2);
     const float* ws_row = a.wscale + (size_t)rb * a.KB;
     for (int i = 0; i < n_kb; ++i) {
@@ -339,6 +353,7 @@ template <typename TIn>
 __global__ void __launch_bounds__(256) f8_quant_kernel(const TIn* __restrict__ x, int T, int KB, int x_ld,
                                                        uint8_t* __restrict__ x8, float* __restrict__ xs, int xs_ld,
                                                        int T_pad) {
+  pdl_launch_dependents();              // the GEMM may start its prologue and weight loads now
   const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   const int t = gw / KB, kb = gw % KB;
   if (t >= T_pad) return;
@@ -385,7 +400,7 @@ static int tmap_u8(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t co
 
 template <int NT>
 static int launch(const Args& a, const CUtensorMap& wm, const CUtensorMap& xm, int row_tiles, int tok_tiles,
-                  cudaStream_t st) {
+                  cudaStream_t st, bool pdl) {
   using C = Cfg<NT>;
   auto k = f8gemm_kernel<NT>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
@@ -395,13 +410,22 @@ static int launch(const Args& a, const CUtensorMap& wm, const CUtensorMap& xm, i
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::kSmem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = a.splits;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {                             // overlap the prologue and the first weight stages with the quantizer
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (a.splits > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = a.splits;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = a.splits > 1 ? 1 : 0;
+  cfg.numAttrs = na;
   e = cudaLaunchKernelEx(&cfg, k, a, wm, xm);
   return (int)(e != cudaSuccess ? e : cudaGetLastError());
 }
@@ -469,10 +493,11 @@ int64_t f8_linear(torch::Tensor x, torch::Tensor w8, torch::Tensor wscale, int64
   a.epi = (int)epi; a.accumulate = accumulate ? 1 : 0; a.alpha = (float)alpha;
   a.err = err.data_ptr<int32_t>(); a.timeout_ns = (unsigned long long)timeout_ns;
   const int rt = (int)(Rp / 128);
+  static const bool pdl = !(getenv("FW_PDL") && atoi(getenv("FW_PDL")) == 0);   // FW_PDL=0: plain launches
   int rc;
-  if (nt == 32) rc = fw::f8::launch<32>(a, wm, xm, rt, (int)tok_tiles, st);
-  else if (nt == 64) rc = fw::f8::launch<64>(a, wm, xm, rt, (int)tok_tiles, st);
-  else rc = fw::f8::launch<128>(a, wm, xm, rt, (int)tok_tiles, st);
+  if (nt == 32) rc = fw::f8::launch<32>(a, wm, xm, rt, (int)tok_tiles, st, pdl);
+  else if (nt == 64) rc = fw::f8::launch<64>(a, wm, xm, rt, (int)tok_tiles, st, pdl);
+  else rc = fw::f8::launch<128>(a, wm, xm, rt, (int)tok_tiles, st, pdl);
   TORCH_CHECK(rc == 0, "f8gemm launch failed: ", cudaGetErrorString((cudaError_t)rc));
   return 2;
 }

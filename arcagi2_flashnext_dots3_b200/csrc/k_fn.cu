@@ -424,8 +424,10 @@ __device__ void norm_rope_head(float* x, int D, const float* w, float eps, const
   __syncthreads();
 }
 
-// One block per row: q heads (norm+rope) -> q, gate copy, k heads (norm+rope) -> k cache, v -> v cache,
-// indexer q heads (norm+rope) -> iq. 256 threads, D <= 1024.
+// One block per (row, head): blockIdx.y < Hq a query head (norm+rope) -> q plus its gate copy, then the KV heads
+// (norm+rope) -> k cache with v -> v cache, then the indexer query heads (norm+rope) -> iq. 256 threads, D <= 1024.
+// The heads are independent, so each gets its own block (a block per row walked the 16-20 heads of a row in
+// series, two block-wide reductions each, and left most SMs idle at decode batch).
 template <typename KT>
 __global__ void qsa_prep_kernel(const float* proj, int ldp, const float* qn, const float* kn, const float* iqn,
                                 const float* rope, int rope_len, KT* kc, KT* vc, const int* block_table, int max_blocks,
@@ -441,8 +443,8 @@ __global__ void qsa_prep_kernel(const float* proj, int ldp, const float* qn, con
   const float* P = proj + (int64_t)row * ldp;
   const float* cs_c = rope + (int64_t)p * rdq;
   const float* cs_s = rope + (int64_t)rope_len * rdq + (int64_t)p * rdq;
-  // q + gate
-  for (int h = 0; h < Hq; ++h) {
+  int h = blockIdx.y;
+  if (h < Hq) {                                   // query head + gate
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
       xs[d] = P[h * 2 * D + d];
       gate_out[(int64_t)row * Hq * D + h * D + d] = P[h * 2 * D + D + d];
@@ -450,11 +452,12 @@ __global__ void qsa_prep_kernel(const float* proj, int ldp, const float* qn, con
     __syncthreads();
     norm_rope_head(xs, D, qn, eps, cs_c, cs_s, rdq, red);
     for (int d = threadIdx.x; d < D; d += blockDim.x) q_out[((int64_t)row * Hq + h) * D + d] = xs[d];
-    __syncthreads();
+    return;
   }
-  const int blk = block_table[(int64_t)s * max_blocks + p / bs];
-  const int64_t coff = ((int64_t)blk * bs + (p % bs)) * KV * D;
-  for (int h = 0; h < KV; ++h) {
+  h -= Hq;
+  if (h < KV) {                                   // key head (norm+rope) and value head into the paged caches
+    const int blk = block_table[(int64_t)s * max_blocks + p / bs];
+    const int64_t coff = ((int64_t)blk * bs + (p % bs)) * KV * D;
     for (int d = threadIdx.x; d < D; d += blockDim.x) xs[d] = P[Hq * 2 * D + h * D + d];
     __syncthreads();
     norm_rope_head(xs, D, kn, eps, cs_c, cs_s, rdq, red);
@@ -462,16 +465,14 @@ __global__ void qsa_prep_kernel(const float* proj, int ldp, const float* qn, con
       stf(&kc[coff + h * D + d], xs[d]);
       stf(&vc[coff + h * D + d], P[Hq * 2 * D + KV * D + h * D + d]);
     }
-    __syncthreads();
+    return;
   }
+  h -= KV;                                        // indexer query head
   const int ib = Hq * 2 * D + 2 * KV * D;
-  for (int h = 0; h < iH; ++h) {
-    for (int d = threadIdx.x; d < iD; d += blockDim.x) xs[d] = P[ib + h * iD + d];
-    __syncthreads();
-    norm_rope_head(xs, iD, iqn, eps, cs_c, cs_s, rdq, red);
-    for (int d = threadIdx.x; d < iD; d += blockDim.x) iq_out[((int64_t)row * iH + h) * iD + d] = xs[d];
-    __syncthreads();
-  }
+  for (int d = threadIdx.x; d < iD; d += blockDim.x) xs[d] = P[ib + h * iD + d];
+  __syncthreads();
+  norm_rope_head(xs, iD, iqn, eps, cs_c, cs_s, rdq, red);
+  for (int d = threadIdx.x; d < iD; d += blockDim.x) iq_out[((int64_t)row * iH + h) * iD + d] = xs[d];
 }
 
 // One block per sequence: compressed indexer keys of every block that completes within this step, from the ring
@@ -533,7 +534,7 @@ void qsa_prep(torch::Tensor proj, torch::Tensor qn, torch::Tensor kn, torch::Ten
   const int rd = rope.size(2), rope_len = rope.size(1);
   CK(D <= 1024 && iD <= 1024 && rd <= D && rd <= iD);
   const int bs = k_cache.size(1), max_blocks = block_table.size(1);
-  dim3 grid(rows);
+  dim3 grid(rows, Hq + KV + iH);
   const size_t sm = std::max(D, iD) * sizeof(float);
 #define PREP(KT)                                                                                                 \
   qsa_prep_kernel<KT><<<grid, 256, sm, STREAM>>>(                                                                \
@@ -1238,11 +1239,87 @@ __global__ void moe_route_kernel(const float* logits, int ld, int32_t* ids, floa
   }
 }
 
+// One warp per token for E <= 32 * EPL experts: lane l holds the probabilities of experts l, l + 32, ... in
+// registers, so the k selection rounds are shuffles only (the block-per-token kernel above spends two block
+// barriers per round). Same selection rule: highest probability first, ties to the lower expert id; weights
+// renormalized over the selected experts.
+template <int EPL>
+__global__ void __launch_bounds__(256) moe_route_warp_kernel(const float* logits, int ld, int T, int32_t* ids,
+                                                             float* w, int E, int k) {
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const float* x = logits + (int64_t)t * ld;
+  float p[EPL];
+  float mx = -FLT_MAX;
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    p[i] = e < E ? x[e] : -FLT_MAX;
+    mx = fmaxf(mx, p[i]);
+  }
+  mx = warp_max(mx);
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    float v = e < E ? __expf(p[i] - mx) : -1.f;
+    if (e < E && !(v >= 0.f)) v = 0.f;   // NaN logits must still yield valid expert ids below
+    p[i] = v;
+    sum += e < E ? v : 0.f;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  float wsum = 0.f;
+  for (int j = 0; j < k; ++j) {
+    float bv = -1.f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = lane + 32 * i;
+      if (p[i] > bv || (p[i] == bv && e < bi)) {
+        bv = p[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < EPL; ++i)
+      if (lane + 32 * i == bi) p[i] = -2.f;
+    if (lane == 0) {
+      ids[t * k + j] = bi;
+      w[t * k + j] = bv / sum;
+    }
+    wsum += bv / sum;
+  }
+  if (lane == 0)
+    for (int j = 0; j < k; ++j) w[t * k + j] /= wsum;
+}
+
 void moe_route(torch::Tensor logits, torch::Tensor ids, torch::Tensor w, int64_t E, int64_t k) {
   const int T = logits.size(0);
   if (!T) return;
-  moe_route_kernel<<<T, 256, E * sizeof(float), STREAM>>>(logits.data_ptr<float>(), logits.size(1),
-                                                          ids.data_ptr<int32_t>(), w.data_ptr<float>(), E, k);
+  const int ld = logits.size(1);
+  const int grid = (T + 7) / 8;
+  if (E <= 128)
+    moe_route_warp_kernel<4><<<grid, 256, 0, STREAM>>>(logits.data_ptr<float>(), ld, T, ids.data_ptr<int32_t>(),
+                                                       w.data_ptr<float>(), E, k);
+  else if (E <= 256)
+    moe_route_warp_kernel<8><<<grid, 256, 0, STREAM>>>(logits.data_ptr<float>(), ld, T, ids.data_ptr<int32_t>(),
+                                                       w.data_ptr<float>(), E, k);
+  else if (E <= 512)
+    moe_route_warp_kernel<16><<<grid, 256, 0, STREAM>>>(logits.data_ptr<float>(), ld, T, ids.data_ptr<int32_t>(),
+                                                        w.data_ptr<float>(), E, k);
+  else
+    moe_route_kernel<<<T, 256, E * sizeof(float), STREAM>>>(logits.data_ptr<float>(), ld, ids.data_ptr<int32_t>(),
+                                                            w.data_ptr<float>(), E, k);
 }
 
 // Stable expert sort of the T*k pairs and the tile item list, in one block of 1024 threads.

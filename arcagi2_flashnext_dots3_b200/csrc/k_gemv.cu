@@ -24,6 +24,7 @@
 #include <cuda_fp16.h>
 #include "wgemm.h"
 #include "ptx.cuh"
+#include "lowbit.cuh"
 
 namespace {
 
@@ -34,6 +35,7 @@ constexpr int kMaxK = 8192;   // longest activation row staged in shared memory 
 // ------------------------------------------------------------------------------------ activation quantization
 // One warp per (row, 128-column group): lane l owns columns 4l..4l+3.
 __global__ void gemv_quant_kernel(const __half* x, int rows, int K, int8_t* xq, float* xs, int* xsum) {
+  fw::pdl_launch_dependents();   // the grouped GEMV that follows may launch now (it waits for these results)
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int G = K / 128;
   if (warp >= rows * G) return;
@@ -58,31 +60,8 @@ __global__ void gemv_quant_kernel(const __half* x, int rows, int K, int8_t* xq, 
   }
 }
 
-// ------------------------------------------------------------------------------------ code extraction
-// quad<FMT>(w, m): codes of block-row columns 4m..4m+3 as bytes in natural order (m = 0..31, compile-time).
-template <int FMT, int M>
-__device__ __forceinline__ uint32_t quad(const uint32_t* w) {
-  if constexpr (FMT == 4) {
-    // word i = columns 8i..8i+7: pairs 4i+k in bits 4k (even col) and 16+4k (odd col)
-    const uint32_t x = w[M / 2];
-    const uint32_t A = x & 0x0F0F0F0Fu;          // [c0, c4, c1, c5]
-    const uint32_t B = (x >> 4) & 0x0F0F0F0Fu;   // [c2, c6, c3, c7]
-    return (M & 1) ? __byte_perm(A, B, 0x7531) : __byte_perm(A, B, 0x6420);
-  } else {
-    // pairs in bits BITS*k (even col) and 16+BITS*k (odd col), PPW pairs per word
-    constexpr int BITS = FMT, PPW = FMT == 3 ? 5 : 8;
-    constexpr uint32_t MASK = ((1u << BITS) - 1u) * 0x00010001u;
-    constexpr int p0 = 2 * M, p1 = 2 * M + 1;
-    const uint32_t P0 = (w[p0 / PPW] >> (BITS * (p0 % PPW))) & MASK;   // [c_{2p0}, 0, c_{2p0+1}, 0]
-    const uint32_t P1 = (w[p1 / PPW] >> (BITS * (p1 % PPW))) & MASK;
-    return __byte_perm(P0, P1, 0x6420);
-  }
-}
-
-template <int FMT>
-struct NWords {
-  static constexpr int value = FMT == 4 ? 16 : FMT == 3 ? 13 : 8;
-};
+using fw::lowbit::NWords;
+using fw::lowbit::quad;
 
 // dot[t] += sum over the 128 columns of group g of codes * x[t] for NT tokens (activations from shared memory,
 // 16 bytes = 4 quads per load, the same address for every thread: a broadcast).
@@ -202,6 +181,7 @@ __global__ void __launch_bounds__(128, MINB) gemv_grouped_kernel(GemvArgs a) {
   __shared__ float gsh[kMaxTok * 64];
   __shared__ float xs_sm[kMaxTok * (kMaxK / 128)];
   __shared__ int xsum_sm[kMaxTok * (kMaxK / 128)];
+  fw::pdl_wait();                // launched early behind gemv_quant: its activations must be complete
   const int n_items = min(*a.n_items, a.max_items);
   const int total = n_items * a.row_tiles;
   const int Kw = a.kg * 32;
@@ -505,9 +485,23 @@ void gemv_grouped(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_
     return;
   }
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(work, (int64_t)sms * 12));
-  if (occ >= 8) gemv_grouped_kernel<8><<<grid, 128, smem, STREAM>>>(a);
-  else if (occ == 6) gemv_grouped_kernel<6><<<grid, 128, smem, STREAM>>>(a);
-  else gemv_grouped_kernel<5><<<grid, 128, smem, STREAM>>>(a);
+  // programmatic launch behind gemv_quant (FW_PDL=0: plain launch)
+  static const bool pdl = !(getenv("FW_PDL") && atoi(getenv("FW_PDL")) == 0);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = STREAM;
+  cudaLaunchAttribute la[1];
+  la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  la[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = la;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e;
+  if (occ >= 8) e = cudaLaunchKernelEx(&cfg, gemv_grouped_kernel<8>, a);
+  else if (occ == 6) e = cudaLaunchKernelEx(&cfg, gemv_grouped_kernel<6>, a);
+  else e = cudaLaunchKernelEx(&cfg, gemv_grouped_kernel<5>, a);
+  TORCH_CHECK(e == cudaSuccess, "gemv_grouped launch failed: ", cudaGetErrorString(e));
 }
 
 }  // namespace

@@ -15,6 +15,7 @@ void register_tp(pybind11::module& m);
 void register_mla(pybind11::module& m);
 void register_dsa(pybind11::module& m);
 void register_f8gemm(pybind11::module& m);
+void register_moe_i8(pybind11::module& m);
 
 void register_kernels(pybind11::module& m) {
   register_fn(m);
@@ -28,4 +29,5 @@ void register_kernels(pybind11::module& m) {
   register_mla(m);
   register_dsa(m);
   register_f8gemm(m);
+  register_moe_i8(m);
 }

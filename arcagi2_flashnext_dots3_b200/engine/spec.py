@@ -281,7 +281,7 @@ class SpecDecoder:
         steps = [len(s.out) for s in seqs]        # index of the first token this verify emits
         if getattr(m, "vocab_sharded", False):
             from ..parallel.tp import sharded_speculative_accept
-            lg = m._mm(x, m.W["lm_head"]).float().view(len(seqs), k1, -1)
+            lg = m._mm(x, m.W["lm_head"], f8=False).float().view(len(seqs), k1, -1)
             return sharded_speculative_accept(lg, m.W["vocab_range"][0], dr, temps, seeds, steps, m.tp.group)
         lg = m.logits(x).float().view(len(seqs), k1, -1)
         return sampling.speculative_accept(lg, dr, temps, seeds, steps)

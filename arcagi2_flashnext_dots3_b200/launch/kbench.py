@@ -65,11 +65,17 @@ def bench_moe(args):
     mi8 = (P + 7) // 8 + E
     pp8, items8, n8 = ops.moe_plan(ids, E, 8, mi8)
     xs8 = ops.moe_scatter(x, pp8)
-    t_gu8 = _time(lambda: wgemm.gemv_grouped(xs8, gu, items8, n8, mi8, act, epi=wgemm.EPI_SILU_MUL), args.reps)
-    t_d8 = _time(lambda: wgemm.gemv_grouped(act, d, items8, n8, mi8, yp), args.reps)
+    t_gu8 = _time(lambda: wgemm.gemv_grouped(xs8, gu, items8, n8, mi8, act, epi=wgemm.EPI_SILU_MUL, kernel="dp4a"),
+                  args.reps)
+    t_d8 = _time(lambda: wgemm.gemv_grouped(act, d, items8, n8, mi8, yp, kernel="dp4a"), args.reps)
+    # tcgen05 kind::i8 on the same plan
+    t_gui = _time(lambda: wgemm.gemv_grouped(xs8, gu, items8, n8, mi8, act, epi=wgemm.EPI_SILU_MUL, kernel="i8"),
+                  args.reps)
+    t_di = _time(lambda: wgemm.gemv_grouped(act, d, items8, n8, mi8, yp, kernel="i8"), args.reps)
     native.check_error()
     for name, t, b in (("moe_gate_up", t_gu, bytes_gu), ("moe_down", t_d, bytes_d),
-                       ("moe_gate_up_gemv", t_gu8, bytes_gu), ("moe_down_gemv", t_d8, bytes_d)):
+                       ("moe_gate_up_gemv", t_gu8, bytes_gu), ("moe_down_gemv", t_d8, bytes_d),
+                       ("moe_gate_up_i8", t_gui, bytes_gu), ("moe_down_i8", t_di, bytes_d)):
         print(json.dumps({"case": name, "tokens": T, "experts": E, "touched": len(touched), "n_tile": n_tile,
                           "ms": round(t, 4), "MB": round(b / 1e6, 1), "GBps": round(b / t / 1e6, 1)}))
 

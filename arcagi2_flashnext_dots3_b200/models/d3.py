@@ -78,10 +78,10 @@ class D3Model:
         self.index_shard = (tp.world, tp.rank) if (tp is not None and cfg.shard_index) else (1, 0)
         self.overlap = None     # utils.observe.TopkOverlap: per-step top-k overlap between DSA layers (eval only)
 
-    def _mm(self, x, ws, epi=wgemm.EPI_STORE, out_dtype=torch.float32):
+    def _mm(self, x, ws, epi=wgemm.EPI_STORE, out_dtype=torch.float32, f8=True):
         if not x.is_cuda:
             return wgemm.matmul(x.float(), ws, epi=epi, out_dtype=torch.float32)
-        return wgemm.matmul(x, ws, epi=epi, out_dtype=out_dtype)
+        return wgemm.matmul(x, ws, epi=epi, out_dtype=out_dtype, f8=f8)
 
     def _head_items(self, H: int, T: int, n_tile: int):
         """Grouped-GEMM plan with one expert per head: items (h, first row h*T + s, count, 0) over n_tile chunks."""
@@ -246,13 +246,13 @@ class D3Model:
         holds only a slice whose indices are not token ids: use :meth:`pick`."""
         if self.vocab_sharded:
             raise RuntimeError("D3Model.logits: the LM head is vocabulary-sharded; select tokens with pick()")
-        return self._mm(x, self.W["lm_head"])
+        return self._mm(x, self.W["lm_head"], f8=False)
 
     def pick(self, x: torch.Tensor, temperature: float = 0.0, seed: int = 0, step: int = 0) -> torch.Tensor:
         """Next token per row (int32): greedy, or Gumbel-max temperature sampling with the sampler's counter RNG.
         With the LM head split over the TP ranks (``vocab_range`` in the weights) only one (value, index) pair
         per row crosses the group."""
-        lg = self._mm(x, self.W["lm_head"])
+        lg = self._mm(x, self.W["lm_head"], f8=False)
         if self.vocab_sharded:
             if getattr(self.tp, "fake", False):
                 return self.tp.sharded_pick(lg, self.W["vocab_range"][0], temperature, seed, step)

@@ -111,10 +111,10 @@ class FNModel:
             d[l] = len(d)
 
     # ------------------------------------------------------------------------------------------ pieces
-    def _mm(self, x, ws, epi=wgemm.EPI_STORE, out_dtype=torch.float32):
+    def _mm(self, x, ws, epi=wgemm.EPI_STORE, out_dtype=torch.float32, f8=True):
         if not x.is_cuda:
             return wgemm.matmul(x.float(), ws, epi=epi, out_dtype=torch.float32)
-        return wgemm.matmul(x, ws, epi=epi, out_dtype=out_dtype)
+        return wgemm.matmul(x, ws, epi=epi, out_dtype=out_dtype, f8=f8)
 
     def _hc(self, h, p, with_inj=True):
         cfg = self.cfg
@@ -256,7 +256,7 @@ class FNModel:
         return x
 
     def logits(self, x: torch.Tensor) -> torch.Tensor:
-        return self._mm(x, self.W["lm_head"])
+        return self._mm(x, self.W["lm_head"], f8=False)
 
     # --------------------------------------------------------------------------------------- helpers
     def assign_blocks(self, slot: int, n_tokens: int, allocator):

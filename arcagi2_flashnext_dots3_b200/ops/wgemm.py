@@ -179,7 +179,9 @@ def f8_reference(x: torch.Tensor, ws: WeightSet, epi: int = EPI_STORE) -> torch.
     T, K = x.shape
     xg = x.float().view(T, K // 128, 128)
     amax = xg.abs().amax(-1, keepdim=True)
-    inv = torch.where(amax > 0, 448.0 / amax, torch.zeros_like(amax))
+    # a tensor / tensor division rounds once, as the kernel's 448.f / m does (torch evaluates 448.0 / amax as
+    # reciprocal(amax) * 448, which rounds twice and now and then moves a code across an e4m3 rounding boundary)
+    inv = torch.where(amax > 0, torch.full_like(amax, 448.0) / amax, torch.zeros_like(amax))
     x8 = (xg * inv).clamp(-448, 448).to(torch.float8_e4m3fn).float()
     xq = (x8 * (amax / 448.0)).view(T, K)
     w = ws.dense(0) if not x.is_cuda else ws.dense(0).to(x.device)
@@ -188,8 +190,11 @@ def f8_reference(x: torch.Tensor, ws: WeightSet, epi: int = EPI_STORE) -> torch.
 
 def matmul(x16: torch.Tensor, ws: WeightSet, out: torch.Tensor = None, epi: int = EPI_STORE,
            out_dtype=torch.float32, accumulate=False, alpha=1.0, n_tile=None, k_splits: int = 0,
-           fan=None) -> torch.Tensor:
-    """Dense y = x @ W^T (or silu(gate)*up for a silu_pairs weight). x16: fp16 [T, K]."""
+           fan=None, f8: bool = True) -> torch.Tensor:
+    """Dense y = x @ W^T (or silu(gate)*up for a silu_pairs weight). x16: fp16 [T, K]. FP8 weight sets run on the
+    kind::f8f6f4 GEMM with e4m3 activations unless ``f8`` is False (or a launch plan is given): then the weights
+    are dequantized to fp16 for the kind::f16 GEMM and the activations keep fp16 (the LM heads use this, so
+    argmax and sampling see unquantized activations)."""
     T = x16.shape[0]
     cols = ws.rows // 2 if epi == EPI_SILU_MUL else ws.rows
     if out is None:
@@ -202,7 +207,7 @@ def matmul(x16: torch.Tensor, ws: WeightSet, out: torch.Tensor = None, epi: int 
         else:
             out.copy_(y.to(out.dtype))
         return out
-    if f8_ok(ws, fan) and n_tile is None and k_splits == 0:
+    if f8 and f8_ok(ws, fan) and n_tile is None and k_splits == 0:
         return f8_linear(x16, ws, out, epi, accumulate, alpha)
     if n_tile is None and k_splits == 0 and not _OLD_DENSE_PLAN:
         n_tile, k_splits = dense_plan(T, ws)
@@ -235,23 +240,39 @@ def grouped(xs16: torch.Tensor, ws: WeightSet, items: torch.Tensor, n_items: tor
 GEMV_MAX_TOK = 8  # items of at most this many tokens can run on the CUDA-core grouped GEMV (csrc/k_gemv.cu)
 
 
+MOE_I8 = __import__("os").environ.get("FW_MOE_I8", "0") == "1"   # decode MoE on tcgen05 kind::i8 (csrc/k_moe_i8.cu)
+
+
+def moe_decode_desc() -> str:
+    """The decode MoE experts' compute path, as the benchmark reports it."""
+    return ("4/3-bit codes x int8 activations (per 128-column group) on tcgen05 kind::i8, int32 accumulate per "
+            "group, fp32 scale folds" if MOE_I8 else
+            "4/3-bit codes x int8 activations (per 128-column group) on dp4a, fp32 accumulate")
+
+
 def gemv_grouped(xs16: torch.Tensor, ws: WeightSet, items: torch.Tensor, n_items: torch.Tensor, max_items: int,
-                 out: torch.Tensor, epi: int = EPI_STORE, row_dst: torch.Tensor = None) -> torch.Tensor:
+                 out: torch.Tensor, epi: int = EPI_STORE, row_dst: torch.Tensor = None, kernel: str = "auto"
+                 ) -> torch.Tensor:
     """Same contract as :func:`grouped` for plans built with n_tile <= 8 (decode-sized expert groups): activations
     are quantized to int8 per 128-column group, then every item (expert, first row, count <= 8) is computed by
-    integer dot products straight from the packed codes (csrc/k_gemv.cu)."""
+    integer dot products straight from the packed codes. ``kernel``: "dp4a" = the CUDA-core GEMV (csrc/k_gemv.cu),
+    "i8" = tcgen05 kind::i8 MMA with the widened codes in tensor memory (csrc/k_moe_i8.cu), "auto" = the one
+    FW_MOE_I8 selects; both give the same bits."""
     cols = ws.rows // 2 if epi == EPI_SILU_MUL else ws.rows
     if not xs16.is_cuda:
         return grouped(xs16, ws, items, n_items, max_items, out, epi=epi, row_dst=row_dst)
     if any(f > 4 for f in ws.fmts):
         raise ValueError("the grouped GEMV handles 2/3/4-bit experts only")
+    use_i8 = kernel == "i8" or (kernel == "auto" and MOE_I8)
     R, K = xs16.shape
-    xq = torch.empty(R, K, dtype=torch.int8, device=xs16.device)
-    xsc = torch.empty(R, K // 128, dtype=torch.float32, device=xs16.device)
-    xsum = torch.empty(R, K // 128, dtype=torch.int32, device=xs16.device)
+    Rq = max(R, 16) if use_i8 else R      # the MMA's 16-row activation box may reach past the last pair
+    xq = torch.empty(Rq, K, dtype=torch.int8, device=xs16.device)
+    xsc = torch.empty(Rq, K // 128, dtype=torch.float32, device=xs16.device)
+    xsum = torch.empty(Rq, K // 128, dtype=torch.int32, device=xs16.device)
     native.C().gemv_quant(xs16, xq, xsc, xsum)
-    native.C().gemv_grouped(ws.blob, ws.exp_off, ws.exp_fmt, ws.row_tiles, ws.kg, items, n_items, max_items, xq, xsc,
-                            xsum, out, cols, epi, row_dst, native.err_word(xs16.device), native.DEFAULT_TIMEOUT_NS)
+    fn = native.C().moe_i8 if use_i8 else native.C().gemv_grouped
+    fn(ws.blob, ws.exp_off, ws.exp_fmt, ws.row_tiles, ws.kg, items, n_items, max_items, xq, xsc, xsum, out, cols,
+       epi, row_dst, native.err_word(xs16.device), native.DEFAULT_TIMEOUT_NS)
     return out
 
 

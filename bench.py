@@ -1,11 +1,12 @@
 #!/usr/bin/env python
 """Headline benchmark: generated tokens/s of Flash-Next-shaped 3/4-bit MoE decode on N B200s (max over ranks).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--global-batch B]
 
 For N > 1 launch with torchrun (one rank per GPU). Each rank serves `--batch` concurrent sequences whose caches
 hold synthetic 6k-12k-token contexts (random-init weights of the full architecture, random cache state of those
-lengths: prefill is outside the measured decode metric). Rank 0 prints one JSON line.
+lengths: prefill is outside the measured decode metric). Rank 0 prints one JSON line. `--global-batch B` switches
+to strong scaling: B sequences in total (B / N per rank), e.g. 64 over 8 GPUs for the TPxEP-8 serving config.
 
 * value: device time of K decode steps (CUDA events around K replays of the captured decode graph = all 48
   layers + LM head + argmax), max over ranks; tokens/s = N * batch / step time.
@@ -88,8 +89,8 @@ def count_launches(model, step_fn):
 
         def wrap(*a, _f=f, _n=n, **k):
             r = _f(*a, **k)
-            # wgemm reports how many kernels it launched (a split-K GEMM adds its reduce launch)
-            counts[_n] = counts.get(_n, 0) + (r if _n == "wgemm" and isinstance(r, int) else 1)
+            # wgemm and f8_linear report how many kernels they launched (a split-K reduce, the activation quantizer)
+            counts[_n] = counts.get(_n, 0) + (r if _n in ("wgemm", "f8_linear") and isinstance(r, int) else 1)
             return r
         setattr(C, n, wrap)
     try:
@@ -106,7 +107,9 @@ def main():
     ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--batch", type=int, default=64, help="sequences per rank (weak scaling)")
+    ap.add_argument("--global-batch", type=int, default=0,
+                    help="strong scaling: this many sequences in total, split evenly over the ranks (overrides --batch)")
     ap.add_argument("--ctx-min", type=int, default=6144)
     ap.add_argument("--ctx-max", type=int, default=12288)
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
@@ -124,13 +127,18 @@ def main():
     from arcagi2_flashnext_dots3_b200.config import EngineConfig, fn_config
     from arcagi2_flashnext_dots3_b200.engine.llm import LLM, DecodeGraph
     from arcagi2_flashnext_dots3_b200.models.fn_weights import engine_bytes, random_engine
-    from arcagi2_flashnext_dots3_b200.ops import native
+    from arcagi2_flashnext_dots3_b200.ops import native, wgemm
     from arcagi2_flashnext_dots3_b200.parallel.ep import EPGroup
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
+    scaling = "weak"
+    if args.global_batch:
+        if args.global_batch % world:
+            raise SystemExit(f"--global-batch {args.global_batch} is not a multiple of {world} ranks")
+        args.batch, scaling = args.global_batch // world, "strong"
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
@@ -222,13 +230,16 @@ def main():
     total_batch = args.batch * world
     value = total_batch / (ms / 1000)
     e2e_value = e2e_tok_step * world / (e2e_ms / 1000)
+    F8 = wgemm.F8_DENSE
+    MOE_DESC = wgemm.moe_decode_desc()
     if rank == 0:
         out = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": K,
-            "warmup": Wm, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "warmup": Wm, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": scaling,
             "vs_baseline": round(value / BASELINE_TOKS, 3),
-            "dtype": "fp16 activations x fp8 weights (dense); int8 activations per 128-column group x 4/3-bit "
-                     "weights (decode MoE); fp32 accumulation",
+            "dtype": ("e4m3 activations per (token, 128-column group) x e4m3 weights (dense)" if F8 else
+                      "fp16 activations x fp8 weights (dense)") + "; int8 activations per 128-column group x "
+                     "4/3-bit weights (decode MoE); fp32 accumulation; LM head fp16 activations x fp8 weights",
             "data": "synthetic (random-init weights N(0,0.02); random cache state for 6k-12k-token contexts)",
             "config": {"model": f"flashnext-shaped {cfg.num_layers}L h{cfg.hidden_size} {cfg.n_experts}/"
                                  f"{cfg.n_experts_orig} experts top-{cfg.top_k} 4/3-bit g128 + FP8 128x128 dense",
@@ -239,10 +250,9 @@ def main():
                        "l2": "inputs larger than L2 (weights streamed per step >> 126 MB)",
                        "ple": f"layers {list(cfg.ple_layers)}, {cfg.ple_rows // 10**6}M x {cfg.ple_dim} fp8 n-gram table",
                        "mtp": "off (no speculative decoding in this measurement)",
-                       "compute": ("dense projections: fp16 tcgen05 MMA, fp32 accumulate; decode MoE experts: "
-                                   "4/3-bit codes x int8 activations (per 128-column group) on dp4a, fp32 "
-                                   "accumulate" if os.environ.get("FW_MOE_GEMV", "1") != "0" else
-                                   "fp16 tcgen05 MMA, fp32 accumulate; activations fp16/fp32"),
+                       "compute": (("dense projections: tcgen05 kind::f8f6f4 (e4m3 x e4m3, per-group scales in "
+                                    "the epilogue)" if F8 else "dense projections: fp16 tcgen05 MMA") +
+                                   ", fp32 accumulate; decode MoE experts: " + MOE_DESC),
                        "valid": not args.layers},
             "p50_tpot_ms": round(p50, 3),
             "clocks": clk,

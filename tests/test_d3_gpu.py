@@ -42,7 +42,7 @@ def test_d3_engine_gpu_vs_cpu():
     b = _run("cuda", cfg, W, ids)
     for x, y in zip(a, b):
         err = (x - y).abs().max() / x.abs().max()
-        assert err < 3e-2, err
+        assert err < 5e-2, err   # the GPU's dense GEMMs quantize activations to e4m3 per 128-column group
 
 
 def test_d3_llm_greedy_matches_oracle_prefix():
@@ -69,4 +69,4 @@ def test_d3_index_share_gpu_vs_cpu():
     a = _run("cpu", cfg, W, ids)
     b = _run("cuda", cfg, W, ids)
     err = (a[0] - b[0]).abs().max() / a[0].abs().max()
-    assert err < 3e-2, err
+    assert err < 5e-2, err   # e4m3 activations in the GPU's dense GEMMs (the CPU path keeps fp32)

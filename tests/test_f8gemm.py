@@ -1,6 +1,12 @@
-"""Dense FP8 GEMM on tcgen05 kind::f8f6f4 (csrc/k_f8gemm.cu) against fp32 references of the same op."""
+"""Dense FP8 GEMM on tcgen05 kind::f8f6f4 (csrc/k_f8gemm.cu) against fp32 references of the same op.
+
+`f8_reference` forms the same e4m3 codes and exact products but sums them in fp32 in another order, so the two
+agree to fp32 rounding (EMU_TOL, relative to the output's scale). On integer data with exact codes the kernel
+must match exactly (`test_f8_linear_exact_on_integers`)."""
 import pytest
 import torch
+
+EMU_TOL = 1e-4
 
 from arcagi2_flashnext_dots3_b200.formats import runtime as rt
 from arcagi2_flashnext_dots3_b200.ops import wgemm
@@ -55,7 +61,7 @@ def test_f8_linear_store(T, R, K):
     torch.cuda.synchronize()
     ref = wgemm.f8_reference(x, ws)
     err = ((out - ref).abs().max() / ref.abs().max()).item()
-    assert err < 1e-3, err
+    assert err < EMU_TOL, err
     full = x.float() @ ws.dense(0).t()
     assert ((out - full).abs().max() / full.abs().max()).item() < 0.05
 
@@ -69,7 +75,7 @@ def test_f8_linear_splits_same_values(splits):
     out = torch.empty(64, 512, device=dev)
     wgemm.f8_linear(x, ws, out, nt=64, splits=splits)
     ref = wgemm.f8_reference(x, ws)
-    assert ((out - ref).abs().max() / ref.abs().max()).item() < 1e-3
+    assert ((out - ref).abs().max() / ref.abs().max()).item() < EMU_TOL
     again = torch.empty_like(out)
     wgemm.f8_linear(x, ws, again, nt=64, splits=splits)
     assert torch.equal(out, again)                   # fixed reduction order: identical bits
@@ -96,6 +102,32 @@ def test_f8_linear_accumulate_alpha_and_matmul_route():
     out = base.clone()
     wgemm.f8_linear(x, ws, out, accumulate=True, alpha=0.5)
     ref = base + 0.5 * wgemm.f8_reference(x, ws)
-    assert ((out - ref).abs().max() / ref.abs().max()).item() < 1e-3
+    assert ((out - ref).abs().max() / ref.abs().max()).item() < EMU_TOL
     y = wgemm.matmul(x, ws)                          # default dense FP8 route
-    assert ((y - wgemm.f8_reference(x, ws)).abs().max() / y.abs().max()).item() < 1e-3
+    assert ((y - wgemm.f8_reference(x, ws)).abs().max() / y.abs().max()).item() < EMU_TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T,splits", [(5, 1), (5, 4), (70, 2)])
+def test_f8_linear_exact_on_integers(T, splits):
+    """Integer weights and activations whose e4m3 codes and scales are exact (every 128 x 128 weight block and
+    every (token, group) of the activations holds one 448, so both scales are exactly 1) and whose products and
+    sums stay far inside fp32's integer range: the kernel must return the exact integer result, whatever the K
+    split or the token tile. Any layout, swizzle, scale or ordering slip shows up as a mismatch."""
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(T + splits)
+    R, K = 256, 512
+    w = torch.randint(-8, 9, (R, K), generator=g).float()
+    for rb in range(R // 128):
+        for kb in range(K // 128):
+            w[rb * 128, kb * 128] = 448.0
+    x = torch.randint(-4, 5, (T, K), generator=g).float()
+    x[:, 1::128] = 448.0
+    ws = wgemm.dense_fp8(w).to(dev)
+    codes, sc = ws.f8_operands()
+    assert torch.all(sc == 1.0)
+    out = torch.empty(T, R, device=dev)
+    wgemm.f8_linear(x.to(dev).half(), ws, out, nt=64 if T <= 64 else 128, splits=splits)
+    torch.cuda.synchronize()
+    want = (x.double() @ w.double().t()).float()
+    assert torch.equal(out.cpu(), want), (out.cpu() - want).abs().max()

@@ -72,6 +72,22 @@ def test_gdn_step(n_tok):
     _close(ss1, ss0, 1e-4)
 
 
+@pytest.mark.parametrize("T,E,k", [(64, 320, 10), (33, 144, 8), (5, 256, 8), (9, 600, 4)])
+def test_moe_route_sizes(T, E, k):
+    """Router top-k at the model sizes (warp-per-token kernel up to 512 experts, block kernel beyond): the same
+    experts as the torch softmax + top-k, weights renormalized over the selection; a NaN logit still yields valid
+    ids."""
+    g = torch.Generator().manual_seed(E + k)
+    logits = torch.randn(T, E + 1, generator=g) * 3
+    logits[0, 5] = float("nan")
+    ids, w = ops.moe_route(logits.cuda(), E, k)
+    ids = ids.cpu()
+    assert int(ids.min()) >= 0 and int(ids.max()) < E
+    ids0, w0 = ops.moe_route(logits[1:], E, k)
+    assert torch.equal(ids[1:], ids0)
+    _close(w[1:], w0, 1e-5)
+
+
 def test_moe_ops():
     g = torch.Generator().manual_seed(5)
     T, E, k, H = 37, 24, 4, 256
@@ -209,6 +225,7 @@ def test_small_model_gpu_vs_cpu(kv, ple):
     native.check_error()
     want = ref.forward(W, cfg, ids)[79:]
     _close(outs["cpu"], want, 2e-3)
-    _close(outs["cuda"], want, 5e-2 if kv == "fp8" else 2e-2)
+    # the GPU path also quantizes the dense projections' activations to e4m3 per 128-column group
+    _close(outs["cuda"], want, 5e-2 if kv == "fp8" else 4e-2)
     agree = (outs["cuda"].argmax(-1) == want.argmax(-1)).float().mean().item()
     assert agree >= 0.9, agree

@@ -32,7 +32,10 @@ def test_dense_gemm(fmt, T):
     ws = (wgemm.dense_f16(w) if fmt == 16 else wgemm.dense_fp8(w)).to("cuda")
     x = torch.randn(T, K, generator=g).half()
     ref = x.float() @ ws.dense(0).cpu().t()
-    y = wgemm.matmul(x.cuda(), ws)
+    # the weight-dequant kind::f16 GEMM (fp16 activations); FP8 weight sets reach it with an explicit launch plan,
+    # their default route being the kind::f8f6f4 GEMM (tests/test_f8gemm.py)
+    nt, ks = wgemm.dense_plan(T, ws)
+    y = wgemm.matmul(x.cuda(), ws, n_tile=nt, k_splits=ks)
     torch.cuda.synchronize()
     native.check_error()
     assert torch.allclose(y.cpu(), ref, atol=2e-3, rtol=2e-3), (y.cpu() - ref).abs().max()
@@ -107,8 +110,9 @@ def test_dense_split_k_deterministic(R, K, T, ks):
     ws = wgemm.dense_fp8(w).to("cuda")
     x = torch.randn(T, K, generator=g).half()
     ref = x.float() @ ws.dense(0).cpu().t()
-    y1 = wgemm.matmul(x.cuda(), ws, k_splits=ks)
-    y2 = wgemm.matmul(x.cuda(), ws, k_splits=ks)
+    nt, ks = wgemm.dense_plan(T, ws) if ks == 0 else (None, ks)   # the kind::f16 GEMM's own plan
+    y1 = wgemm.matmul(x.cuda(), ws, n_tile=nt, k_splits=ks)
+    y2 = wgemm.matmul(x.cuda(), ws, n_tile=nt, k_splits=ks)
     torch.cuda.synchronize()
     native.check_error()
     assert torch.equal(y1, y2), "split-K result is not reproducible"
@@ -167,6 +171,50 @@ def test_gemv_grouped_matches_reference(epi):
         wgemm.gemv_grouped(xs, ws, items, n_items, items.shape[0], out_g, row_dst=addr)
         torch.cuda.synchronize()
         assert torch.allclose(dst[perm_rows].cpu(), out_g.cpu())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("epi", [0, 1])
+@pytest.mark.parametrize("shape", [(6, 384, 256, 13, 3), (24, 2560, 640, 64, 6)])
+def test_moe_i8_equals_gemv(epi, shape):
+    """The tcgen05 kind::i8 grouped MoE kernel (codes widened into tensor memory, integer MMA) gives the CUDA-core
+    GEMV's bits on mixed 4/3/2-bit experts: short rows (fewer groups than its fold lag) and FN-sized rows (20
+    groups), items of 1..8 tokens, store and silu*up epilogues, per-row destinations."""
+    from arcagi2_flashnext_dots3_b200.formats import lowbit_file
+    from arcagi2_flashnext_dots3_b200.formats import runtime as rt
+    from arcagi2_flashnext_dots3_b200.ops import fn_ops, wgemm
+    E, H, I, T, k = shape
+    g = torch.Generator().manual_seed(7 + E)
+    lay = lowbit_file.random_layer(E, H, I, [(4, 3, 2)[e % 3] for e in range(E)], g, symmetric=False)
+    if epi == 1:
+        perm = rt.gate_up_perm(I)
+        blobs = [rt.pack_planar_blob(b.gu, b.gu_s, b.gu_z, b.bits, row_perm=perm) for b in lay.blobs]
+        ws = wgemm.build_weight_set(blobs, [b.bits for b in lay.blobs], 2 * I, H, silu_pairs=True, device="cuda")
+        K, cols = H, I
+    else:
+        blobs = [rt.pack_planar_blob(b.d, b.d_s, b.d_z, b.bits) for b in lay.blobs]
+        ws = wgemm.build_weight_set(blobs, [b.bits for b in lay.blobs], H, I, device="cuda")
+        K, cols = I, H
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32).cuda()
+    P = T * k
+    mi = P // 8 + E + 1
+    pair_pos, items, n_items = fn_ops.moe_plan(ids, E, 8, mi)
+    xs = (torch.randn(P, K, generator=g) * 0.5).half().cuda()
+    dt = torch.float16 if epi else torch.float32
+    a = torch.zeros(P, cols, dtype=dt, device="cuda")
+    b = torch.zeros(P, cols, dtype=dt, device="cuda")
+    wgemm.gemv_grouped(xs, ws, items, n_items, mi, a, epi=epi, kernel="dp4a")
+    wgemm.gemv_grouped(xs, ws, items, n_items, mi, b, epi=epi, kernel="i8")
+    torch.cuda.synchronize()
+    native.check_error()
+    assert torch.equal(a, b), (a.float() - b.float()).abs().max()
+    if epi == 0:
+        dst = torch.zeros(P, cols, dtype=torch.float32, device="cuda")
+        perm_rows = torch.randperm(P, generator=g).cuda()
+        addr = dst.data_ptr() + perm_rows.long() * cols * 4
+        wgemm.gemv_grouped(xs, ws, items, n_items, mi, b, row_dst=addr, kernel="i8")
+        torch.cuda.synchronize()
+        assert torch.equal(dst[perm_rows], a)
 
 
 @pytest.mark.gpu
