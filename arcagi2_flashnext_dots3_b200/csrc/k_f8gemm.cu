@@ -235,11 +235,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();                          // activation scales (and an accumulated output) come from earlier kernels
     const float* xs_base = a.xscale + tt * NT + h * (NT / 2);
     const float* ws_row = a.wscale + (size_t)rb * a.KB;
+    // The group's scales (its weight block's, and the NT/2 activation scales of this thread's token half) are in
+    // registers before the group's accumulator is: loaded one group ahead (two when NT <= 64, where the registers
+    // allow), so their latency overlaps the wait instead of following it.
+    constexpr int NC = NT / 8;
+    constexpr bool kAhead = NT <= 64;
+    float4 cn[NC];
+    float swn = 0.f;
+    if (kAhead && n_kb > 0) {
+      const float4* x0 = reinterpret_cast<const float4*>(xs_base + (size_t)kb0 * a.xs_ld);
+#pragma unroll
+      for (int m = 0; m < NC; ++m) cn[m] = __ldg(x0 + m);
+      swn = __ldg(ws_row + kb0);
+    }
     for (int i = 0; i < n_kb; ++i) {
       const int b = i % kAcc, kb = kb0 + i;
       const uint32_t bph = (uint32_t)(i / kAcc) & 1u;
-      const float sw = __ldg(ws_row + kb);
-      const float4* xs4 = reinterpret_cast<const float4*>(xs_base + (size_t)kb * a.xs_ld);
+      float4 cc[NC];
+      float sw;
+      if constexpr (kAhead) {
+#pragma unroll
+        for (int m = 0; m < NC; ++m) cc[m] = cn[m];
+        sw = swn;
+        if (i + 1 < n_kb) {
+          const float4* xn = reinterpret_cast<const float4*>(xs_base + (size_t)(kb + 1) * a.xs_ld);
+#pragma unroll
+          for (int m = 0; m < NC; ++m) cn[m] = __ldg(xn + m);
+          swn = __ldg(ws_row + kb + 1);
+        }
+      } else {
+        const float4* xs4 = reinterpret_cast<const float4*>(xs_base + (size_t)kb * a.xs_ld);
+#pragma unroll
+        for (int m = 0; m < NC; ++m) cc[m] = __ldg(xs4 + m);
+        sw = __ldg(ws_row + kb);
+      }
       if (!mbar_wait_warp(accf(b), bph, a.err, 7104, abort_flag, lim)) break;
       tc_fence_after();
       uint32_t v[NT / 32][16];
@@ -251,8 +280,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(acce(b));
 #pragma unroll
-      for (int m = 0; m < NT / 8; ++m) {
-        const float4 c4 = __ldg(xs4 + m);
+      for (int m = 0; m < NC; ++m) {
+        const float4 c4 = cc[m];
         const int j = 4 * m;
         acc[j + 0] = fmaf(__uint_as_float(v[j >> 4][(j + 0) & 15]), sw * c4.x, acc[j + 0]);
         acc[j + 1] = fmaf(__uint_as_float(v[j >> 4][(j + 1) & 15]), sw * c4.y, acc[j + 1]);

@@ -192,6 +192,13 @@ __global__ void __launch_bounds__(128, MINB) gemv_grouped_kernel(GemvArgs a) {
     const int e = it.x, t0 = it.y, n = min(it.z, kMaxTok);
     if (n <= 0) continue;
     if (staged != item) {
+      // the unit's first weight group heads for L2 while its activations are staged (a block's row words are
+      // 512 bytes apart: one prefetch per word of this thread's row)
+      const int fmt0 = a.exp_fmt[e];
+      const int nw0 = fmt0 == 4 ? 16 : fmt0 == 3 ? 13 : 8;
+      const uint8_t* b0 = a.wbase + a.exp_off[e] + (int64_t)tile * a.kg * fw::wgemm_block_bytes(fmt0);
+      for (int i = 0; i < nw0; ++i)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(b0 + (i * 128 + threadIdx.x) * 4));
       __syncthreads();
       const int4* src = reinterpret_cast<const int4*>(a.xq + (int64_t)t0 * Kw * 4);
       int4* dst = reinterpret_cast<int4*>(xsm);
