@@ -1246,7 +1246,7 @@ __global__ void moe_route_kernel(const float* logits, int ld, int32_t* ids, floa
 template <int EPL>
 __global__ void __launch_bounds__(256) moe_route_warp_kernel(const float* logits, int ld, int T, int32_t* ids,
                                                              float* w, int E, int k) {
-  const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (t >= T) return;
   const float* x = logits + (int64_t)t * ld;
   float p[EPL];
@@ -1307,15 +1307,21 @@ void moe_route(torch::Tensor logits, torch::Tensor ids, torch::Tensor w, int64_t
   const int T = logits.size(0);
   if (!T) return;
   const int ld = logits.size(1);
-  const int grid = (T + 7) / 8;
-  if (E <= 128)
-    moe_route_warp_kernel<4><<<grid, 256, 0, STREAM>>>(logits.data_ptr<float>(), ld, T, ids.data_ptr<int32_t>(),
+  // threads per block of the warp-per-token kernel (FW_ROUTE_TPB), FW_ROUTE_OLD=1: the block-per-token kernel
+  static const int tpb = getenv("FW_ROUTE_TPB") ? atoi(getenv("FW_ROUTE_TPB")) : 64;
+  static const bool old_k = getenv("FW_ROUTE_OLD") && atoi(getenv("FW_ROUTE_OLD"));
+  const int grid = (T + tpb / 32 - 1) / (tpb / 32);
+  if (old_k)
+    moe_route_kernel<<<T, 256, E * sizeof(float), STREAM>>>(logits.data_ptr<float>(), ld, ids.data_ptr<int32_t>(),
+                                                            w.data_ptr<float>(), E, k);
+  else if (E <= 128)
+    moe_route_warp_kernel<4><<<grid, tpb, 0, STREAM>>>(logits.data_ptr<float>(), ld, T, ids.data_ptr<int32_t>(),
                                                        w.data_ptr<float>(), E, k);
   else if (E <= 256)
-    moe_route_warp_kernel<8><<<grid, 256, 0, STREAM>>>(logits.data_ptr<float>(), ld, T, ids.data_ptr<int32_t>(),
+    moe_route_warp_kernel<8><<<grid, tpb, 0, STREAM>>>(logits.data_ptr<float>(), ld, T, ids.data_ptr<int32_t>(),
                                                        w.data_ptr<float>(), E, k);
   else if (E <= 512)
-    moe_route_warp_kernel<16><<<grid, 256, 0, STREAM>>>(logits.data_ptr<float>(), ld, T, ids.data_ptr<int32_t>(),
+    moe_route_warp_kernel<16><<<grid, tpb, 0, STREAM>>>(logits.data_ptr<float>(), ld, T, ids.data_ptr<int32_t>(),
                                                         w.data_ptr<float>(), E, k);
   else
     moe_route_kernel<<<T, 256, E * sizeof(float), STREAM>>>(logits.data_ptr<float>(), ld, ids.data_ptr<int32_t>(),

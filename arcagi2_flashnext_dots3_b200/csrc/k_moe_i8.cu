@@ -8,7 +8,7 @@
 // bytes, the MMA does the products. Results equal the GEMV's bit for bit: the integer dots are exact in both, and
 // the per-group fp32 folds run in the same order with the same operations.
 //
-// CTA (160 threads, two per SM), persistent over work units (item, 128-row tile), strided by the grid:
+// CTA (160 threads, kCps per SM), persistent over work units (item, 128-row tile), strided by the grid:
 //   warp 0     producer: per (unit, group) one stage = the 2 KB activation tile (16 token rows x 128 int8 by
 //              2-D TMA in the 128-byte swizzle, the MMA's B operand as is) + the packed weight block (4.5 to
 //              8.6 KB, one 1-D bulk copy), 8 stages in flight
@@ -41,11 +41,15 @@ namespace moei8 {
 
 constexpr int kTok = 16;                 // MMA N (the smallest N of an M = 128 MMA); rows past the item's n unused
 constexpr int kMaxTok = 8;               // tokens of one item (plans are built with items of at most 8 tokens)
-constexpr int kSlots = 5;                // TMEM slots, each A (32 columns = 128 int8 per row) + D (16 columns)
+#ifndef FW_MOE_I8_CPS
+#define FW_MOE_I8_CPS 4                  // CTAs per SM
+#endif
+constexpr int kCps = FW_MOE_I8_CPS;
+constexpr int kSlots = kCps >= 4 ? 2 : 5;   // TMEM slots, each A (32 columns = 128 int8 per row) + D (16 columns)
 constexpr int kSlotCols = 48;
-constexpr int kLag = 3;                  // groups between storing a group's A and folding its dots
-constexpr int kTmemCols = 256;
-constexpr int kStages = 8;
+constexpr int kLag = kSlots - 1;         // groups between storing a group's A and folding its dots
+constexpr int kTmemCols = kCps >= 4 ? 128 : 256;
+constexpr int kStages = kCps >= 4 ? 4 : 8;
 constexpr int kBTile = kTok * 128;       // activation tile bytes (1024-aligned start, 128-byte swizzle)
 constexpr int kStageBytes = 11264;       // kBTile + the largest packed block (8576), rounded up to 1024
 constexpr int kThreads = 160;            // warp 0 producer, warps 1-4 rows
@@ -248,7 +252,7 @@ __device__ __forceinline__ bool row_unit(const Args& a, const Ctx& c, int t0, in
   return true;
 }
 
-__global__ void __launch_bounds__(kThreads, 2) moe_i8_kernel(const Args a, const __grid_constant__ CUtensorMap xmap) {
+__global__ void __launch_bounds__(kThreads, kCps) moe_i8_kernel(const Args a, const __grid_constant__ CUtensorMap xmap) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -429,7 +433,7 @@ void moe_i8(torch::Tensor wbase, torch::Tensor exp_off, torch::Tensor exp_fmt, i
     attr = true;
   }
   const int64_t work = max_items * row_tiles;
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(work, (int64_t)sms * 2));
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(work, (int64_t)sms * fw::moei8::kCps));
   static const bool pdl = !(getenv("FW_PDL") && atoi(getenv("FW_PDL")) == 0);   // FW_PDL=0: plain launch
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

@@ -80,6 +80,24 @@ def bench_moe(args):
                           "ms": round(t, 4), "MB": round(b / 1e6, 1), "GBps": round(b / t / 1e6, 1)}))
 
 
+def bench_route(args):
+    """Router top-k (softmax over the experts, top-k, renormalize) at the decode batch, graph-timed."""
+    from ..config import fn_config
+    from ..ops import fn_ops as ops
+    cfg = fn_config()
+    dev = torch.device("cuda")
+    logits = torch.randn(args.tokens, cfg.n_experts + 1, device=dev)
+    ops.moe_route(logits, cfg.n_experts, cfg.top_k)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(10):
+            ops.moe_route(logits, cfg.n_experts, cfg.top_k)
+    t = _time(g.replay, args.reps) / 10
+    print(json.dumps({"case": "moe_route", "tokens": args.tokens, "experts": cfg.n_experts, "k": cfg.top_k,
+                      "us": round(t * 1e3, 2)}))
+
+
 def bench_dense(args):
     """Dense FP8 projections at decode batch: the tcgen05 kind::f8f6f4 GEMM (per-group FP8 activations, the
     default) against the weight-dequant kind::f16 GEMM. Each arm rotates over enough weight copies that every
@@ -258,7 +276,7 @@ def bench_absorb(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["moe", "dense", "attn", "gdn", "mla", "absorb", "all"])
+    ap.add_argument("case", choices=["moe", "dense", "attn", "gdn", "mla", "absorb", "route", "all"])
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--experts", type=int, default=320)
     ap.add_argument("--ctx", type=int, default=9000)
@@ -267,6 +285,7 @@ def main():
     ap.add_argument("--only", default="", help="dense: comma-separated case names")
     args = ap.parse_args()
     cases = {"moe": bench_moe, "dense": bench_dense, "attn": bench_attn, "gdn": bench_gdn, "mla": bench_mla,
+             "route": bench_route,
              "absorb": bench_absorb}
     for name, fn in cases.items():
         if args.case in (name, "all"):
