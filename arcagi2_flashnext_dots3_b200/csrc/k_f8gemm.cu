@@ -533,6 +533,36 @@ int64_t f8_linear(torch::Tensor x, torch::Tensor w8, torch::Tensor wscale, int64
 
 }  // namespace
 
+// How many clusters of `splits` CTAs of the nt-token GEMM can be resident at once on the current device
+// (cudaOccupancyMaxActiveClusters): a launch plan whose clusters exceed it runs in more than one wave.
+int64_t f8_max_clusters(int64_t nt, int64_t splits) {
+  TORCH_CHECK(nt == 32 || nt == 64 || nt == 128, "nt must be 32, 64 or 128");
+  TORCH_CHECK(splits >= 1 && splits <= 8, "splits must be in [1, 8]");
+  auto query = [&](auto kernel, size_t smem) -> int64_t {
+    TORCH_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess,
+                "f8gemm shared memory attribute");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)splits, 1, 1);
+    cfg.blockDim = dim3(fw::f8::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+    TORCH_CHECK(e == cudaSuccess, "cudaOccupancyMaxActiveClusters: ", cudaGetErrorString(e));
+    return n;
+  };
+  if (nt == 32) return query(fw::f8::f8gemm_kernel<32>, fw::f8::Cfg<32>::kSmem);
+  if (nt == 64) return query(fw::f8::f8gemm_kernel<64>, fw::f8::Cfg<64>::kSmem);
+  return query(fw::f8::f8gemm_kernel<128>, fw::f8::Cfg<128>::kSmem);
+}
+
 void register_f8gemm(pybind11::module& m) {
   m.def("f8_linear", &f8_linear, "dense FP8 GEMM (tcgen05 kind::f8f6f4) with per-group FP8 activations");
+  m.def("f8_max_clusters", &f8_max_clusters, "co-resident clusters of the FP8 GEMM for a token tile and K split");
 }

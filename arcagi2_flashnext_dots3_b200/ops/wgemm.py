@@ -146,14 +146,34 @@ F8_MAX_SPLITS = 8           # cluster size along K (portable limit)
 F8_SMS = 148
 
 
+_F8_CLUSTERS = {}
+
+
+def f8_max_clusters(nt: int, s: int) -> int:
+    """Co-resident clusters of `s` CTAs of the FP8 GEMM with token tile `nt` on this GPU (the driver's occupancy
+    query, cached). Without a GPU: the B200 layout of 8 GPCs of about 18 SMs, one CTA per SM."""
+    key = (nt, s)
+    if key not in _F8_CLUSTERS:
+        if torch.cuda.is_available():
+            _F8_CLUSTERS[key] = int(native.C().f8_max_clusters(nt, s))
+        else:
+            _F8_CLUSTERS[key] = 8 * (18 // s)
+    return _F8_CLUSTERS[key]
+
+
 def f8_plan(T: int, ws: WeightSet):
     """(token tile, K splits) of the FP8 dense GEMM: the narrowest of 32/64/128 tokens that holds T (all of a
-    decode batch in one tile, so the weights stream once), then as many K splits (a cluster of CTAs per row tile,
-    reduced in distributed shared memory) as keep the grid within one wave of the SMs."""
+    decode batch in one tile, so the weights stream once), then the most K splits (a cluster of CTAs per row
+    tile, reduced in distributed shared memory) for which every cluster of the grid is resident at once: at most
+    one wave of the SMs, and no more clusters than the GPCs can hold (a cluster's CTAs share a GPC, so clusters of
+    7 on 18-SM GPCs fit two per GPC and 20 of them would take two waves)."""
     nt = 32 if T <= 32 else 64 if T <= 64 else 128
     units = ws.row_tiles * ((T + nt - 1) // nt)
-    s = max(1, min(F8_MAX_SPLITS, ws.kg, F8_SMS // max(1, units)))
-    return nt, s
+    best = 1
+    for s in range(2, min(F8_MAX_SPLITS, ws.kg) + 1):
+        if units * s <= F8_SMS and units <= f8_max_clusters(nt, s):
+            best = s
+    return nt, best
 
 
 def f8_ok(ws: WeightSet, fan) -> bool:
