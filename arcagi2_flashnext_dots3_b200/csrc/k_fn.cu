@@ -282,6 +282,41 @@ __global__ void gdn_conv_kernel(const float* proj, int ldp, const float* conv_w,
   }
 }
 
+// Prefill form of the convolution (no commit count): one thread per (sequence, token, channel); the kc-1 inputs
+// before a token come from this step's rows or the conv state, which gdn_conv_state_kernel rewrites afterwards.
+// Same products in the same order as gdn_conv_kernel.
+__global__ void gdn_conv_par_kernel(const float* proj, int ldp, const float* conv_w, const float* conv_state,
+                                    const int* slots, float* out, int C, int kc, int n_tok, int B) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)B * n_tok * C) return;
+  const int c = idx % C;
+  const int64_t bt = idx / C;
+  const int t = bt % n_tok, b = bt / n_tok;
+  const float* st = conv_state + ((int64_t)slots[b] * C + c) * (kc - 1);
+  const float* w = conv_w + (int64_t)c * kc;
+  float acc = w[kc - 1] * proj[((int64_t)b * n_tok + t) * ldp + c];
+  for (int j = 0; j < kc - 1; ++j) {
+    const int tp = t - (kc - 1) + j;
+    const float v = tp >= 0 ? proj[((int64_t)b * n_tok + tp) * ldp + c] : st[kc - 1 + tp];
+    acc += w[j] * v;
+  }
+  out[((int64_t)b * n_tok + t) * C + c] = silu(acc);
+}
+
+// The conv state after a prefill step: the last kc-1 inputs (entry j reads entry j + n_tok of the old state when
+// the step is shorter than the window, so ascending j never reads an entry it already wrote).
+__global__ void gdn_conv_state_kernel(const float* proj, int ldp, float* conv_state, const int* slots, int C, int kc,
+                                      int n_tok, int B) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)B * C) return;
+  const int b = idx / C, c = idx % C;
+  float* st = conv_state + ((int64_t)slots[b] * C + c) * (kc - 1);
+  for (int j = 0; j < kc - 1; ++j) {
+    const int tp = n_tok - (kc - 1) + j;
+    st[j] = tp >= 0 ? proj[((int64_t)b * n_tok + tp) * ldp + c] : st[j + n_tok];
+  }
+}
+
 // Gated delta rule for one (sequence, value head) over n_tok tokens; DK = DV = 128, 256 threads:
 // thread (j = tid & 127, half = tid >> 7) keeps S[64*half .. 64*half+63][j] in registers.
 template <typename ST>
@@ -379,10 +414,21 @@ void gdn_step(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor conv_state
   CK(kc >= 2 && kc <= 8);
   auto qkv = torch::empty({rows, C}, proj.options());
   const int64_t nthr = (int64_t)B * C;
-  gdn_conv_kernel<<<(nthr + 255) / 256, 256, 0, STREAM>>>(proj.data_ptr<float>(), proj.size(1),
-                                                          conv_w.data_ptr<float>(), conv_state.data_ptr<float>(),
-                                                          slots.data_ptr<int32_t>(), qkv.data_ptr<float>(), C, kc,
-                                                          n_tok, B, ncm);
+  if (!ncm && n_tok >= 16) {             // prefill: every (token, channel) in parallel, then the state
+    const int64_t nall = nthr * n_tok;
+    gdn_conv_par_kernel<<<(nall + 255) / 256, 256, 0, STREAM>>>(proj.data_ptr<float>(), proj.size(1),
+                                                                conv_w.data_ptr<float>(), conv_state.data_ptr<float>(),
+                                                                slots.data_ptr<int32_t>(), qkv.data_ptr<float>(), C,
+                                                                kc, n_tok, B);
+    gdn_conv_state_kernel<<<(nthr + 255) / 256, 256, 0, STREAM>>>(proj.data_ptr<float>(), proj.size(1),
+                                                                  conv_state.data_ptr<float>(),
+                                                                  slots.data_ptr<int32_t>(), C, kc, n_tok, B);
+  } else {
+    gdn_conv_kernel<<<(nthr + 255) / 256, 256, 0, STREAM>>>(proj.data_ptr<float>(), proj.size(1),
+                                                            conv_w.data_ptr<float>(), conv_state.data_ptr<float>(),
+                                                            slots.data_ptr<int32_t>(), qkv.data_ptr<float>(), C, kc,
+                                                            n_tok, B, ncm);
+  }
   dim3 grid(B, nv);
   if (ssm.scalar_type() == torch::kBFloat16)
     gdn_recur_kernel<__nv_bfloat16><<<grid, 256, 0, STREAM>>>(
@@ -522,6 +568,49 @@ __global__ void qsa_compress_kernel(const float* proj, int ldp, int kr_off, floa
   }
 }
 
+// Prefill form: one block per (sequence, compressed block completing in this step), the blocks independent; the
+// raw-key ring is read as it was at the step start and refreshed by qsa_ring_kernel afterwards. Same sums in the
+// same order as qsa_compress_kernel.
+template <typename CT>
+__global__ void qsa_compress_par_kernel(const float* proj, int ldp, int kr_off, const float* ring, CT* comp,
+                                        int max_comp, const float* ikn, const float* rope, int rope_len, int rdq,
+                                        const int* slots, const int* positions, int r, int RL, int iD, int n_tok,
+                                        float eps) {
+  extern __shared__ float xs[];  // [iD]
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const int s = slots[b];
+  const int p0 = positions[b];
+  const int cb = (p0 + r) / r - 1 + blockIdx.y;   // first block whose last position is >= p0, then the next ones
+  if ((cb + 1) * r > p0 + n_tok) return;          // completes in a later step
+  const int st = cb * r, p = st + r - 1;
+  const float* rg = ring + (int64_t)s * RL * iD;
+  for (int d = threadIdx.x; d < iD; d += blockDim.x) {
+    float acc = 0.f;
+    for (int q = st; q <= p; ++q) {
+      const float v = q >= p0 ? proj[((int64_t)b * n_tok + (q - p0)) * ldp + kr_off + d] : rg[(q % RL) * iD + d];
+      acc += v;
+    }
+    xs[d] = acc / r;
+  }
+  __syncthreads();
+  norm_rope_head(xs, iD, ikn, eps, rope + (int64_t)st * rdq, rope + (int64_t)rope_len * rdq + (int64_t)st * rdq, rdq,
+                 red);
+  if (cb < max_comp)
+    for (int d = threadIdx.x; d < iD; d += blockDim.x) stf(&comp[((int64_t)s * max_comp + cb) * iD + d], xs[d]);
+}
+
+// Refresh the raw-key ring with the last min(RL, n_tok) raw keys of the step (one block per sequence).
+__global__ void qsa_ring_kernel(const float* proj, int ldp, int kr_off, float* ring, const int* slots,
+                                const int* positions, int RL, int iD, int n_tok) {
+  const int b = blockIdx.x;
+  float* rg = ring + (int64_t)slots[b] * RL * iD;
+  const int p0 = positions[b];
+  for (int t = max(0, n_tok - RL); t < n_tok; ++t)
+    for (int d = threadIdx.x; d < iD; d += blockDim.x)
+      rg[((p0 + t) % RL) * iD + d] = proj[((int64_t)b * n_tok + t) * ldp + kr_off + d];
+}
+
 void qsa_prep(torch::Tensor proj, torch::Tensor qn, torch::Tensor kn, torch::Tensor iqn, torch::Tensor ikn,
               torch::Tensor rope, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
               torch::Tensor slots, torch::Tensor positions, torch::Tensor kr_ring, torch::Tensor comp_cache,
@@ -551,6 +640,20 @@ void qsa_prep(torch::Tensor proj, torch::Tensor qn, torch::Tensor kn, torch::Ten
   const int RL = kr_ring.size(1);
   CK(RL >= ratio);
   const size_t smc = (RL * iD + iD) * sizeof(float);
+  if (n_tok >= 2 * ratio) {              // prefill: the completing blocks in parallel, then the ring
+    dim3 g2(B, n_tok / ratio + 1);
+#define COMP_PAR(CT)                                                                                               \
+  qsa_compress_par_kernel<CT><<<g2, 128, iD * sizeof(float), STREAM>>>(                                            \
+      proj.data_ptr<float>(), proj.size(1), kr_off, kr_ring.data_ptr<float>(), (CT*)comp_cache.data_ptr(),         \
+      comp_cache.size(1), ikn.data_ptr<float>(), rope.data_ptr<float>(), rope_len, rd, slots.data_ptr<int32_t>(),  \
+      positions.data_ptr<int32_t>(), ratio, RL, iD, n_tok, (float)eps)
+    if (comp_cache.scalar_type() == torch::kBFloat16) COMP_PAR(__nv_bfloat16);
+    else COMP_PAR(float);
+#undef COMP_PAR
+    qsa_ring_kernel<<<B, 128, 0, STREAM>>>(proj.data_ptr<float>(), proj.size(1), kr_off, kr_ring.data_ptr<float>(),
+                                           slots.data_ptr<int32_t>(), positions.data_ptr<int32_t>(), RL, iD, n_tok);
+    return;
+  }
   if (comp_cache.scalar_type() == torch::kBFloat16)
     qsa_compress_kernel<__nv_bfloat16><<<B, 128, smc, STREAM>>>(
         proj.data_ptr<float>(), proj.size(1), kr_off, kr_ring.data_ptr<float>(), (__nv_bfloat16*)comp_cache.data_ptr(),

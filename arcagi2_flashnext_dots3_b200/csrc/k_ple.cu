@@ -66,6 +66,54 @@ __global__ void ple_ids_kernel(const int32_t* ids, int B, int n_tok, const int32
   hs[n - 1] = since;
 }
 
+// Prefill form: one block per sequence, tokens over the threads. Token j's hashes need the n-1 tokens before it
+// (this step's ids, or the history for positions before the step) and the length of the eos-free run that ends
+// just before it, which a walk back over at most n-1 tokens gives. Thread 0 rewrites the history after a block
+// barrier, once every thread has read it. Same hashes as the sequential kernel above.
+__global__ void ple_ids_par_kernel(const int32_t* ids, int n_tok, const int32_t* slots, int64_t* hist, int n,
+                                   const int64_t* mult, const int64_t* offs, const int64_t* sizes, int hpn, int eos,
+                                   int64_t* rows) {
+  const int b = blockIdx.x;
+  int64_t* hs = hist + (int64_t)slots[b] * n;  // [n-1 previous tokens, newest first][tokens since eos]
+  const int64_t since0 = hs[n - 1];
+  const int nh = (n - 1) * hpn;
+  const int32_t* tk = ids + (int64_t)b * n_tok;
+  for (int j = threadIdx.x; j < n_tok; j += blockDim.x) {
+    const int64_t t = tk[j];
+    int64_t* out = rows + ((int64_t)b * n_tok + j) * nh;
+    // tokens since the last eos as the sequential walk would count them at token j (only values up to n-1 matter)
+    int run = 0;
+    bool hit = false;
+    for (int q = 1; q <= min(j, n - 1); ++q) {
+      if (tk[j - q] == eos) {
+        hit = true;
+        break;
+      }
+      ++run;
+    }
+    const int64_t since = hit ? run : (j <= n - 1 ? since0 + j : (int64_t)(n - 1));
+    for (int ng = 2; ng <= n; ++ng) {
+      uint64_t mixed = (uint64_t)t * (uint64_t)mult[0];
+      for (int q = 1; q < ng; ++q) {
+        const int64_t prev = q <= j ? (int64_t)tk[j - q] : hs[q - j - 1];
+        const int64_t sq = since >= q ? prev : (int64_t)eos;
+        mixed ^= (uint64_t)sq * (uint64_t)mult[q];
+      }
+      for (int h = (ng - 2) * hpn; h < (ng - 1) * hpn; ++h) {
+        const int64_t m = (int64_t)mixed, s = sizes[h];
+        out[h] = ((m % s) + s) % s + offs[h];
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int64_t since = since0;
+    for (int j = 0; j < n_tok; ++j) since = tk[j] == eos ? 0 : since + 1;
+    for (int q = n - 2; q >= 0; --q) hs[q] = q < n_tok ? (int64_t)tk[n_tok - 1 - q] : hs[q - n_tok];
+    hs[n - 1] = since;
+  }
+}
+
 __global__ void ple_gather_kernel(const __nv_fp8_e4m3* table, int64_t n_rows, int dim, const int64_t* rows, int nh,
                                   float scale, __half* emb) {
   const int t = blockIdx.x, h = blockIdx.y;
@@ -153,10 +201,16 @@ void ple_ids(torch::Tensor ids, torch::Tensor slots, int64_t n_tok, torch::Tenso
   const int B = slots.size(0), n = hist.size(1);
   CK(ids.scalar_type() == torch::kInt32 && hist.scalar_type() == torch::kInt64 && rows.scalar_type() == torch::kInt64);
   CK(rows.size(0) == B * n_tok && rows.size(1) == (n - 1) * hpn && mult.numel() >= n - 1 + 1);
-  if (B) ple_ids_kernel<<<(B + 63) / 64, 64, 0, STREAM>>>(ids.data_ptr<int32_t>(), B, n_tok, slots.data_ptr<int32_t>(),
-                                                         hist.data_ptr<int64_t>(), n, mult.data_ptr<int64_t>(),
-                                                         offs.data_ptr<int64_t>(), sizes.data_ptr<int64_t>(), hpn,
-                                                         eos, rows.data_ptr<int64_t>());
+  if (B && n_tok >= 32)   // prefill: tokens in parallel
+    ple_ids_par_kernel<<<B, 256, 0, STREAM>>>(ids.data_ptr<int32_t>(), n_tok, slots.data_ptr<int32_t>(),
+                                              hist.data_ptr<int64_t>(), n, mult.data_ptr<int64_t>(),
+                                              offs.data_ptr<int64_t>(), sizes.data_ptr<int64_t>(), hpn, eos,
+                                              rows.data_ptr<int64_t>());
+  else if (B)
+    ple_ids_kernel<<<(B + 63) / 64, 64, 0, STREAM>>>(ids.data_ptr<int32_t>(), B, n_tok, slots.data_ptr<int32_t>(),
+                                                     hist.data_ptr<int64_t>(), n, mult.data_ptr<int64_t>(),
+                                                     offs.data_ptr<int64_t>(), sizes.data_ptr<int64_t>(), hpn,
+                                                     eos, rows.data_ptr<int64_t>());
 }
 
 void ple_gather(torch::Tensor table, torch::Tensor rows, double scale, torch::Tensor emb) {

@@ -88,6 +88,31 @@ def test_moe_route_sizes(T, E, k):
     _close(w[1:], w0, 1e-5)
 
 
+def test_ple_ids_prefill_matches_cpu():
+    """n-gram row ids of prefill-sized steps (tokens in parallel on the GPU, eos tokens inside the step, history
+    carried across steps, a one-token decode step in between) equal the sequential CPU walk, history included."""
+    from arcagi2_flashnext_dots3_b200.models import fn_ple
+    cfg = fn_small_config(ple_layers=(0,))
+    W = fn_weights.random_dense(cfg, seed=3)
+    n, hpn = cfg.ngram_size, cfg.heads_per_ngram
+    nh = (n - 1) * hpn
+    g = torch.Generator().manual_seed(3)
+    slots = torch.tensor([2, 0], dtype=torch.int32)
+    hist_c = torch.zeros(3, n, dtype=torch.int64)
+    hist_g = hist_c.cuda()
+    dev = {k: W[k].cuda() for k in ("ple_mult", "ple_offs", "ple_sizes")}
+    for n_tok in (40, 1, 70, 33):
+        ids = torch.randint(0, cfg.vocab_size, (2 * n_tok,), generator=g)
+        ids[3::7] = cfg.eos_token_id
+        want = fn_ple._ids_cpu(ids, slots, n_tok, hist_c, W, cfg)
+        got = torch.empty(2 * n_tok, nh, dtype=torch.int64, device="cuda")
+        native.C().ple_ids(ids.to(torch.int32).cuda(), slots.cuda(), n_tok, hist_g, dev["ple_mult"], dev["ple_offs"],
+                           dev["ple_sizes"], hpn, cfg.eos_token_id, got)
+        torch.cuda.synchronize()
+        assert torch.equal(got.cpu(), want), n_tok
+        assert torch.equal(hist_g.cpu(), hist_c), n_tok
+
+
 def test_moe_ops():
     g = torch.Generator().manual_seed(5)
     T, E, k, H = 37, 24, 4, 256
