@@ -442,6 +442,23 @@ void gdn_step(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor conv_state
         nv, n_tok, (float)eps, gate_sigmoid, ncm);
 }
 
+// The GDN causal convolution of a prefill step (every token in parallel, then the state), for the chunked
+// prefill in k_gdn_chunk.cu. qkv: [rows, C] fp32 output.
+void gdn_conv_prefill_impl(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor conv_state, torch::Tensor slots,
+                           torch::Tensor qkv, int64_t n_tok) {
+  const int rows = proj.size(0);
+  const int B = rows / n_tok, C = qkv.size(1), kc = conv_w.size(1);
+  CK(kc >= 2 && kc <= 8 && proj.is_contiguous() && qkv.is_contiguous());
+  const int64_t nthr = (int64_t)B * C, nall = nthr * n_tok;
+  gdn_conv_par_kernel<<<(nall + 255) / 256, 256, 0, STREAM>>>(proj.data_ptr<float>(), proj.size(1),
+                                                              conv_w.data_ptr<float>(), conv_state.data_ptr<float>(),
+                                                              slots.data_ptr<int32_t>(), qkv.data_ptr<float>(), C, kc,
+                                                              n_tok, B);
+  gdn_conv_state_kernel<<<(nthr + 255) / 256, 256, 0, STREAM>>>(proj.data_ptr<float>(), proj.size(1),
+                                                                conv_state.data_ptr<float>(), slots.data_ptr<int32_t>(),
+                                                                C, kc, n_tok, B);
+}
+
 // ============================================================================================ attention
 // RMSNorm(1+w) + partial RoPE (neox half split on the first rd dims) of one head vector held by `nthr` threads,
 // dims d = tid, tid + nthr, ... ; x in smem.
@@ -1669,4 +1686,9 @@ extern "C" __attribute__((visibility("default"))) int fw_qsa_select_noalloc(
   topk_rows_kernel<<<rows, 512, 0, stream>>>(scores, ld, nullptr, 0, nblk, sel, sparse, positions, r, n_tok);
   e = cudaGetLastError();
   return e == cudaSuccess ? FW_NOALLOC_OK : 1000 + (int)e;
+}
+
+void gdn_conv_prefill(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor conv_state, torch::Tensor slots,
+                      torch::Tensor qkv, int64_t n_tok) {
+  gdn_conv_prefill_impl(proj, conv_w, conv_state, slots, qkv, n_tok);
 }

@@ -16,6 +16,7 @@ void register_mla(pybind11::module& m);
 void register_dsa(pybind11::module& m);
 void register_f8gemm(pybind11::module& m);
 void register_moe_i8(pybind11::module& m);
+void register_gdn_chunk(pybind11::module& m);
 
 void register_kernels(pybind11::module& m) {
   register_fn(m);
@@ -30,4 +31,5 @@ void register_kernels(pybind11::module& m) {
   register_dsa(m);
   register_f8gemm(m);
   register_moe_i8(m);
+  register_gdn_chunk(m);
 }

@@ -206,6 +206,45 @@ def bench_gdn(args):
                       "GBps": round(b / t / 1e6, 1)}))
 
 
+def bench_gdn_prefill(args):
+    """GDN prefill of one sequence of --ctx tokens at FN size (48 value heads, 16 key heads, 128 x 128 states):
+    the chunked tcgen05 delta rule against the sequential recurrence, plus the chunk kernel's per-phase times
+    (%globaltimer of one CTA, averaged over its chunks)."""
+    from ..config import fn_config
+    from ..ops import native
+    cfg = fn_config()
+    dev = torch.device("cuda")
+    n = args.ctx
+    nk, nv, dk, dv = cfg.lin_k_heads, cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim
+    Cq = 2 * nk * dk + nv * dv
+    g = torch.Generator(device=dev).manual_seed(0)
+    qkv = torch.randn(n, Cq, device=dev, generator=g)
+    proj = torch.randn(n, Cq + nv * dv + 2 * nv, device=dev, generator=g)
+    ssm = (torch.randn(2, nv, dk, dv, device=dev, generator=g) * 0.05).bfloat16()
+    A_log = torch.log(torch.rand(nv, device=dev, generator=g) * 0.2 + 0.01)
+    dt = torch.randn(nv, device=dev, generator=g) * 0.3
+    nw = torch.rand(dv, device=dev, generator=g) + 0.5
+    slots = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = torch.empty(n, nv * dv, dtype=torch.float16, device=dev)
+    err = native.err_word(dev)
+    C = native.C()
+    trace = torch.zeros((n + 63) // 64 * 10, dtype=torch.int64, device=dev)
+
+    def chunked(tr=None):
+        C.gdn_chunk(qkv, proj, ssm, A_log, dt, nw, slots, out, nk, nv, n, cfg.rms_eps, 0, err,
+                    native.DEFAULT_TIMEOUT_NS, tr)
+    t = _time(chunked, args.reps)
+    chunked(trace)
+    torch.cuda.synchronize()
+    native.check_error()
+    tr = trace.view(-1, 10).double().cpu()
+    steps = (tr[:, 1:] - tr[:, :-1]).mean(0) / 1e3
+    per_chunk = ((tr[1:, 0] - tr[:-1, 0]).mean() / 1e3).item() if tr.shape[0] > 1 else 0.0
+    print(json.dumps({"case": "gdn_prefill_chunked", "tokens": n, "heads": nv, "ms": round(t, 4),
+                      "tok_per_s_layer": round(n / t * 1e3, 1), "chunk_us": round(per_chunk, 2),
+                      "phase_us": [round(x, 2) for x in steps.tolist()]}))
+
+
 def bench_mla(args):
     """D3 latent attention: tcgen05 kernel vs the CUDA-core kernel, DSA (128 heads, 512+64, top-2048) and SWA
     (64 heads, 1024+64, window 513) decode rows."""
@@ -276,7 +315,8 @@ def bench_absorb(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["moe", "dense", "attn", "gdn", "mla", "absorb", "route", "all"])
+    ap.add_argument("case", choices=["moe", "dense", "attn", "gdn", "mla", "absorb", "route", "gdn_prefill",
+                                     "all"])
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--experts", type=int, default=320)
     ap.add_argument("--ctx", type=int, default=9000)
@@ -285,7 +325,7 @@ def main():
     ap.add_argument("--only", default="", help="dense: comma-separated case names")
     args = ap.parse_args()
     cases = {"moe": bench_moe, "dense": bench_dense, "attn": bench_attn, "gdn": bench_gdn, "mla": bench_mla,
-             "route": bench_route,
+             "route": bench_route, "gdn_prefill": bench_gdn_prefill,
              "absorb": bench_absorb}
     for name, fn in cases.items():
         if args.case in (name, "all"):

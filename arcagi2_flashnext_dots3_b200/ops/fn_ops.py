@@ -79,6 +79,10 @@ def hc_residual(h: torch.Tensor, y: torch.Tensor, inj: torch.Tensor) -> None:
 
 
 # --------------------------------------------------------------------------------------- Gated DeltaNet
+GDN_CHUNK = __import__("os").environ.get("FW_GDN_CHUNK", "1") != "0"   # chunked tcgen05 prefill (k_gdn_chunk.cu)
+GDN_CHUNK_MIN = 64        # tokens per sequence from which a step runs the chunked form
+
+
 def gdn_step(proj: torch.Tensor, conv_w: torch.Tensor, conv_state: torch.Tensor, ssm: torch.Tensor,
              A_log: torch.Tensor, dt_bias: torch.Tensor, norm_w: torch.Tensor, slots: torch.Tensor, cfg,
              n_tok: int = 1, n_commit: torch.Tensor = None) -> torch.Tensor:
@@ -89,9 +93,16 @@ def gdn_step(proj: torch.Tensor, conv_w: torch.Tensor, conv_state: torch.Tensor,
     ``n_commit`` (int32 [B]): write back only the states after the first n_commit[b] tokens (speculative verify)."""
     if _cuda(proj):
         out = torch.empty(proj.shape[0], cfg.lin_v_heads * cfg.lin_v_dim, dtype=torch.float16, device=proj.device)
+        gate = 1 if cfg.gdn_gate == "sigmoid" else 0
+        if (GDN_CHUNK and n_commit is None and n_tok >= GDN_CHUNK_MIN and ssm.dtype == torch.bfloat16
+                and cfg.lin_k_dim == 128 and cfg.lin_v_dim == 128):
+            # prefill: every token's convolution in parallel, then the chunked delta rule on tcgen05
+            native.C().gdn_prefill(proj, conv_w, conv_state, ssm, A_log, dt_bias, norm_w, slots, out,
+                                   cfg.lin_k_heads, cfg.lin_v_heads, n_tok, cfg.rms_eps, gate,
+                                   native.err_word(proj.device), native.DEFAULT_TIMEOUT_NS)
+            return out
         native.C().gdn_step(proj, conv_w, conv_state, ssm, A_log, dt_bias, norm_w, slots, out, cfg.lin_k_heads,
-                            cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim, n_tok, cfg.rms_eps,
-                            1 if cfg.gdn_gate == "sigmoid" else 0, n_commit)
+                            cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim, n_tok, cfg.rms_eps, gate, n_commit)
         return out
     nk, nv, dk, dv = cfg.lin_k_heads, cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim
     C = 2 * nk * dk + nv * dv
