@@ -43,10 +43,14 @@ constexpr int kTileS = D * D * 2;        // S^T: [128 dv][128 dk]
 constexpr int oQ = 0, oK = oQ + kTileQ, oW = oK + kTileQ, oT = oW + kTileQ, oP = oT + kTileT, oVb = oP + kTileT,
               oKb = oVb + kTileX, oVn = oKb + kTileX, oKd = oVn + kTileX, oS = oKd + kTileX,
               oL = oS + kTileS,                      // fp32 L [64][64]
-              oTf = oL + C * C * 4,                  // fp32 T, column c of thread c: [64 rows][64 cols]
-              oVec = oTf + C * C * 4,                // gc [64], beta [64]
+              oTf = oL + C * C * 4,                  // fp32 T [64 rows][64 cols]
+              oX = oTf + C * C * 4,                  // fp32 [3][16][16] partial products of the blocked solve
+              oVec = oX + 3 * 256 * 4,               // gc [64], beta [64]
               oBar = oVec + 2 * C * 4, kSmemUsed = oBar + 64;
 constexpr size_t kSmem = 1024 + (size_t)kSmemUsed;
+// fp32 staging of 64 rows x 128 (V rows in the load phase, output rows at the end) over the L / T / X area
+constexpr int kStage = 132;              // row stride in floats (16-byte rows, conflict-free column reads)
+static_assert(C * kStage * 4 <= oVec - oL, "staging area");
 // TMEM columns
 constexpr uint32_t tA = 0, tQK = 64, tU = 128, tW = 256, tS = 384;
 
@@ -113,7 +117,7 @@ struct Args {
   int gate_sigmoid;
   int* err;
   unsigned long long timeout_ns;
-  long long* trace;             // optional: %globaltimer at each phase start of CTA (0, 0), [chunks][10]
+  long long* trace;             // optional: %globaltimer at phase starts of CTA (0, 0), [chunks][16]
 };
 
 // Wait for an MMA commit; every thread polls (bounded). False (and the shared abort flag set) on timeout.
@@ -186,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Args a) {
     const int nreal = min(C, a.n_tok - t0);
     const int64_t row0 = (int64_t)b * a.n_tok + t0;
     // ---------------------------------------------------------------- P0: load the chunk
-    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 10 + 0] = (long long)globaltimer_ns();
+    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 16 + 0] = (long long)globaltimer_ns();
     if (warp == 0) {                     // inclusive cumulative log decay and beta (padded tokens: g 0, beta 0)
       float gg[2], bb[2];
 #pragma unroll
@@ -213,41 +217,53 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Args a) {
     }
     __syncthreads();
     {
-      // Q and K rows: two threads per token row (64 columns each)
+      // Q and K rows (two threads per token row, 64 columns each) into their tiles, V rows (fp32) into the
+      // staging area for the transposed operands
       const int i = tid >> 1, half = tid & 1;
       const bool real = i < nreal;
       const __nv_bfloat16* qp = a.q + ((row0 + i) * a.nk + hk) * D + 64 * half;
       const __nv_bfloat16* kp = a.k + ((row0 + i) * a.nk + hk) * D + 64 * half;
+      const float* vp = a.qkv + (row0 + i) * a.Cq + 2 * a.nk * D + hv * D + 64 * half;
+      float* stg = reinterpret_cast<float*>(g + oL) + i * kStage + 64 * half;
 #pragma unroll
       for (int c8 = 0; c8 < 64; c8 += 8) {
         float vq[8], vk[8];
+        float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
         if (real) {
           ld_chunk8(qp + c8, vq);
           ld_chunk8(kp + c8, vk);
+          v0 = *reinterpret_cast<const float4*>(vp + c8);
+          v1 = *reinterpret_cast<const float4*>(vp + c8 + 4);
         } else {
 #pragma unroll
           for (int e = 0; e < 8; ++e) vq[e] = vk[e] = 0.f;
         }
         st_chunk8(base + oQ, i, 64 * half + c8, C, vq);
         st_chunk8(base + oK, i, 64 * half + c8, C, vk);
+        *reinterpret_cast<float4*>(stg + c8) = v0;
+        *reinterpret_cast<float4*>(stg + c8 + 4) = v1;
       }
-      // transposed operands: thread = feature n (a value column or a key column), walking the chunk's tokens
+    }
+    __syncthreads();
+    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 16 + 10] = (long long)globaltimer_ns();
+    {
+      // transposed operands: thread = feature n, reading column n of the staged V rows and of the K tile
       const int n = tid;
       const float gl = sgc[C - 1];
-      const float* vcol = a.qkv + row0 * a.Cq + 2 * a.nk * D + hv * D + n;
-      const __nv_bfloat16* kcol = a.k + (row0 * a.nk + hk) * D + n;
-#pragma unroll 4
+      const float* stg = reinterpret_cast<const float*>(g + oL);
+      const uint8_t* ktile = g + oK;
+#pragma unroll 2
       for (int j8 = 0; j8 < C; j8 += 8) {
         float vb[8], kb[8], kd[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int j = j8 + e;
-          const bool real = j < nreal;
-          const float vv = real ? vcol[(int64_t)j * a.Cq] : 0.f;
-          const float kk = real ? __bfloat162float(kcol[(int64_t)j * a.nk * D]) : 0.f;
+          const float vv = stg[j * kStage + n];
+          const float kk = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(ktile + sw_off(j, n, C)));
+          const float gj = sgc[j];
           vb[e] = sbeta[j] * vv;
-          kb[e] = sbeta[j] * __expf(sgc[j]) * kk;
-          kd[e] = __expf(gl - sgc[j]) * kk;
+          kb[e] = sbeta[j] * __expf(gj) * kk;
+          kd[e] = __expf(gl - gj) * kk;
         }
         st_chunk8(base + oVb, n, j8, D, vb);
         st_chunk8(base + oKb, n, j8, D, kb);
@@ -257,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Args a) {
     fence_proxy_async_smem();
     __syncthreads();
     // ---------------------------------------------------------------- P1: K K^T and Q K^T
-    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 10 + 1] = (long long)globaltimer_ns();
+    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 16 + 1] = (long long)globaltimer_ns();
     if (tid == 0 && !*abort_flag) {
       tc_fence_after();
       mma_tiles(tmem + tA, base + oK, C, base + oK, C, D / 16, id64x64, false);
@@ -270,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Args a) {
     phase ^= 1u;
     tc_fence_after();
     // ---------------------------------------------------------------- P2: L (fp32) and P (bf16) rows
-    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 10 + 2] = (long long)globaltimer_ns();
+    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 16 + 2] = (long long)globaltimer_ns();
     {
       uint32_t ra[32], rq[32];
       float l[C], p[C];
@@ -301,27 +317,60 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Args a) {
     }
     __syncthreads();
     // ---------------------------------------------------------------- P3: T = (I + L)^-1, one column per thread
-    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 10 + 3] = (long long)globaltimer_ns();
-    if (tid < C) {
-      const int c = tid;
-      float* tc = sTf;                   // [row][col], column c owned by thread c
-      for (int i = 0; i < C; ++i) {
-        float v;
-        if (i < c) v = 0.f;
-        else if (i == c) v = 1.f;
-        else {
-          float s = 0.f;
-          for (int jj = c; jj < i; ++jj) s += sL[i * C + jj] * tc[jj * C + c];
-          v = -s;
+    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 16 + 3] = (long long)globaltimer_ns();
+    {
+      // blocked: the four 16 x 16 diagonal blocks by forward substitution (one column per thread), then the
+      // off-diagonal blocks by block diagonals, T_ij = -T_ii sum_{k=j}^{i-1} L_ik T_kj (16 x 16 products)
+      float* sX = reinterpret_cast<float*>(g + oX);
+      if (tid < C) {
+        const int kb = tid >> 4, c = tid & 15, col = 16 * kb + c;
+        for (int r = 0; r < 16 * kb; ++r) sTf[r * C + col] = 0.f;
+        for (int ri = 0; ri < 16; ++ri) {
+          const int r = 16 * kb + ri;
+          float v;
+          if (ri < c) {
+            v = 0.f;
+          } else if (ri == c) {
+            v = 1.f;
+          } else {
+            float acc = 0.f;
+            for (int jj = c; jj < ri; ++jj) acc += sL[r * C + 16 * kb + jj] * sTf[(16 * kb + jj) * C + col];
+            v = -acc;
+          }
+          sTf[r * C + col] = v;
         }
-        tc[i * C + c] = v;
-        st_bf16(base + oT + sw_off(i, c, C), v);
+        for (int r = 16 * kb + 16; r < C; ++r) sTf[r * C + col] = 0.f;   // below: filled by the block levels
+      }
+      __syncthreads();
+      for (int d = 1; d < 4; ++d) {
+        const int nb = 4 - d;
+        for (int e = tid; e < nb * 256; e += kThreads) {
+          const int bj = e >> 8, bi = bj + d, r = (e >> 4) & 15, c = e & 15;
+          float acc = 0.f;
+          for (int kk = bj; kk < bi; ++kk) {
+#pragma unroll
+            for (int m = 0; m < 16; ++m) acc += sL[(16 * bi + r) * C + 16 * kk + m] * sTf[(16 * kk + m) * C + 16 * bj + c];
+          }
+          sX[e] = acc;
+        }
+        __syncthreads();
+        for (int e = tid; e < nb * 256; e += kThreads) {
+          const int bj = e >> 8, bi = bj + d, r = (e >> 4) & 15, c = e & 15;
+          float acc = 0.f;
+          for (int m = 0; m <= r; ++m) acc += sTf[(16 * bi + r) * C + 16 * bi + m] * sX[(bj << 8) + (m << 4) + c];
+          sTf[(16 * bi + r) * C + 16 * bj + c] = -acc;
+        }
+        __syncthreads();
+      }
+      for (int e = tid; e < C * 8; e += kThreads) {     // bf16 operand rows
+        const int r = e >> 3, c8 = (e & 7) * 8;
+        st_chunk8(base + oT, r, c8, C, sTf + r * C + c8);
       }
     }
     fence_proxy_async_smem();
     __syncthreads();
     // ---------------------------------------------------------------- P4: U = T (beta V), W = T (beta e^gc K)
-    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 10 + 4] = (long long)globaltimer_ns();
+    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 16 + 4] = (long long)globaltimer_ns();
     if (tid == 0 && !*abort_flag) {
       tc_fence_after();
       mma_tiles(tmem + tU, base + oT, C, base + oVb, D, C / 16, id64x128, false);
@@ -334,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Args a) {
     phase ^= 1u;
     tc_fence_after();
     // ---------------------------------------------------------------- P5: W rows -> bf16 operand
-    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 10 + 5] = (long long)globaltimer_ns();
+    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 16 + 5] = (long long)globaltimer_ns();
     {
       uint32_t r[32];
 #pragma unroll
@@ -355,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Args a) {
     tc_fence_before();
     __syncthreads();
     // ---------------------------------------------------------------- P6: V_new = U - W S, O1 = Q S
-    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 10 + 6] = (long long)globaltimer_ns();
+    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 16 + 6] = (long long)globaltimer_ns();
     if (tid == 0 && !*abort_flag) {
       tc_fence_after();
       mma_tiles(tmem + tU, base + oW, C, base + oS, D, D / 16, id64x128_neg, true);
@@ -368,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Args a) {
     phase ^= 1u;
     tc_fence_after();
     // ---------------------------------------------------------------- P7: V_new^T, e^gc O1, e^gl S
-    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 10 + 7] = (long long)globaltimer_ns();
+    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 16 + 7] = (long long)globaltimer_ns();
     {
       const float gl = sgc[C - 1];
       uint32_t r[32];
@@ -403,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Args a) {
     tc_fence_before();
     __syncthreads();
     // ---------------------------------------------------------------- P8: O += P V_new, S += Kd^T V_new
-    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 10 + 8] = (long long)globaltimer_ns();
+    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 16 + 8] = (long long)globaltimer_ns();
     if (tid == 0 && !*abort_flag) {
       tc_fence_after();
       mma_tiles(tmem + tW, base + oP, C, base + oVn, D, C / 16, id64x128, true);
@@ -416,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Args a) {
     phase ^= 1u;
     tc_fence_after();
     // ---------------------------------------------------------------- P9: output rows, S^T for the next chunk
-    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 10 + 9] = (long long)globaltimer_ns();
+    if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 16 + 9] = (long long)globaltimer_ns();
     {
       float o[D];
       uint32_t r[32];
@@ -428,21 +477,40 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Args a) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[32 * c + e] = __uint_as_float(r[e]);
       }
-      if (row_lane && ti < nreal && !*abort_flag) {
+      // rows normalized by their own threads into the staging area, then written out column-parallel (the z
+      // gates read and the outputs written in full rows of 128 per warp instruction)
+      float* stg = reinterpret_cast<float*>(g + oL);
+      if (row_lane) {
         float ss = 0.f;
 #pragma unroll
         for (int n = 0; n < D; ++n) ss += o[n] * o[n];
         const float rn = rsqrtf(ss / D + a.eps);
-        const int64_t row = row0 + ti;
-        const float* z = a.proj + row * a.ldp + a.Cq + hv * D;
-        __half* op = a.out + row * (a.nv * D) + hv * D;
 #pragma unroll
-        for (int n = 0; n < D; ++n) {
-          const float zz = z[n];
-          const float gz = a.gate_sigmoid ? sigm_f(zz) : zz * sigm_f(zz);
-          op[n] = __float2half_rn(o[n] * rn * a.norm_w[n] * gz);
+        for (int n = 0; n < D; n += 4)
+          *reinterpret_cast<float4*>(stg + ti * kStage + n) =
+              make_float4(o[n] * rn, o[n + 1] * rn, o[n + 2] * rn, o[n + 3] * rn);
+      }
+      __syncthreads();
+      if (!*abort_flag) {
+        const int n = tid;
+        const float nw = a.norm_w[n];
+        const float* zp = a.proj + row0 * a.ldp + a.Cq + hv * D + n;
+        __half* op = a.out + row0 * (a.nv * D) + hv * D + n;
+        for (int i0 = 0; i0 < nreal; i0 += 16) {
+          float zz[16];                  // a batch of gate loads in flight before the stores
+#pragma unroll
+          for (int e = 0; e < 16; ++e) zz[e] = i0 + e < nreal ? __ldg(zp + (int64_t)(i0 + e) * a.ldp) : 0.f;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int i = i0 + e;
+            if (i < nreal) {
+              const float gz = a.gate_sigmoid ? sigm_f(zz[e]) : zz[e] * sigm_f(zz[e]);
+              op[(int64_t)i * (a.nv * D)] = __float2half_rn(stg[i * kStage + n] * nw * gz);
+            }
+          }
         }
       }
+      if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 16 + 11] = (long long)globaltimer_ns();
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         tmem_ld16(tmem + lane_base + tS + 32 * c, *reinterpret_cast<uint32_t(*)[16]>(r));
@@ -451,6 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Args a) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) st_bf16(base + oS + sw_off(32 * c + e, tid, D), __uint_as_float(r[e]));
       }
+      if (a.trace && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) a.trace[ch * 16 + 12] = (long long)globaltimer_ns();
     }
     fence_proxy_async_smem();
     __syncthreads();
@@ -573,7 +642,7 @@ void gdn_chunk(torch::Tensor qkv, torch::Tensor proj, torch::Tensor ssm, torch::
   a.err = err.data_ptr<int32_t>();
   a.timeout_ns = (unsigned long long)timeout_ns;
   if (trace) {
-    TORCH_CHECK(trace->scalar_type() == torch::kInt64 && trace->numel() >= (n_tok + C - 1) / C * 10, "trace int64");
+    TORCH_CHECK(trace->scalar_type() == torch::kInt64 && trace->numel() >= (n_tok + C - 1) / C * 16, "trace int64");
     a.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
   }
   static bool attr = false;

@@ -228,7 +228,7 @@ def bench_gdn_prefill(args):
     out = torch.empty(n, nv * dv, dtype=torch.float16, device=dev)
     err = native.err_word(dev)
     C = native.C()
-    trace = torch.zeros((n + 63) // 64 * 10, dtype=torch.int64, device=dev)
+    trace = torch.zeros((n + 63) // 64 * 16, dtype=torch.int64, device=dev)
 
     def chunked(tr=None):
         C.gdn_chunk(qkv, proj, ssm, A_log, dt, nw, slots, out, nk, nv, n, cfg.rms_eps, 0, err,
@@ -237,12 +237,16 @@ def bench_gdn_prefill(args):
     chunked(trace)
     torch.cuda.synchronize()
     native.check_error()
-    tr = trace.view(-1, 10).double().cpu()
-    steps = (tr[:, 1:] - tr[:, :-1]).mean(0) / 1e3
+    tr = trace.view(-1, 16).double().cpu()
+    marks = torch.cat([tr[:-1, :10], tr[1:, :1]], 1)            # phase starts P0..P9, next chunk's P0
+    steps = (marks[:, 1:] - marks[:, :-1]).mean(0) / 1e3
     per_chunk = ((tr[1:, 0] - tr[:-1, 0]).mean() / 1e3).item() if tr.shape[0] > 1 else 0.0
+    sub = {"p0_rows_us": round(((tr[:, 10] - tr[:, 0]).mean() / 1e3).item(), 2),
+           "p9_out_us": round(((tr[:, 11] - tr[:, 9]).mean() / 1e3).item(), 2),
+           "p9_state_us": round(((tr[:, 12] - tr[:, 11]).mean() / 1e3).item(), 2)}
     print(json.dumps({"case": "gdn_prefill_chunked", "tokens": n, "heads": nv, "ms": round(t, 4),
                       "tok_per_s_layer": round(n / t * 1e3, 1), "chunk_us": round(per_chunk, 2),
-                      "phase_us": [round(x, 2) for x in steps.tolist()]}))
+                      "phase_us": [round(x, 2) for x in steps.tolist()], **sub}))
 
 
 def bench_mla(args):
