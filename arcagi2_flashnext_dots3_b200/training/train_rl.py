@@ -76,6 +76,8 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--save-every", type=int, default=0)
     ap.add_argument("--dry", action="store_true", help="forward/backward only, no optimizer step")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="reduce the gradients after the whole backward instead of from the backward's hooks")
     a = ap.parse_args(argv)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -99,7 +101,7 @@ def main(argv=None):
         m.router.requires_grad_("router" in a.trainable)
     groups = [g for g in model.param_groups(a.lr_scales, a.lr_router, a.lr_norms)
               if all(p.requires_grad for p in g["params"])]
-    opt = ShardedAdam(groups)
+    opt = ShardedAdam(groups, overlap=not a.no_overlap)
     files = sorted(glob.glob(os.path.join(a.data, "*.npz")))
     if not files:
         raise SystemExit(f"no records in {a.data}")
@@ -112,6 +114,10 @@ def main(argv=None):
     logf = open(out / "log.jsonl", "a") if rank == 0 else None
     while step < total:
         t0 = time.time()
+        if cuda:                             # device time of the step (backward + reduction + update), max over ranks
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            ev0.record()
         batch = order[step * a.per_step:(step + 1) * a.per_step][rank::world]
         opt.zero_grad()
         st = {"lp": 0.0, "ent": 0.0, "n": 0, "clipped": 0}
@@ -132,10 +138,19 @@ def main(argv=None):
             gnorm = opt.grad_norm()
             opt.step(lr_factor(step, total, a.warmup))
         step += 1
+        dev_ms = None
+        if cuda:
+            ev1.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([ev0.elapsed_time(ev1)], device=dev)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dev_ms = round(float(t), 2)
         if logf:
             logf.write(json.dumps({"step": step, "loss_lp": st["lp"] / max(1, st["n"]), "ent": st["ent"] / max(1, st["n"]),
                                    "tokens": st["n"], "grad_norm": gnorm, "lr_factor": lr_factor(step - 1, total, a.warmup),
-                                   "s": round(time.time() - t0, 3)}) + "\n")
+                                   "s": round(time.time() - t0, 3), "step_ms_device_max_ranks": dev_ms,
+                                   "overlap": not a.no_overlap, "world": world}) + "\n")
             logf.flush()
         if a.save_every and step % a.save_every == 0:
             ckpt.save(out, step, model, opt, rank)
