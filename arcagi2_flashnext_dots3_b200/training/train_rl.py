@@ -76,10 +76,20 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--save-every", type=int, default=0)
     ap.add_argument("--dry", action="store_true", help="forward/backward only, no optimizer step")
+    ap.add_argument("--write-synthetic", type=int, nargs=2, metavar=("N", "L"), default=None,
+                    help="write N random rollout records of L tokens (second half generated) into --data and exit")
     ap.add_argument("--no-overlap", action="store_true",
                     help="reduce the gradients after the whole backward instead of from the backward's hooks")
     a = ap.parse_args(argv)
 
+    if a.write_synthetic:
+        n, L = a.write_synthetic
+        cfg, _ = load_model_weights(a.build, 1) if not a.build.startswith("random:") else (
+            CONFIGS[a.build.split(":", 1)[1]](), None)
+        rng = np.random.default_rng(a.seed)
+        write_records(a.data, [(rng.integers(0, cfg.vocab_size, L), np.arange(L // 2, L), float(rng.normal()))
+                               for _ in range(n)])
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     cuda = torch.cuda.is_available()
