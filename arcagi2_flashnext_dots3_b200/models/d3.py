@@ -248,19 +248,36 @@ class D3Model:
             raise RuntimeError("D3Model.logits: the LM head is vocabulary-sharded; select tokens with pick()")
         return self._mm(x, self.W["lm_head"], f8=False)
 
-    def pick(self, x: torch.Tensor, temperature: float = 0.0, seed: int = 0, step: int = 0) -> torch.Tensor:
-        """Next token per row (int32): greedy, or Gumbel-max temperature sampling with the sampler's counter RNG.
-        With the LM head split over the TP ranks (``vocab_range`` in the weights) only one (value, index) pair
-        per row crosses the group."""
+    def pick(self, x: torch.Tensor, temperature: float = 0.0, seed: int = 0, step: int = 0, top_k: int = 0,
+             top_p: float = 1.0) -> torch.Tensor:
+        """Next token per row (int32): greedy, Gumbel-max temperature sampling with the sampler's counter RNG, or
+        top-k / top-p sampling (the sampler's candidate rule). With the LM head split over the TP ranks
+        (``vocab_range`` in the weights) one (value, index) pair per row crosses the group for greedy and
+        full-vocabulary sampling, K pairs per row for top-k / top-p (:func:`..parallel.tp.sharded_sample`)."""
         lg = self._mm(x, self.W["lm_head"], f8=False)
+        filtered = temperature > 0 and (top_k > 0 or top_p < 1.0)
         if self.vocab_sharded:
             if getattr(self.tp, "fake", False):
+                if filtered:
+                    raise NotImplementedError("fake TP emulates the greedy / full-vocabulary pick only")
                 return self.tp.sharded_pick(lg, self.W["vocab_range"][0], temperature, seed, step)
-            from ..parallel.tp import sharded_pick
+            from ..parallel.tp import sharded_pick, sharded_sample
+            if filtered:
+                return sharded_sample(lg, self.W["vocab_range"][0], self.cfg.vocab_size, self.tp.group, temperature,
+                                      top_k, top_p, seed, step)
             return sharded_pick(lg, self.W["vocab_range"][0], self.tp.group, temperature, seed, step)
         if temperature <= 0:
             return ops.argmax(lg)
         from ..ops import sampling
+        if filtered:
+            B = lg.shape[0]
+            dev = lg.device
+            ids, _ = sampling.sample(lg.float().contiguous(), torch.full((B,), temperature, device=dev),
+                                     torch.full((B,), top_k, dtype=torch.int32, device=dev),
+                                     torch.full((B,), top_p, device=dev),
+                                     torch.full((B,), seed, dtype=torch.int64, device=dev),
+                                     torch.full((B,), step, dtype=torch.int64, device=dev), want_lp=False)
+            return ids
         u = sampling.uniform_torch(seed, step, torch.arange(lg.shape[1], device=lg.device))
         return (lg.float() / temperature - torch.log(-torch.log(u))[None, :]).argmax(-1).to(torch.int32)
 

@@ -233,8 +233,8 @@ def sharded_pick(local_logits: torch.Tensor, v0: int, group=None, temperature: f
     lowest index on ties. Because the noise of a token does not depend on which rank holds it, the result
     equals the token the unsharded CPU sampler (ops.sampling's torch path, top-k and top-p off) picks. The GPU
     sampler kernel evaluates the same noise with its own logf, which may differ from torch.log in the last bit,
-    so a near-tie between two tokens can resolve differently there. Top-k and top-p are not supported on the
-    sharded path: only greedy and full-vocabulary temperature sampling. Returns int32 [T]."""
+    so a near-tie between two tokens can resolve differently there. Top-k / top-p sampling over a split head is
+    :func:`sharded_sample`. Returns int32 [T]."""
     from ..ops import sampling
     x = local_logits.float()
     T, Vl = x.shape
@@ -257,6 +257,66 @@ def sharded_pick(local_logits: torch.Tensor, v0: int, group=None, temperature: f
         allp = torch.stack(parts)
     best = allp[:, :, 0].argmax(0)   # ranks hold increasing vocabulary ranges: the first max has the lowest index
     return allp[best, torch.arange(T, device=pair.device), 1].to(torch.int32)
+
+
+def sharded_sample(local_logits: torch.Tensor, v0: int, vocab: int, group=None, temperature: float = 1.0,
+                   top_k: int = 0, top_p: float = 1.0, seed: int = 0, step: int = 0) -> torch.Tensor:
+    """Top-k / top-p sampling when every TP rank holds the logits of its own vocabulary slice [v0, v0 + V_local)
+    of a `vocab`-token head. The rule is the unsharded sampler's (ops.sampling._sample_row): the K = min(top_k or
+    CAND, CAND, vocab) highest logits in (value desc, index asc) order, their fp32 cumulative exp((v - v_max) / T),
+    the top-p cut relative to that mass, one uniform from the counter hash at index `vocab` scaled by the kept
+    mass, the first candidate whose cumulative mass exceeds it. The global top K lies in the union of the ranks'
+    local top K, so each rank sends K (value, global index) pairs per row (an all-gather of world x K x 2 floats)
+    instead of the logits, and every rank draws the same token. On CPU ranks it returns the CPU sampler's token; on
+    GPU ranks the cumulative sums run as a parallel scan whose last bit can differ, so a near-tie may resolve
+    differently from the CPU. Greedy and full-vocabulary sampling (top_k 0, top_p 1) go to :func:`sharded_pick`.
+    Returns int32 [T]."""
+    from ..ops import sampling
+    import numpy as np
+    if temperature <= 0 or (top_k <= 0 and top_p >= 1.0):
+        return sharded_pick(local_logits, v0, group, temperature, seed, step)
+    x = local_logits.float()
+    T, Vl = x.shape
+    K = min(top_k if top_k > 0 else sampling.CAND, sampling.CAND, vocab)
+    kl = min(K, Vl)
+    vals = x.new_full((T, K), -float("inf"))
+    idx = torch.full((T, K), vocab, dtype=torch.float32, device=x.device)    # padding sorts after real tokens
+    if kl:
+        # local top kl in (value desc, index asc): stable sort on the values of the index-ordered slice
+        order = torch.sort(x, dim=-1, descending=True, stable=True).indices[:, :kl]
+        vals[:, :kl] = x.gather(1, order)
+        idx[:, :kl] = (order + v0).float()
+    pair = torch.stack([vals, idx], -1).contiguous()                          # [T, K, 2]
+    world = dist.get_world_size(group)
+    if dist.get_backend(group) == "nccl":
+        allp = torch.empty(world, T, K, 2, dtype=pair.dtype, device=pair.device)
+        dist.all_gather_into_tensor(allp, pair, group=group)
+    else:
+        parts = [torch.empty_like(pair) for _ in range(world)]
+        dist.all_gather(parts, pair, group=group)
+        allp = torch.stack(parts)
+    cand = allp.permute(1, 0, 2, 3).reshape(T, world * K, 2)
+    out = torch.empty(T, dtype=torch.int32)
+    u = float(sampling.uniform(seed, step, [vocab])[0])
+    for r in range(T):
+        v, gi = cand[r, :, 0], cand[r, :, 1]
+        o1 = torch.argsort(gi, stable=True)                                   # index asc, then value desc (stable)
+        o2 = o1[torch.sort(v[o1], descending=True, stable=True).indices][:K]
+        vs, ids = v[o2], gi[o2].long()
+        if x.is_cuda:
+            cum = torch.cumsum(torch.exp((vs - vs[0]) / temperature), 0)
+            cut = K - 1 if top_p >= 1.0 else int(torch.nonzero(cum >= top_p * cum[-1])[0])
+            lim = u * float(cum[cut])
+            hit = torch.nonzero(cum[: cut + 1] > lim)
+            out[r] = int(ids[int(hit[0]) if len(hit) else cut])
+        else:
+            vv = vs.numpy()
+            cum = np.cumsum(np.exp((vv - vv[0]) / np.float32(temperature)).astype(np.float32), dtype=np.float32)
+            cut = K - 1 if top_p >= 1.0 else int(np.argmax(cum >= np.float32(top_p) * cum[-1]))
+            lim = sampling.uniform(seed, step, [vocab])[0] * cum[cut]
+            hit = cum[: cut + 1] > lim
+            out[r] = int(ids[int(np.argmax(hit)) if hit.any() else cut])
+    return out.to(local_logits.device)
 
 
 def shard_d3_weights(W: dict, cfg, rank: int, world: int, shard_vocab: bool = False) -> dict:

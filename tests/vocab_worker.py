@@ -24,6 +24,15 @@ def main():
         got = sharded_pick(logits[:, v0:v1], v0, temperature=temp, seed=seed, step=step)
         want = [sampling._sample_row(logits[r], temp, 0, 1.0, seed, step) for r in range(T)]
         assert got.tolist() == want, (got.tolist(), want)
+    # top-k / top-p over the split head: the unsharded CPU sampler's tokens
+    from arcagi2_flashnext_dots3_b200.parallel.tp import sharded_sample
+    lgk = logits.clone()
+    lgk[4, 5] = lgk[4, 995] = lgk[4].max() + 0.5      # a tie inside the top k across ranks
+    for seed, step, temp, k, p in [(5, 1, 1.0, 20, 1.0), (6, 3, 0.8, 0, 0.9), (7, 8, 1.3, 50, 0.5),
+                                   (8, 0, 0.6, 3, 0.95), (9, 2, 1.0, 2000, 0.99)]:
+        got = sharded_sample(lgk[:, v0:v1], v0, V, temperature=temp, top_k=k, top_p=p, seed=seed, step=step)
+        want = [sampling._sample_row(lgk[r], temp, k, p, seed, step) for r in range(T)]
+        assert got.tolist() == want, (seed, got.tolist(), want)
     # speculative verification over the split head: same accepted counts and next tokens as unsharded
     from arcagi2_flashnext_dots3_b200.parallel.tp import sharded_speculative_accept
     B, k = 5, 3
