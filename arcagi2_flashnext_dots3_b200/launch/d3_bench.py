@@ -39,6 +39,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl", "q8", "q4"])
     ap.add_argument("--eager", action="store_true", help="no CUDA graph (for launch lists)")
+    ap.add_argument("--sp", action="store_true",
+                    help="sequence parallel: residual rows split over the TP ranks, NCCL reduce-scatter / all-gather")
     ap.add_argument("--shard-vocab", action="store_true",
                     help="with TP: each rank holds its slice of the LM head; tokens via the sharded pick")
     args = ap.parse_args()
@@ -56,7 +58,8 @@ def main():
     if world > 1:
         from ..parallel.tp import TPGroup, tp_config
         lc = tp_config(cfg, world)
-        tp = TPGroup(rank, world, dev, max_tokens=max(64, args.batch), hidden=cfg.hidden_size, comm=args.comm)
+        tp = TPGroup(rank, world, dev, max_tokens=max(64, args.batch), hidden=cfg.hidden_size,
+                     comm="nccl" if args.sp else args.comm, sequence_parallel=args.sp)
     W = random_engine(cfg, dev, seed=0, tp=(rank, world) if world > 1 else None,
                       shard_vocab=args.shard_vocab and world > 1)
     B, total = args.batch, args.ctx + args.warmup + args.steps + 16

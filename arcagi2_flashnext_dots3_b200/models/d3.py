@@ -138,6 +138,8 @@ class D3Model:
         o_lat = d3.mla_attn(q_lat, q_pe, c.latent[l], c.block_table, slots, positions, n_tok, sel, window,
                             self.scale)
         o = self._absorb(o_lat, p, "uv")                        # [H, T, dv]
+        if self.tp is not None and getattr(self.tp, "sp", False):   # sequence parallel: the partial, scattered later
+            return self._mm(d3.mla_out(o, gate), p["o"])
         if self.tp is not None:  # row-parallel o-projection fused with the all-reduce; adds into h itself
             self.tp.linear_allreduce_add(self, d3.mla_out(o, gate), p["o"], self._h)
             return None
@@ -178,6 +180,8 @@ class D3Model:
         sg = torch.full((T,), float("inf") if tp.rank == 0 else float("-inf"), device=x.device)
         part = torch.zeros(T, cfg.hidden_size, dtype=torch.float32, device=x.device)
         ops.moe_combine(part, ypair, pp, wl, ysh, sg, torch.ones(T, 1, dtype=torch.float32, device=x.device))
+        if h is None:          # sequence parallel: the caller reduce-scatters the partial
+            return part
         tp.allreduce_add(h, part)
 
     def _moe(self, x, p, h):
@@ -218,6 +222,8 @@ class D3Model:
 
     def step_from_h(self, h: torch.Tensor, slots: torch.Tensor, positions: torch.Tensor, n_tok: int = 1):
         cfg, W = self.cfg, self.W
+        if self.tp is not None and getattr(self.tp, "sp", False):
+            return self._step_sp(h.float(), slots, positions, n_tok)
         h = h.float().contiguous()
         self._h = h
         if self.tp is not None and hasattr(self.tp, "begin_forward"):
@@ -234,6 +240,35 @@ class D3Model:
                 sact = self._mm(x, L["mlp"]["gu"], epi=wgemm.EPI_SILU_MUL, out_dtype=self.act)
                 y = self._mm(sact, L["mlp"]["d"])
         return d3.add_rms(h, y, W["norm"], cfg.rms_eps, self.act)
+
+    def _step_sp(self, h, slots, positions, n_tok):
+        """Sequence-parallel layer loop: this rank keeps T/W rows of the residual stream (zero-padded to a multiple
+        of the group size) and normalizes only those; the attention and MoE partials (row-parallel products over
+        this rank's heads / experts, all tokens) are reduce-scattered into it, and the normalized rows are
+        all-gathered before the next column-parallel GEMM. The dense MLP layers are replicated: their output rows
+        are sliced. Returns the final normalized hidden states of all T tokens."""
+        cfg, W, tp = self.cfg, self.W, self.tp
+        T = h.shape[0]
+        Tp, Tl = tp.sp_rows(T)
+        if Tp != T:
+            h = torch.nn.functional.pad(h, (0, 0, 0, Tp - T))
+        h_loc = h[tp.rank * Tl:(tp.rank + 1) * Tl].contiguous()
+        if hasattr(tp, "begin_forward"):
+            tp.begin_forward()
+        y = None
+        for l, L in enumerate(W["layers"]):
+            x = tp.all_gather(d3.add_rms(h_loc, y, L["ln1"], cfg.rms_eps, self.act), T)
+            y = tp.reduce_scatter(self._attn(x, L["attn"], l, slots, positions, n_tok))
+            x = tp.all_gather(d3.add_rms(h_loc, y, L["ln2"], cfg.rms_eps, self.act), T)
+            if cfg.is_moe(l):
+                y = tp.reduce_scatter(self._moe_tp(x, L["moe"], None))
+            else:
+                sact = self._mm(x, L["mlp"]["gu"], epi=wgemm.EPI_SILU_MUL, out_dtype=self.act)
+                full = self._mm(sact, L["mlp"]["d"]).float()
+                if Tp != T:
+                    full = torch.nn.functional.pad(full, (0, 0, 0, Tp - T))
+                y = full[tp.rank * Tl:(tp.rank + 1) * Tl].contiguous()
+        return tp.all_gather(d3.add_rms(h_loc, y, W["norm"], cfg.rms_eps, self.act), T)
 
     @property
     def vocab_sharded(self) -> bool:

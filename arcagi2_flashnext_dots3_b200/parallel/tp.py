@@ -30,11 +30,16 @@ def tp_config(cfg, world: int):
 
 class TPGroup:
     def __init__(self, rank: int, world: int, device, max_tokens: int, hidden: int, group=None, comm: str = "fused",
-                 timeout_ns: int = None, q_bits: int = 8, hadamard: bool = False, error_feedback: bool = False):
+                 timeout_ns: int = None, q_bits: int = 8, hadamard: bool = False, error_feedback: bool = False,
+                 sequence_parallel: bool = False):
         """``comm="q8"`` options: ``q_bits`` 8 or 4 (codes -7..7), ``hadamard`` (128-point Walsh-Hadamard rotation
         of every scale group before quantizing), ``error_feedback`` (within one forward pass each rank adds the
         quantization error it carried out of the previous all-reduce to its next input; :meth:`begin_forward`
-        clears the carry)."""
+        clears the carry). ``sequence_parallel``: the residual stream is split by tokens over the ranks; the
+        row-parallel outputs are reduce-scattered into it and the normalized rows all-gathered before the next
+        column-parallel GEMM (:meth:`reduce_scatter`, :meth:`all_gather`; the reference's TP groups with
+        reduce-scatter / all-gather, flashnext/kaggle/code_dataset/fnext/base/host_dp.py:131-144)."""
+        self.sp = sequence_parallel
         if comm == "q4":     # shorthand: 4-bit payload with rotation and error feedback
             comm, q_bits, hadamard, error_feedback = "q8", 4, True, True
         self.rank, self.world, self.comm = rank, world, comm
@@ -78,6 +83,41 @@ class TPGroup:
             self.carry = torch.zeros(self.slot, dtype=torch.float32, device=self.device) if error_feedback else None
         elif comm != "nccl":
             raise ValueError(comm)
+
+    # ------------------------------------------------------------------------------------ sequence parallel
+    def sp_rows(self, T: int):
+        """(padded token count, rows per rank) of a T-token residual split over the ranks."""
+        Tl = -(-T // self.world)
+        return Tl * self.world, Tl
+
+    def reduce_scatter(self, partial: torch.Tensor) -> torch.Tensor:
+        """This rank's token rows [Tl, H] of the sum over ranks of partial [T, H] (fp32; T padded to world * Tl)."""
+        T, H = partial.shape
+        Tp, Tl = self.sp_rows(T)
+        x = partial.float()
+        if Tp != T:
+            x = torch.nn.functional.pad(x, (0, 0, 0, Tp - T))
+        x = x.contiguous()
+        out = torch.empty(Tl, H, dtype=torch.float32, device=x.device)
+        if x.is_cuda:
+            dist.reduce_scatter_tensor(out, x, group=self.group)
+        else:   # gloo has no reduce-scatter
+            dist.all_reduce(x, group=self.group)
+            out.copy_(x[self.rank * Tl:(self.rank + 1) * Tl])
+        return out
+
+    def all_gather(self, x_loc: torch.Tensor, T: int) -> torch.Tensor:
+        """The first T rows of every rank's [Tl, C] rows stacked in rank order."""
+        x_loc = x_loc.contiguous()
+        Tl = x_loc.shape[0]
+        if x_loc.is_cuda:
+            out = torch.empty(Tl * self.world, *x_loc.shape[1:], dtype=x_loc.dtype, device=x_loc.device)
+            dist.all_gather_into_tensor(out, x_loc, group=self.group)
+        else:
+            parts = [torch.empty_like(x_loc) for _ in range(self.world)]
+            dist.all_gather(parts, x_loc, group=self.group)
+            out = torch.cat(parts)
+        return out[:T]
 
     # ------------------------------------------------------------------------------------ fused GEMM path
     def begin(self):

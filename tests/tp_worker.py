@@ -50,6 +50,16 @@ def main():
         native.check_error(dev)
     err = (got - ref).abs().max() / ref.abs().max()
     tol = 2e-2 if (cuda or comm == "q8") else 1e-4
+    if comm == "nccl":
+        # sequence parallel: residual rows split over the ranks, reduce-scatter / all-gather around the layers
+        tps = TPGroup(rank, world, dev, max_tokens=32, hidden=cfg.hidden_size, comm="nccl", sequence_parallel=True)
+        ms = D3Model(lc, to_engine(shard_d3_weights(W, cfg, rank, world), lc, dev),
+                     allocate_caches(lc, dev, 2, 64, block_size=16), dev, tp=tps)
+        got_sp = run(ms, ids, dev)
+        if cuda:
+            torch.cuda.synchronize()
+        err_sp = float((got_sp - ref).abs().max() / ref.abs().max())
+        assert err_sp < tol, (rank, "sp", err_sp)
     if comm == "q8":
         # the kernel's quantized all-reduce equals its torch statement on the gathered partials
         from arcagi2_flashnext_dots3_b200.parallel.tp import qar_reference
