@@ -5,10 +5,11 @@
 // CUDA cores by spending about one integer instruction per weight:
 //
 //   * activations are quantized once per row and 128-column group to int8 (scale = absmax / 127) by
-//     `gemv_quant`, which also stores the group sums of the codes;
+//     `gemv_quant`, which also stores the group sums of the codes, with the columns of every 8-column block in the
+//     order the 4-bit words unpack into (lowbit.cuh);
 //   * each thread owns one weight row of a 128-row tile and streams that row's code words from HBM (word i of
 //     row r at (i * 128 + r) * 4: a warp reads 128 contiguous bytes);
-//   * codes are moved into byte lanes in natural column order with shift / mask / byte-permute and multiplied
+//   * codes are moved into byte lanes in that order with shift / mask (/ byte-permute below 4 bits) and multiplied
 //     with the int8 activations by `dp4a` (4 products per instruction), exact in int32;
 //   * per (row, group): y += s_w * s_x * (sum q*x - z * sum x) in fp32.
 //
@@ -49,8 +50,13 @@ __global__ void gemv_quant_kernel(const __half* x, int rows, int K, int8_t* xq, 
   const float inv = m > 0.f ? 127.f / m : 0.f;
   const int q0 = __float2int_rn(a.x * inv), q1 = __float2int_rn(a.y * inv);
   const int q2 = __float2int_rn(b.x * inv), q3 = __float2int_rn(b.y * inv);
-  reinterpret_cast<uint32_t*>(xq + (int64_t)r * K + g * 128)[lane] =
+  const uint32_t own =
       (uint32_t)(q0 & 255) | ((uint32_t)(q1 & 255) << 8) | ((uint32_t)(q2 & 255) << 16) | ((uint32_t)(q3 & 255) << 24);
+  // columns of each 8-column block in the order [0, 4, 1, 5, 2, 6, 3, 7] (lowbit.cuh): lanes 2b and 2b+1 hold
+  // columns 8b..8b+3 and 8b+4..8b+7 and write words [c0 c4 c1 c5] and [c2 c6 c3 c7]
+  const uint32_t other = __shfl_xor_sync(0xffffffffu, own, 1);
+  reinterpret_cast<uint32_t*>(xq + (int64_t)r * K + g * 128)[lane] =
+      (lane & 1) ? __byte_perm(own, other, 0x3726) : __byte_perm(own, other, 0x5140);
   int sum = q0 + q1 + q2 + q3;
 #pragma unroll
   for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);

@@ -13,7 +13,7 @@
 //              2-D TMA in the 128-byte swizzle, the MMA's B operand as is) + the packed weight block (4.5 to
 //              8.6 KB, one 1-D bulk copy), 8 stages in flight
 //   warps 1-4  one thread per weight row (TMEM lane = row): read the row's code words from the stage, widen
-//              them to 128 bytes in natural column order and tcgen05.st them as the A operand of a TMEM slot
+//              them to 128 bytes in the activations' column order and tcgen05.st them as the A operand of a TMEM slot
 //              (5 slots of A 32 columns + D 16 columns). The last of the four warps to finish a group (an
 //              acquire-release counter per slot, no polling) issues its 4 x tcgen05.mma kind::i8 (M 128 rows,
 //              N 16 tokens, K 32, A read from tensor memory) and commits them to the slot's `done` and the

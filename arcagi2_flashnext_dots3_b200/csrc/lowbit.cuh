@@ -6,8 +6,10 @@
 //   3-bit: 5 pairs per word, pair p in bits 3(p%5) (even column) and 16+3(p%5) (odd column) of word p/5
 //   2-bit: 8 pairs per word, pair p in bits 2(p%8) and 16+2(p%8) of word p/8
 //
-// quad<FMT, M>(w) returns the unsigned codes of columns 4M..4M+3 as four bytes in natural column order (M = 0..31),
-// the int8 operand layout of both dp4a and the tcgen05 kind::i8 MMA.
+// The int8 activations of the grouped GEMV kernels are stored with the columns of every 8-column block in the order
+// [0, 4, 1, 5, 2, 6, 3, 7] (gemv_quant), the order in which the 4-bit words yield their codes with one mask each.
+// quad<FMT, M>(w) returns the unsigned codes at positions 4M..4M+3 of that order (M = 0..31) as four bytes: the
+// int8 operand layout of both dp4a and the tcgen05 kind::i8 MMA.
 #pragma once
 #include <cstdint>
 
@@ -17,19 +19,18 @@ namespace lowbit {
 template <int FMT, int M>
 __device__ __forceinline__ uint32_t quad(const uint32_t* w) {
   if constexpr (FMT == 4) {
-    // word i = columns 8i..8i+7: pairs 4i+k in bits 4k (even col) and 16+4k (odd col)
+    // word i = columns 8i..8i+7: x & 0x0F0F0F0F = [c0, c4, c1, c5], (x >> 4) & 0x0F0F0F0F = [c2, c6, c3, c7]
     const uint32_t x = w[M / 2];
-    const uint32_t A = x & 0x0F0F0F0Fu;          // [c0, c4, c1, c5]
-    const uint32_t B = (x >> 4) & 0x0F0F0F0Fu;   // [c2, c6, c3, c7]
-    return (M & 1) ? __byte_perm(A, B, 0x7531) : __byte_perm(A, B, 0x6420);
+    return (M & 1) ? (x >> 4) & 0x0F0F0F0Fu : x & 0x0F0F0F0Fu;
   } else {
-    // pairs in bits BITS*k (even col) and 16+BITS*k (odd col), PPW pairs per word
+    // pairs in bits BITS*k (even col) and 16+BITS*k (odd col), PPW pairs per word; block b = M / 2 holds pairs
+    // 4b..4b+3 = (c0 c1) (c2 c3) (c4 c5) (c6 c7): even M takes pairs 4b and 4b+2, odd M pairs 4b+1 and 4b+3
     constexpr int BITS = FMT, PPW = FMT == 3 ? 5 : 8;
     constexpr uint32_t MASK = ((1u << BITS) - 1u) * 0x00010001u;
-    constexpr int p0 = 2 * M, p1 = 2 * M + 1;
-    const uint32_t P0 = (w[p0 / PPW] >> (BITS * (p0 % PPW))) & MASK;   // [c_{2p0}, 0, c_{2p0+1}, 0]
-    const uint32_t P1 = (w[p1 / PPW] >> (BITS * (p1 % PPW))) & MASK;
-    return __byte_perm(P0, P1, 0x6420);
+    constexpr int pa = 4 * (M / 2) + (M & 1), pb = pa + 2;
+    const uint32_t Pa = (w[pa / PPW] >> (BITS * (pa % PPW))) & MASK;   // [c_a, 0, c_a+1, 0]
+    const uint32_t Pb = (w[pb / PPW] >> (BITS * (pb % PPW))) & MASK;
+    return __byte_perm(Pa, Pb, 0x6240);
   }
 }
 
