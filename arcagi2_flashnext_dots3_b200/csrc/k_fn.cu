@@ -16,6 +16,7 @@
 #include <type_traits>
 #include <atomic>
 #include <cub/block/block_scan.cuh>
+#include "ptx.cuh"
 #include "kernels.h"
 
 namespace {
@@ -394,10 +395,100 @@ __global__ void __launch_bounds__(256) gdn_recur_kernel(const float* qkv, const 
   }
 }
 
+// Decode form (one token per sequence, bf16 state) for one (sequence, value head): the 32 KB state arrives by one
+// bulk copy into shared memory and leaves by one bulk store, and thread j owns column j of it: a first pass over
+// the rows forms (S^T k)_j, a second applies the update and accumulates o_j. The only block-wide steps are the q / k
+// norms and the output norm. The arithmetic is gdn_recur_kernel's (its sums over the rows run in one order here
+// instead of two halves).
+__global__ void __launch_bounds__(128) gdn_decode1_kernel(const float* qkv, const float* proj, int ldp,
+                                                          __nv_bfloat16* ssm, const int* slots, const float* A_log,
+                                                          const float* dt_bias, const float* norm_w, __half* out,
+                                                          int nk, int nv, float eps, int gate_sigmoid,
+                                                          const int* n_commit, int* err, uint64_t timeout_ns) {
+  constexpr int DK = 128, DV = 128;
+  __shared__ __align__(128) __nv_bfloat16 Ss[DK * DV];
+  __shared__ float q_s[DK], k_s[DK], red[8];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  const int b = blockIdx.x, hv = blockIdx.y, j = threadIdx.x, warp = j >> 5, lane = j & 31;
+  const int hk = hv / (nv / nk);
+  __nv_bfloat16* S = ssm + ((int64_t)slots[b] * nv + hv) * DK * DV;
+  const uint32_t sbar = fw::smem_u32(&bar), sS = fw::smem_u32(Ss);
+  if (j == 0) {
+    abort_flag = 0;
+    fw::mbar_init(sbar, 1);
+    fw::fence_mbar_init();
+  }
+  __syncthreads();
+  if (j == 0) {
+    fw::mbar_arrive_expect_tx(sbar, DK * DV * 2);
+    fw::tma_bulk_g2s(sS, S, DK * DV * 2, sbar, fw::l2_policy_evict_first());
+  }
+  const int C = 2 * nk * DK + nv * DV;
+  const float* x = qkv + (int64_t)b * C;
+  const float* pr = proj + (int64_t)b * ldp;
+  const float qv = x[hk * DK + j], kv = x[nk * DK + hk * DK + j];
+  float q2 = qv * qv, k2 = kv * kv;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    q2 += __shfl_xor_sync(0xffffffffu, q2, o);
+    k2 += __shfl_xor_sync(0xffffffffu, k2, o);
+  }
+  if (lane == 0) {
+    red[warp] = q2;
+    red[4 + warp] = k2;
+  }
+  __syncthreads();
+  const float qn = red[0] + red[1] + red[2] + red[3], kn = red[4] + red[5] + red[6] + red[7];
+  q_s[j] = qv * rsqrtf(qn + 1e-6f) * rsqrtf((float)DK);
+  k_s[j] = kv * rsqrtf(kn + 1e-6f);
+  const float beta = sigm(pr[C + nv * DV + hv]);
+  const float g = -__expf(A_log[hv]) * softplus(pr[C + nv * DV + nv + hv] + dt_bias[hv]);
+  const float dec = __expf(g);
+  const float vj = x[2 * nk * DK + hv * DV + j];
+  if (j == 0 && !fw::mbar_wait(sbar, 0, err, 6601, &abort_flag, timeout_ns)) abort_flag = 1;
+  __syncthreads();                       // q_s, k_s written; the state landed (or the wait gave up)
+  const bool ok = !abort_flag;
+  float o = 0.f;
+  if (ok) {
+    float acc = 0.f;
+#pragma unroll 8
+    for (int r = 0; r < DK; ++r) acc += __bfloat162float(Ss[r * DV + j]) * dec * k_s[r];
+    const float u = beta * (vj - acc);
+#pragma unroll 8
+    for (int r = 0; r < DK; ++r) {
+      const float sv = __bfloat162float(Ss[r * DV + j]) * dec + k_s[r] * u;
+      o += sv * q_s[r];
+      Ss[r * DV + j] = __float2bfloat16_rn(sv);
+    }
+  }
+  float o2 = o * o;
+#pragma unroll
+  for (int w = 16; w; w >>= 1) o2 += __shfl_xor_sync(0xffffffffu, o2, w);
+  __syncthreads();                       // every thread is past its reads of red
+  if (lane == 0) red[warp] = o2;
+  fw::fence_proxy_async_smem();          // the updated state is visible to the bulk store
+  __syncthreads();
+  if (ok) {
+    const float ss = red[0] + red[1] + red[2] + red[3];
+    const float on = o * rsqrtf(ss / DV + eps) * norm_w[j];
+    const float z = pr[C + hv * DV + j];
+    const float gz = gate_sigmoid ? sigm(z) : silu(z);
+    out[(int64_t)b * (nv * DV) + hv * DV + j] = __float2half_rn(on * gz);
+  }
+  const int m = n_commit ? n_commit[b] : 1;
+  if (j == 0 && ok && m >= 1) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(S), "r"(sS), "r"(DK * DV * 2)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+  }
+}
+
 void gdn_step(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor conv_state, torch::Tensor ssm,
               torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor norm_w, torch::Tensor slots, torch::Tensor out,
               int64_t nk, int64_t nv, int64_t dk, int64_t dv, int64_t n_tok, double eps, int64_t gate_sigmoid,
-              c10::optional<torch::Tensor> n_commit) {
+              c10::optional<torch::Tensor> n_commit, c10::optional<torch::Tensor> err_word, int64_t timeout_ns) {
   CK(dk == 128 && dv == 128);
   const int* ncm = nullptr;
   if (n_commit) {
@@ -430,6 +521,15 @@ void gdn_step(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor conv_state
                                                             n_tok, B, ncm);
   }
   dim3 grid(B, nv);
+  static const bool decode1 = getenv("FW_GDN_DECODE1") && atoi(getenv("FW_GDN_DECODE1")) == 1;
+  if (decode1 && n_tok == 1 && ssm.scalar_type() == torch::kBFloat16 && err_word) {
+    gdn_decode1_kernel<<<grid, 128, 0, STREAM>>>(
+        qkv.data_ptr<float>(), proj.data_ptr<float>(), proj.size(1), (__nv_bfloat16*)ssm.data_ptr(),
+        slots.data_ptr<int32_t>(), A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), norm_w.data_ptr<float>(),
+        (__half*)out.data_ptr(), nk, nv, (float)eps, gate_sigmoid, ncm, err_word->data_ptr<int32_t>(),
+        (uint64_t)timeout_ns);
+    return;
+  }
   if (ssm.scalar_type() == torch::kBFloat16)
     gdn_recur_kernel<__nv_bfloat16><<<grid, 256, 0, STREAM>>>(
         qkv.data_ptr<float>(), proj.data_ptr<float>(), proj.size(1), (__nv_bfloat16*)ssm.data_ptr(),

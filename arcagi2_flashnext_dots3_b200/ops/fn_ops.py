@@ -102,7 +102,8 @@ def gdn_step(proj: torch.Tensor, conv_w: torch.Tensor, conv_state: torch.Tensor,
                                    native.err_word(proj.device), native.DEFAULT_TIMEOUT_NS)
             return out
         native.C().gdn_step(proj, conv_w, conv_state, ssm, A_log, dt_bias, norm_w, slots, out, cfg.lin_k_heads,
-                            cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim, n_tok, cfg.rms_eps, gate, n_commit)
+                            cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim, n_tok, cfg.rms_eps, gate, n_commit,
+                            native.err_word(proj.device), native.DEFAULT_TIMEOUT_NS)
         return out
     nk, nv, dk, dv = cfg.lin_k_heads, cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim
     C = 2 * nk * dk + nv * dv

@@ -72,6 +72,36 @@ def test_gdn_step(n_tok):
     _close(ss1, ss0, 1e-4)
 
 
+@pytest.mark.parametrize("commit", [None, "mixed"])
+def test_gdn_decode_bf16_state(commit):
+    """One-token decode with the bf16 state (the serving layout: state by bulk copy, one column per thread) against
+    the fp32 torch statement from the same bf16-rounded state; a commit count of 0 leaves a sequence's state
+    untouched."""
+    cfg = fn_small_config()
+    g = torch.Generator().manual_seed(9)
+    nk, nv, dk, dv = cfg.lin_k_heads, cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim
+    C = 2 * nk * dk + nv * dv
+    B, S = 3, 4
+    proj = torch.randn(B, C + nv * dv + 2 * nv, generator=g)
+    conv_w = torch.randn(C, cfg.conv_kernel, generator=g) * 0.3
+    conv_state = torch.randn(S, C, cfg.conv_kernel - 1, generator=g)
+    ssm = (torch.randn(S, nv, dk, dv, generator=g) * 0.1).bfloat16()
+    A_log, dt, nw = torch.randn(nv, generator=g), torch.randn(nv, generator=g), torch.randn(dv, generator=g)
+    slots = torch.tensor([2, 0, 3], dtype=torch.int32)
+    ncm = torch.tensor([1, 0, 1], dtype=torch.int32) if commit else None
+    cs0, ss0 = conv_state.clone(), ssm.float()
+    want = ops.gdn_step(proj, conv_w, cs0, ss0, A_log, dt, nw, slots, cfg, 1, n_commit=ncm)
+    cs1, ss1 = conv_state.cuda(), ssm.cuda()
+    got = ops.gdn_step(proj.cuda(), conv_w.cuda(), cs1, ss1, A_log.cuda(), dt.cuda(), nw.cuda(), slots.cuda(), cfg,
+                       1, n_commit=None if ncm is None else ncm.cuda())
+    torch.cuda.synchronize()
+    native.check_error()
+    _close(got, want, 1e-2)
+    _close(ss1.float(), ss0, 1e-2)
+    if commit:
+        assert torch.equal(ss1[0].cpu(), ssm[0])          # slot 0 (commit count 0) keeps its state
+
+
 @pytest.mark.parametrize("T,E,k", [(64, 320, 10), (33, 144, 8), (5, 256, 8), (9, 600, 4)])
 def test_moe_route_sizes(T, E, k):
     """Router top-k at the model sizes (warp-per-token kernel up to 512 experts, block kernel beyond): the same
