@@ -169,6 +169,40 @@ __global__ void hc_prenorm_warp_kernel(const float* h, const float* w, __half* o
   }
 }
 
+// One block of four warps per (token, stream) row, each warp a quarter of the row in registers (float4 loads): four
+// times the warps of the warp-per-row form on a decode batch's few hundred rows.
+template <int V4>
+__global__ void __launch_bounds__(128) hc_prenorm_split_kernel(const float* h, const float* w, __half* out, int H,
+                                                               int S, float eps) {
+  __shared__ float red[4];
+  const int row = blockIdx.x, s = row % S, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q4 = H / 16;                 // float4 of one quarter
+  const float4* x = reinterpret_cast<const float4*>(h + (int64_t)row * H) + warp * q4;
+  const float4* ww = reinterpret_cast<const float4*>(w + (int64_t)s * H) + warp * q4;
+  float4 v[V4];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < V4; ++j) {
+    const int i = lane + 32 * j;
+    v[j] = i < q4 ? x[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  const float r = rsqrtf((red[0] + red[1] + red[2] + red[3]) / H + eps);
+  __half2* o = reinterpret_cast<__half2*>(out + (int64_t)row * H) + warp * q4 * 2;
+#pragma unroll
+  for (int j = 0; j < V4; ++j) {
+    const int i = lane + 32 * j;
+    if (i < q4) {
+      const float4 a = ww[i];
+      o[2 * i] = __floats2half2_rn(v[j].x * r * (1.f + a.x), v[j].y * r * (1.f + a.y));
+      o[2 * i + 1] = __floats2half2_rn(v[j].z * r * (1.f + a.z), v[j].w * r * (1.f + a.w));
+    }
+  }
+}
+
 __global__ void hc_prenorm_kernel(const float* h, const float* w, __half* out, int H, float eps) {
   __shared__ float sh[32];
   const int t = blockIdx.x, s = blockIdx.y, S = gridDim.y;
@@ -187,6 +221,15 @@ void hc_prenorm(torch::Tensor h, torch::Tensor w, torch::Tensor out, int64_t H, 
   const int hc = h.size(1) / H;
   if (!T) return;
   const int rows = T * hc;
+  if (H % 64 == 0 && H <= 4096 && rows <= 4096) {   // decode-sized batches: four warps per row
+    if (H <= 2048)
+      hc_prenorm_split_kernel<4><<<rows, 128, 0, STREAM>>>(h.data_ptr<float>(), w.data_ptr<float>(),
+                                                           (__half*)out.data_ptr(), H, hc, (float)eps);
+    else
+      hc_prenorm_split_kernel<8><<<rows, 128, 0, STREAM>>>(h.data_ptr<float>(), w.data_ptr<float>(),
+                                                           (__half*)out.data_ptr(), H, hc, (float)eps);
+    return;
+  }
   if (H % 128 == 0 && H <= 4096) {
     const int blocks = (rows * 32 + 255) / 256;
     if (H <= 1024)
