@@ -30,6 +30,13 @@ from ..ops import fn_ops as ops
 from ..ops import native
 
 
+def _max_ms(ms: float, dev) -> float:
+    """Device time of this rank -> the maximum over the ranks."""
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--layers", type=int, default=0, help="0: the config's 46")
@@ -41,6 +48,9 @@ def main():
     ap.add_argument("--eager", action="store_true", help="no CUDA graph (for launch lists)")
     ap.add_argument("--sp", action="store_true",
                     help="sequence parallel: residual rows split over the TP ranks, NCCL reduce-scatter / all-gather")
+    ap.add_argument("--turn2", type=int, default=0,
+                    help="second turn: every session appends this many new prompt tokens (one prefill step per "
+                         "session on the kept cache), then decodes --steps more tokens")
     ap.add_argument("--shard-vocab", action="store_true",
                     help="with TP: each rank holds its slice of the LM head; tokens via the sharded pick")
     args = ap.parse_args()
@@ -58,11 +68,12 @@ def main():
     if world > 1:
         from ..parallel.tp import TPGroup, tp_config
         lc = tp_config(cfg, world)
-        tp = TPGroup(rank, world, dev, max_tokens=max(64, args.batch), hidden=cfg.hidden_size,
+        tp = TPGroup(rank, world, dev, max_tokens=max(64, args.batch, args.turn2), hidden=cfg.hidden_size,
                      comm="nccl" if args.sp else args.comm, sequence_parallel=args.sp)
     W = random_engine(cfg, dev, seed=0, tp=(rank, world) if world > 1 else None,
                       shard_vocab=args.shard_vocab and world > 1)
-    B, total = args.batch, args.ctx + args.warmup + args.steps + 16
+    B = args.batch
+    total = args.ctx + args.warmup + args.steps * (2 if args.turn2 else 1) + args.turn2 + 16
     caches = allocate_caches(lc, dev, B, total, block_size=64)
     m = D3Model(lc, W, caches, dev, tp=tp)
     alloc = BlockAllocator(caches.n_blocks, B)
@@ -105,14 +116,42 @@ def main():
     b.record()
     torch.cuda.synchronize()
     native.check_error(dev)
-    ms = torch.tensor([a.elapsed_time(b) / args.steps], device=dev)
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms)
+    ms = _max_ms(a.elapsed_time(b) / args.steps, dev)
+    extra = {}
+    if args.turn2:
+        # turn 2 of every session: the new user message is prefilled onto the kept cache (one step of turn2 tokens
+        # per session, eager), its last row picks the first reply token, then the batch decodes again
+        new = torch.randint(0, cfg.vocab_size, (B, args.turn2), device=dev, dtype=torch.int32,
+                            generator=torch.Generator(device=dev).manual_seed(2))
+        torch.cuda.synchronize()
+        dist.barrier()
+        a.record()
+        for s in range(B):
+            x = m.step(new[s], slots[s:s + 1], pos[s:s + 1], args.turn2)
+            ids[s:s + 1].copy_(m.pick(x[-1:]))
+        b.record()
+        pos.add_(args.turn2)
+        torch.cuda.synchronize()
+        native.check_error(dev)
+        pre_ms = _max_ms(a.elapsed_time(b), dev)
+        dist.barrier()
+        a.record()
+        for _ in range(args.steps):
+            run()
+        b.record()
+        torch.cuda.synchronize()
+        native.check_error(dev)
+        ms2 = _max_ms(a.elapsed_time(b) / args.steps, dev)
+        extra = {"turn2_tokens": args.turn2, "turn2_prefill_ms": round(pre_ms, 2),
+                 "turn2_prefill_tok_per_s": round(B * args.turn2 / pre_ms * 1e3, 1),
+                 "turn2_ctx": args.ctx + args.warmup + args.steps + args.turn2,
+                 "turn2_ms_per_step": round(ms2, 3), "turn2_tok_per_s": round(B / ms2 * 1e3, 1)}
     if rank == 0:
         print(json.dumps({"bench": "d3_decode", "model": cfg.name, "layers": cfg.num_layers,
                           "experts": cfg.n_experts, "tp": world, "comm": args.comm if world > 1 else None,
+                          "sp": bool(args.sp and world > 1),
                           "batch": B, "ctx": args.ctx, "ms_per_step": round(ms, 3),
-                          "tok_per_s": round(B / ms * 1e3, 1), "graph": g is not None,
+                          "tok_per_s": round(B / ms * 1e3, 1), "graph": g is not None, **extra,
                           "build_s": round(build_s, 1),
                           "mem_GB": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1)}), flush=True)
     # the graph may hold NCCL calls (--comm nccl): every reference to it, the bound replay method included, must
