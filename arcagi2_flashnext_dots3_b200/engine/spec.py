@@ -1,6 +1,6 @@
 """Speculative decoding: drafters propose k tokens per sequence, one main-model step verifies all k + 1 positions.
 
-Step (greedy sequences; the reference's MTP-3 verify loop, SURVEY call stack 3.2, with the recurrent-state
+Step (greedy sequences; the reference's MTP-3 verify loop, fnext/mtp/fnmtp.py, with the recurrent-state
 rollback of its RecoverSSM / lazy-fold patches, fnext/kv/0001-...recoverssm.patch and fnext/base/gdn_lazy.py):
 
 1. tokens [pending, d_1 .. d_k] of every sequence run through the main model in one step (``verify=True``): the
