@@ -276,9 +276,62 @@ __global__ void hc_mix_kernel(const float* u, const __half* hn, __half* out, int
   }
 }
 
+// Four columns per thread (16-byte fp32 and 8-byte fp16 accesses): the per-token elementwise kernels of a decode
+// step move a few MB each and are bound by instructions per byte and latency, not by bandwidth.
+__device__ __forceinline__ float4 h4_to_f4(uint2 v) {
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+__device__ __forceinline__ uint2 f4_to_h4(float4 v) {
+  __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+  uint2 r;
+  r.x = *reinterpret_cast<uint32_t*>(&a);
+  r.y = *reinterpret_cast<uint32_t*>(&b);
+  return r;
+}
+
+__device__ __forceinline__ void fma4(float4& acc, float a, float4 v) {
+  acc.x = fmaf(a, v.x, acc.x);
+  acc.y = fmaf(a, v.y, acc.y);
+  acc.z = fmaf(a, v.z, acc.z);
+  acc.w = fmaf(a, v.w, acc.w);
+}
+
+__global__ void hc_mix4_kernel(const float4* u, const uint2* hn, uint2* out, int hc, int H4) {
+  const int t = blockIdx.x;
+  const float inv = 1.f / hc;
+  for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < H4; i += blockDim.x * gridDim.y) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < hc; ++s) {
+      const int64_t o = ((int64_t)t * hc + s) * H4 + i;
+      const float4 uv = u[o], hv = h4_to_f4(hn[o]);
+      acc.x += sigm(uv.x) * hv.x;
+      acc.y += sigm(uv.y) * hv.y;
+      acc.z += sigm(uv.z) * hv.z;
+      acc.w += sigm(uv.w) * hv.w;
+    }
+    out[(int64_t)t * H4 + i] = f4_to_h4(make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+  }
+}
+
+inline bool vec4_ok(int64_t H, std::initializer_list<const void*> ptrs) {
+  if (H % 4) return false;
+  for (const void* p : ptrs)
+    if (reinterpret_cast<uintptr_t>(p) % 16) return false;
+  return true;
+}
+
 void hc_mix(torch::Tensor u, torch::Tensor hn, torch::Tensor out, int64_t hc, int64_t H) {
   const int T = u.size(0);
   if (!T) return;
+  if (vec4_ok(H, {u.data_ptr(), hn.data_ptr(), out.data_ptr()})) {
+    const int H4 = H / 4;
+    hc_mix4_kernel<<<dim3(T, (H4 + 127) / 128), 128, 0, STREAM>>>(
+        (const float4*)u.data_ptr(), (const uint2*)hn.data_ptr(), (uint2*)out.data_ptr(), hc, H4);
+    return;
+  }
   hc_mix_kernel<<<dim3(T, (H + 255) / 256), 256, 0, STREAM>>>(u.data_ptr<float>(), (const __half*)hn.data_ptr(), (__half*)out.data_ptr(),
                                        hc, H);
 }
@@ -291,9 +344,28 @@ __global__ void hc_residual_kernel(float* h, const float* y, const float* inj, i
   }
 }
 
+__global__ void hc_residual4_kernel(float4* h, const float4* y, const float* inj, int hc, int H4) {
+  const int t = blockIdx.x;
+  for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < H4; i += blockDim.x * gridDim.y) {
+    const float4 v = y[(int64_t)t * H4 + i];
+    for (int s = 0; s < hc; ++s) {
+      float4& d = h[((int64_t)t * hc + s) * H4 + i];
+      float4 a = d;
+      fma4(a, inj[t * hc + s], v);
+      d = a;
+    }
+  }
+}
+
 void hc_residual(torch::Tensor h, torch::Tensor y, torch::Tensor inj) {
   const int T = h.size(0), hc = inj.size(1), H = y.size(1);
   if (!T) return;
+  if (vec4_ok(H, {h.data_ptr(), y.data_ptr()})) {
+    const int H4 = H / 4;
+    hc_residual4_kernel<<<dim3(T, (H4 + 127) / 128), 128, 0, STREAM>>>(
+        (float4*)h.data_ptr(), (const float4*)y.data_ptr(), inj.data_ptr<float>(), hc, H4);
+    return;
+  }
   hc_residual_kernel<<<dim3(T, (H + 255) / 256), 256, 0, STREAM>>>(h.data_ptr<float>(), y.data_ptr<float>(), inj.data_ptr<float>(), hc, H);
 }
 
@@ -1689,12 +1761,37 @@ __global__ void moe_combine_kernel(float* h, const float* ypair, const int32_t* 
   }
 }
 
+__global__ void moe_combine4_kernel(float4* h, const float4* ypair, const int32_t* pair_pos, const float* w,
+                                    const float4* ysh, const float* sg, int ld_sg, const float* inj, int k, int hc,
+                                    int H4) {
+  const int t = blockIdx.x;
+  const float g = sigm(sg[(int64_t)t * ld_sg]);
+  for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < H4; i += blockDim.x * gridDim.y) {
+    const float4 sv = ysh[(int64_t)t * H4 + i];
+    float4 y = make_float4(g * sv.x, g * sv.y, g * sv.z, g * sv.w);
+    for (int j = 0; j < k; ++j) fma4(y, w[t * k + j], ypair[(int64_t)pair_pos[t * k + j] * H4 + i]);
+    for (int s = 0; s < hc; ++s) {
+      float4& d = h[((int64_t)t * hc + s) * H4 + i];
+      float4 a = d;
+      fma4(a, inj[t * hc + s], y);
+      d = a;
+    }
+  }
+}
+
 void moe_combine(torch::Tensor h, torch::Tensor ypair, torch::Tensor pair_pos, torch::Tensor w, torch::Tensor ysh,
                  torch::Tensor sg, torch::Tensor inj) {
   const int T = pair_pos.size(0), k = pair_pos.size(1);
   if (!T) return;
   const int H = ysh.size(1), hc = inj.size(1);
   const int ld_sg = sg.dim() == 1 ? sg.stride(0) : sg.stride(0);
+  if (vec4_ok(H, {h.data_ptr(), ypair.data_ptr(), ysh.data_ptr()})) {
+    const int H4 = H / 4;
+    moe_combine4_kernel<<<dim3(T, (H4 + 127) / 128), 128, 0, STREAM>>>(
+        (float4*)h.data_ptr(), (const float4*)ypair.data_ptr(), pair_pos.data_ptr<int32_t>(), w.data_ptr<float>(),
+        (const float4*)ysh.data_ptr(), sg.data_ptr<float>(), ld_sg, inj.data_ptr<float>(), k, hc, H4);
+    return;
+  }
   moe_combine_kernel<<<dim3(T, (H + 255) / 256), 256, 0, STREAM>>>(h.data_ptr<float>(), ypair.data_ptr<float>(), pair_pos.data_ptr<int32_t>(),
                                             w.data_ptr<float>(), ysh.data_ptr<float>(), sg.data_ptr<float>(), ld_sg,
                                             inj.data_ptr<float>(), k, hc, H);
