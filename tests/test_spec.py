@@ -118,9 +118,16 @@ def test_speculative_accept_preserves_the_sampling_distribution():
     p = torch.softmax(lg[0, 0] / T, -1)
     n = 20000
     counts = torch.zeros(V)
-    for seed in range(n):
-        acc, nxt = sampling.speculative_accept(lg, torch.tensor([[3]]), [T], [seed], [0])
-        counts[3 if acc[0] == 1 else nxt[0]] += 1
+    # 20000 calls on tensors of a few elements: one intra-op thread (with a pool per parallel test worker, thread
+    # hand-offs made each call hundreds of times slower than its ~0.5 ms)
+    threads = torch.get_num_threads()
+    torch.set_num_threads(1)
+    try:
+        for seed in range(n):
+            acc, nxt = sampling.speculative_accept(lg, torch.tensor([[3]]), [T], [seed], [0])
+            counts[3 if acc[0] == 1 else nxt[0]] += 1
+    finally:
+        torch.set_num_threads(threads)
     tv = 0.5 * float((counts / n - p).abs().sum())
     assert tv < 0.015, (tv, (counts / n).tolist(), p.tolist())   # sampling noise alone: ~0.005
 
