@@ -148,7 +148,8 @@ def main():
                  "turn2_ms_per_step": round(ms2, 3), "turn2_tok_per_s": round(B / ms2 * 1e3, 1)}
     if rank == 0:
         print(json.dumps({"bench": "d3_decode", "model": cfg.name, "layers": cfg.num_layers,
-                          "experts": cfg.n_experts, "tp": world, "comm": args.comm if world > 1 else None,
+                          "experts": cfg.n_experts, "tp": world,
+                          "comm": ("nccl" if args.sp else args.comm) if world > 1 else None,
                           "sp": bool(args.sp and world > 1),
                           "batch": B, "ctx": args.ctx, "ms_per_step": round(ms, 3),
                           "tok_per_s": round(B / ms * 1e3, 1), "graph": g is not None, **extra,
